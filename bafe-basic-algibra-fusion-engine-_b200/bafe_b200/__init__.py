@@ -1,0 +1,358 @@
+"""bafe_b200 -- B200 execution backend for BAFE, with a front end that
+mirrors BAFE's `@bafe.jit` API (bafe/python/bafe/__init__.py).
+
+    import bafe_b200 as bafe
+
+    @bafe.jit
+    def f(A, B, C):
+        return bafe.relu(bafe.matmul(A, B) + C)
+
+    out = f(A, B, C)        # numpy in, numpy out; runs on the GPU
+
+Tracing, argument-layout detection (Fortran-contiguous -> "col"), the
+per-(shape, dtype, layout) cache and the host-pointer call follow the
+reference's JittedFunction (__init__.py:310-545).  The graph goes to
+libbafe_cuda.so's bafe_cuda_jit_get_or_compile -- the drop-in for BAFE's
+bafe_jit_get_or_compile -- without BAFE's optimizer in between: at the
+sizes BAFE targets its extractor returns the same unfused chain the trace
+builds, and the backend does the fusion.
+
+Lower-level entry points: GraphBuilder (graph.py), compile_graph() ->
+Kernel, Kernel.run_device() for device-resident buffers (torch tensors or
+raw pointers) on a CUDA stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import functools
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _binding
+from ._binding import (BafeGraph, DTYPE_BF16, DTYPE_F16, DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_I64, check,
+                       last_error, lib)
+from .graph import LAYOUT_NAMES, GraphBuilder
+
+__version__ = "0.1.0"
+
+_NP_TO_BAFE = {
+    np.dtype("float32"): DTYPE_F32, np.dtype("float64"): DTYPE_F64, np.dtype("int32"): DTYPE_I32,
+    np.dtype("int64"): DTYPE_I64, np.dtype("float16"): DTYPE_F16,
+}
+_BAFE_TO_NP = {v: k for k, v in _NP_TO_BAFE.items()}
+_BAFE_TO_NP[DTYPE_BF16] = np.dtype("uint16")   # bf16 travels as raw 16-bit words
+
+
+# ---------------------------------------------------------------- backend --
+
+def set_option(key: str, value: str) -> None:
+    """Backend option, e.g. set_option("gemm_precision", "exact")."""
+    if lib.bafe_cuda_set_option(key.encode(), str(value).encode()) != 0:
+        raise ValueError(f"bad option {key}={value}")
+
+
+def get_option(key: str) -> str:
+    buf = ctypes.create_string_buffer(64)
+    if lib.bafe_cuda_get_option(key.encode(), buf, len(buf)) != 0:
+        raise KeyError(key)
+    return buf.value.decode()
+
+
+def jit_stats() -> dict:
+    s = lib.bafe_cuda_jit_get_stats()
+    return {"hits": s.hits, "misses": s.misses, "compiles": s.compiles, "compile_failures": s.compile_failures}
+
+
+def jit_clear() -> None:
+    lib.bafe_cuda_jit_clear()
+
+
+def jit_invalidate_memory_cache() -> None:
+    lib.bafe_cuda_jit_invalidate_memory_cache()
+
+
+def set_cache_dir(path: str) -> None:
+    lib.bafe_cuda_jit_set_cache_dir(str(path).encode())
+
+
+def cache_dir() -> str:
+    return lib.bafe_cuda_jit_cache_dir().decode()
+
+
+def graph_hash(graph: BafeGraph) -> str:
+    buf = ctypes.create_string_buffer(65)
+    if lib.bafe_cuda_jit_hash_graph(ctypes.byref(graph), buf, 65) != 0:
+        raise RuntimeError("hash failed")
+    return buf.value.decode()
+
+
+def launch_count() -> int:
+    return int(lib.bafe_cuda_launch_count())
+
+
+class Kernel:
+    """A compiled plan: the host function BAFE's ABI returns, plus device entry."""
+
+    def __init__(self, fn_ptr: int, n_inputs: int, out_shape: tuple, out_dtype: np.dtype, graph: BafeGraph):
+        self.fn_ptr = fn_ptr
+        self.plan = lib.bafe_cuda_plan_of(ctypes.c_void_p(fn_ptr))
+        if self.plan < 0:
+            raise RuntimeError("function pointer is not a bafe_cuda plan")
+        self.n_inputs = n_inputs
+        self.out_shape = out_shape
+        self.out_dtype = out_dtype
+        self.graph = graph
+        self._sig = ctypes.CFUNCTYPE(None, *([ctypes.c_void_p] * (n_inputs + 1)))
+        self._call = self._sig(fn_ptr)
+
+    def describe(self) -> str:
+        n = lib.bafe_cuda_plan_describe(self.plan, None, 0)
+        buf = ctypes.create_string_buffer(n + 1)
+        lib.bafe_cuda_plan_describe(self.plan, buf, n + 1)
+        return buf.value.decode()
+
+    @property
+    def output_bytes(self) -> int:
+        return int(lib.bafe_cuda_plan_output_bytes(self.plan))
+
+    def input_bytes(self, i: int) -> int:
+        return int(lib.bafe_cuda_plan_input_bytes(self.plan, i))
+
+    def call_host_ptrs(self, ptrs: Sequence[int]) -> None:
+        """Call the ABI function (host pointers, synchronous) and raise on error."""
+        lib.bafe_cuda_clear_error()
+        self._call(*[ctypes.c_void_p(p) for p in ptrs])
+        code, msg = last_error()
+        if code:
+            raise RuntimeError(f"bafe_cuda kernel failed (code {code}): {msg}")
+
+    def __call__(self, *arrays: np.ndarray, out: Optional[np.ndarray] = None) -> np.ndarray:
+        if len(arrays) != self.n_inputs:
+            raise TypeError(f"kernel takes {self.n_inputs} inputs, got {len(arrays)}")
+        if out is None:
+            out = np.zeros(self.out_shape, dtype=self.out_dtype)
+        self.call_host_ptrs([a.ctypes.data for a in arrays] + [out.ctypes.data])
+        return out
+
+    def run_device(self, ptrs: Sequence[int], stream: int = 0) -> None:
+        """Enqueue on device buffers (inputs..., out) on `stream` (cudaStream_t)."""
+        arr = (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+        check(lib.bafe_cuda_run_device(self.plan, arr, len(ptrs), ctypes.c_void_p(int(stream))), "run_device")
+
+    def run_torch(self, inputs: Sequence, out, stream=None) -> None:
+        """run_device on torch CUDA tensors (contiguous in the layout the graph declares)."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        self.run_device([t.data_ptr() for t in inputs] + [out.data_ptr()], s.cuda_stream)
+
+
+def compile_graph(builder: GraphBuilder) -> Kernel:
+    """bafe_cuda_jit_get_or_compile on a built graph."""
+    err = ctypes.create_string_buffer(4096)
+    fn = lib.bafe_cuda_jit_get_or_compile(ctypes.byref(builder.graph), err, len(err))
+    if not fn:
+        raise RuntimeError(f"bafe_cuda_jit_get_or_compile failed: {err.value.decode(errors='replace')}")
+    out = builder.output
+    out_shape = builder.shape(out)
+    out_dtype = _BAFE_TO_NP[builder.dtype(out)]
+    return Kernel(fn, builder.graph.n_inputs, out_shape, out_dtype, builder.graph)
+
+
+# ------------------------------------------------------------- tracing --
+
+_TRACE: Optional[GraphBuilder] = None
+
+
+def _trace() -> GraphBuilder:
+    if _TRACE is None:
+        raise RuntimeError("no active trace - bafe ops can only be called inside a function decorated with @bafe.jit")
+    return _TRACE
+
+
+class Tensor:
+    """Symbolic tensor handle during tracing (bafe/python/bafe/__init__.py:123-177)."""
+    __slots__ = ("node_id", "shape", "dtype", "_name")
+
+    def __init__(self, node_id: int, shape: tuple, dtype: int, name: Optional[str] = None):
+        self.node_id = node_id
+        self.shape = shape
+        self.dtype = dtype
+        self._name = name
+
+    def __add__(self, other: "Tensor") -> "Tensor":
+        return _op("add", self, other)
+
+    def __sub__(self, other: "Tensor") -> "Tensor":
+        return _op("sub", self, other)
+
+    def __mul__(self, other: "Tensor") -> "Tensor":
+        return _op("mul", self, other)
+
+    def __matmul__(self, other: "Tensor") -> "Tensor":
+        if len(self.shape) < 2 or len(other.shape) < 2:
+            raise ValueError("matmul requires rank>=2 tensors")
+        if self.shape[-1] != other.shape[-2]:
+            raise ValueError(f"matmul shape mismatch: {self.shape} @ {other.shape} (K dim must match)")
+        return _op("matmul", self, other)
+
+    @property
+    def name(self) -> Optional[str]:
+        return self._name
+
+    def __repr__(self) -> str:
+        return f"Tensor(shape={self.shape}, dtype={_BAFE_TO_NP[self.dtype]})"
+
+
+def _op(op: str, *xs: Tensor, **attrs) -> Tensor:
+    tb = _trace()
+    nid = tb.add(op, [x.node_id for x in xs], **attrs)
+    return Tensor(nid, tb.shape(nid), tb.dtype(nid))
+
+
+def input(shape: Tuple[int, ...], dtype="float32", name: str = "x", layout: str = "row") -> Tensor:
+    """Declare an input (bafe/python/bafe/__init__.py:196-218)."""
+    tb = _trace()
+    np_dt = np.dtype(dtype)
+    if np_dt not in _NP_TO_BAFE:
+        raise ValueError(f"unsupported dtype {dtype}; supported: {list(_NP_TO_BAFE)}")
+    if layout not in LAYOUT_NAMES:
+        raise ValueError(f"unsupported layout {layout!r}; supported: {list(LAYOUT_NAMES)}")
+    nid = tb.add_input(name, tuple(int(s) for s in shape), _NP_TO_BAFE[np_dt], LAYOUT_NAMES[layout])
+    return Tensor(nid, tb.shape(nid), _NP_TO_BAFE[np_dt], name=name)
+
+
+def matmul(a: Tensor, b: Tensor) -> Tensor:
+    return a @ b
+
+
+def add(a: Tensor, b: Tensor) -> Tensor:
+    return a + b
+
+
+def sub(a: Tensor, b: Tensor) -> Tensor:
+    return a - b
+
+
+def mul(a: Tensor, b: Tensor) -> Tensor:
+    return a * b
+
+
+def relu(x: Tensor) -> Tensor:
+    return _op("relu", x)
+
+
+def sigmoid(x: Tensor) -> Tensor:
+    return _op("sigmoid", x)
+
+
+def tanh(x: Tensor) -> Tensor:
+    return _op("tanh", x)
+
+
+def neg(x: Tensor) -> Tensor:
+    return _op("neg", x)
+
+
+def bias_add(x: Tensor, bias: Tensor) -> Tensor:
+    return _op("bias_add", x, bias)
+
+
+def transpose(x: Tensor, perm: Tuple[int, ...]) -> Tensor:
+    return _op("transpose", x, perm=list(perm))
+
+
+def reduce_sum(x: Tensor, axes: Tuple[int, ...], keepdims: bool = False) -> Tensor:
+    return _op("reduce_sum", x, axes=list(axes), keepdims=keepdims)
+
+
+def reduce_max(x: Tensor, axes: Tuple[int, ...], keepdims: bool = False) -> Tensor:
+    return _op("reduce_max", x, axes=list(axes), keepdims=keepdims)
+
+
+def reshape(x: Tensor, shape: Tuple[int, ...]) -> Tensor:
+    return _op("reshape", x, shape=list(shape))
+
+
+def broadcast_to(x: Tensor, shape: Tuple[int, ...]) -> Tensor:
+    return _op("broadcast_to", x, shape=list(shape))
+
+
+def _layout_of(a: np.ndarray) -> str:
+    """__init__.py:345-349: Fortran-contiguous rank>=2 arrays are "col"."""
+    if a.ndim >= 2 and a.flags["F_CONTIGUOUS"] and not a.flags["C_CONTIGUOUS"]:
+        return "col"
+    return "row"
+
+
+class JittedFunction:
+    """A traced function compiled by the B200 backend (mirrors __init__.py:310-545)."""
+
+    def __init__(self, fn: Callable):
+        self._fn = fn
+        self._compiled: dict = {}
+        functools.update_wrapper(self, fn)
+
+    def kernel_for(self, *args: np.ndarray) -> Kernel:
+        key = tuple((a.shape, str(a.dtype), _layout_of(a)) for a in args)
+        if key not in self._compiled:
+            self._compiled[key] = self._compile(args)
+        return self._compiled[key]
+
+    def __call__(self, *args: np.ndarray) -> np.ndarray:
+        if not args:
+            raise TypeError("jitted function requires at least one input")
+        for a in args:
+            if not isinstance(a, np.ndarray):
+                raise TypeError(f"expected numpy array, got {type(a)}")
+        k = self.kernel_for(*args)
+        # Keep each argument's memory layout: a col-major kernel reads the
+        # Fortran buffer as is (__init__.py:369-380).
+        ptrs = []
+        keep = []
+        for a in args:
+            if not (a.flags["C_CONTIGUOUS"] or a.flags["F_CONTIGUOUS"]):
+                a = np.ascontiguousarray(a)
+            keep.append(a)
+            ptrs.append(a.ctypes.data)
+        out = np.zeros(k.out_shape, dtype=k.out_dtype)
+        k.call_host_ptrs(ptrs + [out.ctypes.data])
+        return out
+
+    def _compile(self, args: Sequence[np.ndarray]) -> Kernel:
+        global _TRACE
+        _TRACE = GraphBuilder()
+        try:
+            tensors = []
+            code = self._fn.__code__
+            for i, a in enumerate(args):
+                np_dt = np.dtype(a.dtype)
+                if np_dt not in _NP_TO_BAFE:
+                    raise TypeError(f"unsupported dtype {np_dt}")
+                name = code.co_varnames[i] if i < len(code.co_varnames) else f"in{i}"
+                tensors.append(input(a.shape, np_dt, name=name, layout=_layout_of(a)))
+            result = self._fn(*tensors)
+            if not isinstance(result, Tensor):
+                raise TypeError(f"jitted function must return a Tensor, got {type(result)}")
+            _TRACE.set_output(result.node_id)
+            builder = _TRACE
+        finally:
+            _TRACE = None
+        return compile_graph(builder)
+
+
+def jit(fn: Callable = None, **_ignored):
+    """Decorator (bafe.jit).  Search/autotune options of the reference
+    configure its optimizer, which this backend does not run; they are
+    accepted and ignored."""
+    if fn is not None:
+        return JittedFunction(fn)
+    return lambda f: JittedFunction(f)
+
+
+__all__ = [
+    "Tensor", "jit", "input", "matmul", "add", "sub", "mul", "relu", "sigmoid", "tanh", "neg", "bias_add",
+    "transpose", "reduce_sum", "reduce_max", "reshape", "broadcast_to", "GraphBuilder", "compile_graph",
+    "Kernel", "set_option", "get_option", "jit_stats", "jit_clear", "jit_invalidate_memory_cache",
+    "set_cache_dir", "cache_dir", "graph_hash", "launch_count", "last_error",
+]

@@ -1,0 +1,137 @@
+"""ctypes binding to libbafe_cuda.so (the C ABI declared in include/bafe_cuda.h).
+
+The graph structs mirror BAFE's POD graph byte for byte: the reference
+binds the same layout at bafe/python/bafe/_binding.py:62-112 (types.h:55-58,
+ops.h:239-250, ir.h:133-155).  The backend reads these structs by pointer,
+so the field order and types are fixed by the reference's ABI.
+
+The library is found at $BAFE_CUDA_LIB, else next to this package
+(../lib/libbafe_cuda.so).  There is no fallback: without the CUDA library
+the import fails.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import (POINTER, Structure, c_bool, c_char, c_char_p, c_double, c_int, c_int32, c_int64,
+                    c_size_t, c_void_p)
+from pathlib import Path
+
+BAFE_MAX_RANK = 8
+BAFE_MAX_ATTR_LEN = 32
+BAFE_MAX_CHILDREN = 4
+BAFE_MAX_NODES = 4096
+
+DTYPE_F32, DTYPE_F64, DTYPE_I32, DTYPE_I64, DTYPE_F16, DTYPE_BF16 = range(6)
+LAYOUT_ROW, LAYOUT_COL, LAYOUT_BLOCKED, LAYOUT_TC = range(4)
+
+
+class BafeShape(Structure):
+    _fields_ = [("dims", c_int32 * BAFE_MAX_RANK), ("rank", c_int32)]
+
+
+class BafeOpAttrs(Structure):
+    _fields_ = [
+        ("n_axes", c_int32), ("axes", c_int32 * BAFE_MAX_ATTR_LEN),
+        ("n_perm", c_int32), ("perm", c_int32 * BAFE_MAX_ATTR_LEN),
+        ("n_shape", c_int32), ("shape", c_int32 * BAFE_MAX_ATTR_LEN),
+        ("keepdims", c_bool), ("scalar_value", c_double), ("has_scalar", c_bool),
+        ("name", c_char * BAFE_MAX_ATTR_LEN),
+    ]
+
+
+class BafeNode(Structure):
+    _fields_ = [
+        ("id", c_int32), ("op_name", c_char_p), ("attrs", BafeOpAttrs),
+        ("n_children", c_int), ("children", c_int32 * BAFE_MAX_CHILDREN),
+        ("shape", BafeShape), ("dtype", c_int), ("layout", c_int),
+        ("input_name", c_char * BAFE_MAX_ATTR_LEN), ("is_input", c_bool),
+        ("is_constant", c_bool), ("const_value", c_double),
+    ]
+
+
+class BafeGraph(Structure):
+    _fields_ = [
+        ("nodes", BafeNode * BAFE_MAX_NODES), ("n_nodes", c_int),
+        ("inputs", c_int32 * BAFE_MAX_NODES), ("n_inputs", c_int),
+        ("outputs", c_int32 * BAFE_MAX_NODES), ("n_outputs", c_int),
+    ]
+
+
+class BafeJitStats(Structure):
+    _fields_ = [("hits", c_int), ("misses", c_int), ("compiles", c_int), ("compile_failures", c_int)]
+
+
+PACKAGE_ROOT = Path(__file__).resolve().parent.parent
+
+
+def library_path() -> str:
+    env = os.environ.get("BAFE_CUDA_LIB")
+    if env:
+        return env
+    return str(PACKAGE_ROOT / "lib" / "libbafe_cuda.so")
+
+
+def _load() -> ctypes.CDLL:
+    path = library_path()
+    if not Path(path).exists():
+        raise ImportError(
+            f"libbafe_cuda.so not found at {path}: build it with "
+            f"`make -C {PACKAGE_ROOT}` (or __graft_entry__.build())")
+    lib = ctypes.CDLL(path)
+    G = POINTER(BafeGraph)
+    proto = {
+        "bafe_cuda_version": ([], c_int),
+        "bafe_cuda_jit_hash_graph": ([G, c_char_p, c_size_t], c_int),
+        "bafe_cuda_jit_get_or_compile": ([G, c_char_p, c_size_t], c_void_p),
+        "bafe_cuda_jit_set_cache_dir": ([c_char_p], None),
+        "bafe_cuda_jit_cache_dir": ([], c_char_p),
+        "bafe_cuda_jit_get_stats": ([], BafeJitStats),
+        "bafe_cuda_jit_clear": ([], None),
+        "bafe_cuda_jit_invalidate_memory_cache": ([], None),
+        "bafe_cuda_plan_of": ([c_void_p], c_int),
+        "bafe_cuda_plan_num_inputs": ([c_int], c_int),
+        "bafe_cuda_plan_describe": ([c_int, c_char_p, c_size_t], c_int),
+        "bafe_cuda_plan_output_bytes": ([c_int], c_int64),
+        "bafe_cuda_plan_input_bytes": ([c_int, c_int], c_int64),
+        "bafe_cuda_run_device": ([c_int, POINTER(c_void_p), c_int, c_void_p], c_int),
+        "bafe_cuda_run_host": ([c_int, POINTER(c_void_p), c_int], c_int),
+        "bafe_cuda_last_error": ([c_char_p, c_size_t], c_int),
+        "bafe_cuda_clear_error": ([], None),
+        "bafe_cuda_set_option": ([c_char_p, c_char_p], c_int),
+        "bafe_cuda_get_option": ([c_char_p, c_char_p, c_size_t], c_int),
+        "bafe_cuda_launch_count": ([], c_int64),
+        "bafe_cuda_abi_size": ([c_int], c_int64),
+    }
+    for name, (args, res) in proto.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+lib = _load()
+
+# Every symbol include/bafe_cuda.h declares (checked by the CPU test suite).
+EXPORTED_SYMBOLS = (
+    "bafe_cuda_jit_hash_graph", "bafe_cuda_jit_get_or_compile", "bafe_cuda_jit_set_cache_dir",
+    "bafe_cuda_jit_cache_dir", "bafe_cuda_jit_get_stats", "bafe_cuda_jit_clear",
+    "bafe_cuda_jit_invalidate_memory_cache", "bafe_cuda_version", "bafe_cuda_plan_of",
+    "bafe_cuda_plan_num_inputs", "bafe_cuda_plan_describe", "bafe_cuda_plan_output_bytes",
+    "bafe_cuda_plan_input_bytes", "bafe_cuda_run_device", "bafe_cuda_run_host", "bafe_cuda_last_error",
+    "bafe_cuda_clear_error", "bafe_cuda_set_option", "bafe_cuda_get_option", "bafe_cuda_launch_count",
+    "bafe_cuda_abi_size",
+)
+
+
+def last_error() -> tuple[int, str]:
+    buf = ctypes.create_string_buffer(8192)
+    code = lib.bafe_cuda_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    """Raise RuntimeError with the library's message when rc is nonzero."""
+    if rc != 0:
+        code, msg = last_error()
+        raise RuntimeError(f"{what} failed (code {rc}): {msg}")

@@ -1,0 +1,329 @@
+// api.cpp -- the extern "C" surface of libbafe_cuda.so (include/bafe_cuda.h):
+// plan cache keyed by graph hash, host-function trampolines, stats, options.
+#include "internal.h"
+
+#include <cuda_runtime.h>
+
+#include <array>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#define BAFE_API extern "C" __attribute__((visibility("default")))
+
+namespace bafe_cuda {
+
+Options& options() {
+    static Options o;
+    static bool init = false;
+    if (!init) {
+        init = true;
+        if (const char* p = getenv("BAFE_GEMM_PRECISION")) o.gemm_precision = p;
+        if (const char* d = getenv("BAFE_DEVICE")) o.device = atoi(d);
+    }
+    return o;
+}
+
+namespace {
+
+std::recursive_mutex g_mu;
+std::vector<Plan*> g_plans;                 // plan id -> plan (nullptr once dropped)
+std::map<std::string, int> g_by_key;        // plan key -> plan id
+bafe_jit_stats g_stats = {0, 0, 0, 0};
+
+// ------------------------------------------------------- trampolines --
+// The legacy kernel ABI has no context argument (jit.h:26-35): the caller
+// gets a bare function pointer and calls f(in_0, ..., in_{n-1}, out).  Each
+// live plan is therefore bound to one of kSlots distinct functions; the
+// function reads the first n+1 pointer arguments (n = the plan's input
+// count, at most kMaxArgs-1) and runs the plan on them.
+constexpr int kSlots = 256;          // the reference caches 256 kernels (jit.c:164)
+constexpr int kMaxArgs = 17;         // 16 inputs + out
+int g_slot_plan[kSlots];
+bool g_slots_init = false;
+
+int run_slot(int slot, void** a);
+
+template <int S>
+void trampoline(void* p0, void* p1, void* p2, void* p3, void* p4, void* p5, void* p6, void* p7, void* p8,
+                void* p9, void* p10, void* p11, void* p12, void* p13, void* p14, void* p15, void* p16) {
+    void* a[kMaxArgs] = {p0, p1, p2, p3, p4, p5, p6, p7, p8, p9, p10, p11, p12, p13, p14, p15, p16};
+    run_slot(S, a);
+}
+typedef void (*TrampolineFn)(void*, void*, void*, void*, void*, void*, void*, void*, void*, void*, void*, void*,
+                             void*, void*, void*, void*, void*);
+
+template <size_t... I>
+constexpr std::array<TrampolineFn, sizeof...(I)> make_trampolines(std::index_sequence<I...>) {
+    return {{&trampoline<(int)I>...}};
+}
+const std::array<TrampolineFn, kSlots> kTrampolines = make_trampolines(std::make_index_sequence<kSlots>{});
+
+void init_slots() {
+    if (g_slots_init) return;
+    for (int i = 0; i < kSlots; ++i) g_slot_plan[i] = -1;
+    g_slots_init = true;
+}
+
+int slot_of_plan(int plan_id) {
+    for (int i = 0; i < kSlots; ++i)
+        if (g_slot_plan[i] == plan_id) return i;
+    return -1;
+}
+
+int run_slot(int slot, void** a) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    int pid = g_slot_plan[slot];
+    if (pid < 0 || pid >= (int)g_plans.size() || !g_plans[pid]) {
+        set_error(10, "stale kernel function: its plan was dropped by bafe_cuda_jit_clear or invalidate");
+        return 10;
+    }
+    Plan& p = *g_plans[pid];
+    return run_plan_host(p, a, p.n_inputs + 1);
+}
+
+void drop_all_plans() {
+    for (Plan* p : g_plans) {
+        if (!p) continue;
+        release_plan_device_state(*p);
+        delete p;
+    }
+    g_plans.clear();
+    g_by_key.clear();
+    init_slots();
+    for (int i = 0; i < kSlots; ++i) g_slot_plan[i] = -1;
+}
+
+Plan* plan_ptr(int id) {
+    if (id < 0 || id >= (int)g_plans.size()) return nullptr;
+    return g_plans[id];
+}
+
+void write_err(char* buf, size_t n, const std::string& msg) {
+    if (buf && n > 0) snprintf(buf, n, "%s", msg.c_str());
+}
+
+}  // namespace
+}  // namespace bafe_cuda
+
+using namespace bafe_cuda;
+
+BAFE_API int bafe_cuda_version(void) { return 1000; }
+
+BAFE_API int bafe_cuda_jit_hash_graph(const bafe_graph* g, char* out, size_t out_size) {
+    return hash_graph(g, out, out_size);
+}
+
+BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* err_buf, size_t err_buf_size) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    init_slots();
+    if (err_buf && err_buf_size) err_buf[0] = '\0';
+    char hash[65];
+    if (hash_graph(g, hash, sizeof(hash)) < 0) {
+        write_err(err_buf, err_buf_size, "hash failed");
+        return nullptr;
+    }
+    const Options& opt = options();
+    std::string key = std::string(hash) + "|prec=" + opt.gemm_precision;
+    auto it = g_by_key.find(key);
+    if (it != g_by_key.end() && plan_ptr(it->second)) {
+        int slot = slot_of_plan(it->second);
+        if (slot >= 0) {
+            g_stats.hits++;
+            return reinterpret_cast<bafe_kernel_fn>(kTrampolines[slot]);
+        }
+    }
+    g_stats.misses++;
+    Graph G;
+    std::string err;
+    if (parse_graph(g, G, err) != 0) {
+        write_err(err_buf, err_buf_size, err);
+        set_error(2, err);
+        g_stats.compile_failures++;
+        return nullptr;
+    }
+    if ((int)G.inputs.size() > kMaxArgs - 1) {
+        err = "graph has more than 16 inputs";
+        write_err(err_buf, err_buf_size, err);
+        set_error(2, err);
+        g_stats.compile_failures++;
+        return nullptr;
+    }
+    Plan* p = new Plan();
+    p->graph_hash = hash;
+    p->key = key;
+    if (lower_graph(G, opt, *p, err) != 0) {
+        write_err(err_buf, err_buf_size, err);
+        set_error(2, err);
+        g_stats.compile_failures++;
+        delete p;
+        return nullptr;
+    }
+    bool from_cache = false;
+    if (compile_cubin(p->source, p->source_hash, p->cubin, from_cache, err) != 0) {
+        write_err(err_buf, err_buf_size, err);
+        set_error(3, err);
+        g_stats.compile_failures++;
+        delete p;
+        return nullptr;
+    }
+    if (from_cache) g_stats.hits++;   // on-disk hit, counted like jit.c:241
+    else g_stats.compiles++;
+    int slot = slot_of_plan(-1);
+    if (slot < 0) {
+        // The reference stops caching after 256 kernels (jit.c:320); a
+        // context-free function needs a slot, so evict the oldest plan.
+        int victim = -1;
+        for (int i = 0; i < (int)g_plans.size(); ++i)
+            if (g_plans[i] && slot_of_plan(i) >= 0) { victim = i; break; }
+        if (victim >= 0) {
+            slot = slot_of_plan(victim);
+            g_by_key.erase(g_plans[victim]->key);
+            release_plan_device_state(*g_plans[victim]);
+            delete g_plans[victim];
+            g_plans[victim] = nullptr;
+            g_slot_plan[slot] = -1;
+        }
+    }
+    if (slot < 0) {
+        write_err(err_buf, err_buf_size, "no free kernel slot");
+        delete p;
+        return nullptr;
+    }
+    p->id = (int)g_plans.size();
+    g_plans.push_back(p);
+    g_by_key[key] = p->id;
+    g_slot_plan[slot] = p->id;
+    return reinterpret_cast<bafe_kernel_fn>(kTrampolines[slot]);
+}
+
+BAFE_API void bafe_cuda_jit_set_cache_dir(const char* dir) {
+    if (!dir) return;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    set_cache_dir(dir);
+}
+
+BAFE_API const char* bafe_cuda_jit_cache_dir(void) {
+    static std::string s;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    s = cache_dir();
+    return s.c_str();
+}
+
+BAFE_API bafe_jit_stats bafe_cuda_jit_get_stats(void) { return g_stats; }
+
+BAFE_API void bafe_cuda_jit_clear(void) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    drop_all_plans();
+    g_stats = {0, 0, 0, 0};
+}
+
+BAFE_API void bafe_cuda_jit_invalidate_memory_cache(void) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    drop_all_plans();
+}
+
+BAFE_API int bafe_cuda_plan_of(bafe_kernel_fn fn) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    init_slots();
+    for (int i = 0; i < kSlots; ++i)
+        if (reinterpret_cast<bafe_kernel_fn>(kTrampolines[i]) == fn) return g_slot_plan[i];
+    return -1;
+}
+
+BAFE_API int bafe_cuda_plan_num_inputs(int plan) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    return p ? p->n_inputs : -1;
+}
+
+BAFE_API int bafe_cuda_plan_describe(int plan, char* buf, size_t buf_size) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    std::string s = p ? p->describe : std::string();
+    if (buf && buf_size) snprintf(buf, buf_size, "%s", s.c_str());
+    return (int)s.size();
+}
+
+BAFE_API int64_t bafe_cuda_plan_output_bytes(int plan) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    return p ? p->out_bytes : -1;
+}
+
+BAFE_API int64_t bafe_cuda_plan_input_bytes(int plan, int i) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p || i < 0 || i >= p->n_inputs) return -1;
+    return p->in_bytes[i];
+}
+
+BAFE_API int bafe_cuda_run_device(int plan, void* const* ptrs, int n_ptrs, void* stream) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
+    return run_plan_device(*p, ptrs, n_ptrs, stream);
+}
+
+BAFE_API int bafe_cuda_run_host(int plan, void* const* ptrs, int n_ptrs) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
+    return run_plan_host(*p, ptrs, n_ptrs);
+}
+
+BAFE_API int bafe_cuda_last_error(char* buf, size_t buf_size) {
+    std::string msg;
+    int code = get_error(msg);
+    if (buf && buf_size) snprintf(buf, buf_size, "%s", msg.c_str());
+    return code;
+}
+
+BAFE_API void bafe_cuda_clear_error(void) { clear_error(); }
+
+BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
+    if (!key || !value) return -1;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Options& o = options();
+    std::string k = key, v = value;
+    if (k == "gemm_precision") {
+        if (v != "auto" && v != "3xtf32" && v != "tf32" && v != "exact") return -1;
+        o.gemm_precision = v;
+        return 0;
+    }
+    if (k == "device") {
+        char* end = nullptr;
+        long d = strtol(value, &end, 10);
+        if (!end || *end || d < -1) return -1;
+        o.device = (int)d;
+        return 0;
+    }
+    return -1;
+}
+
+BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
+    if (!key) return -1;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Options& o = options();
+    std::string k = key, v;
+    if (k == "gemm_precision") v = o.gemm_precision;
+    else if (k == "device") v = std::to_string(o.device);
+    else return -1;
+    if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());
+    return 0;
+}
+
+BAFE_API int64_t bafe_cuda_launch_count(void) { return g_launch_count; }
+
+BAFE_API int64_t bafe_cuda_abi_size(int which) {
+    switch (which) {
+        case 0: return (int64_t)sizeof(bafe_graph);
+        case 1: return (int64_t)sizeof(bafe_node);
+        case 2: return (int64_t)sizeof(bafe_op_attrs);
+        case 3: return (int64_t)sizeof(bafe_shape);
+    }
+    return -1;
+}

@@ -1,0 +1,166 @@
+// internal.h -- shared declarations of libbafe_cuda.so's host runtime.
+//
+// Pipeline (one call of bafe_cuda_jit_get_or_compile):
+//   parse_graph   bafe_graph (BAFE's POD struct) -> Graph (validated, typed)
+//   lower_graph   Graph -> Plan: fusion into launch steps + generated CUDA
+//                 source for all of the plan's kernels (one module)
+//   compile       NVRTC -> sm_100a cubin, cached on disk by source hash
+//   run           driver-API module load (lazily, per device), launches
+#pragma once
+
+#include "bafe_cuda.h"
+
+#include <cstdint>
+#include <string>
+#include <vector>
+
+namespace bafe_cuda {
+
+// ---------------------------------------------------------------- graph --
+
+enum class Op {
+    Input, Constant, MatMul, Add, Sub, Mul, BiasAdd, Relu, Neg, Sigmoid, Tanh,
+    Transpose, ReduceSum, ReduceMax, Reshape, BroadcastTo, LayoutTransform,
+    FusedMatmulRelu, FusedMatmulBias, FusedMatmulBiasRelu, FusedBiasRelu,
+    Unknown
+};
+
+struct Shape {
+    int rank = 0;
+    int64_t d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int64_t numel() const {
+        int64_t n = 1;
+        for (int i = 0; i < rank; ++i) n *= d[i];
+        return n;
+    }
+    bool same(const Shape& o) const {
+        if (rank != o.rank) return false;
+        for (int i = 0; i < rank; ++i) if (d[i] != o.d[i]) return false;
+        return true;
+    }
+    std::string str() const;
+};
+
+struct Node {
+    int id = -1;
+    Op op = Op::Unknown;
+    std::string opname;
+    std::vector<int> ch;
+    Shape shape;
+    int dtype = BAFE_DTYPE_F32;
+    int layout = BAFE_LAYOUT_ROW_MAJOR;
+    int input_index = -1;          // position in g->inputs (kernel parameter order)
+    std::string name;
+    std::vector<int> perm, axes, tshape;
+    bool keepdims = false;
+};
+
+struct Graph {
+    std::vector<Node> nodes;
+    std::vector<int> inputs;       // node ids in parameter order
+    int root = -1;
+};
+
+int parse_graph(const bafe_graph* g, Graph& out, std::string& err);
+int hash_graph(const bafe_graph* g, char* out, size_t out_size);
+
+// Byte size of one stored element of a BAFE dtype.
+int dtype_size(int dtype);
+// Compute type the emitter uses for a node of this dtype (F16/BF16 -> F32).
+int compute_dtype(int dtype);
+const char* dtype_ctype(int dtype);   // device C type of the STORAGE (u16 for halves)
+
+// -------------------------------------------------------------- options --
+
+struct Options {
+    std::string gemm_precision = "auto";   // auto | 3xtf32 | tf32 | exact
+    int device = -1;                        // -1: current device
+};
+Options& options();
+
+// ----------------------------------------------------------------- plan --
+
+struct BufRef {
+    enum Kind { In, Tmp, Out } kind = Tmp;
+    int idx = 0;
+};
+
+enum class StepKind { Ew, GemmExact, GemmTc, Transpose2d, Gather, Reduce, Zero };
+
+struct Step {
+    StepKind kind = StepKind::Ew;
+    std::string kernel;            // entry point (extern "C") in the plan's module
+    std::string kernel_vec;        // Ew: vectorised entry point ("" if none)
+    BufRef dst;
+    std::vector<BufRef> srcs;      // operands in kernel argument order
+    int64_t dst_bytes = 0;
+    // Ew / Zero
+    int64_t n = 0, ncols = 1;
+    std::vector<int> src_esize;    // Ew: stored element size of each operand
+    std::vector<bool> src_row;     // Ew: operand indexed by column (row vector)
+    int dst_esize = 4;
+    // GEMM
+    int64_t M = 0, N = 0, K = 0, batch = 1;
+    int64_t a_bstride = 0, b_bstride = 0, o_bstride = 0;
+    int a_col = 0, b_col = 0;
+    int n_epi = 0;                 // epilogue operands are srcs[2..2+n_epi)
+    bool direct = false;           // fused-form summation order (one chunk)
+    int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
+    // Transpose2d (output M x N), Gather, Reduce
+    int64_t gdims[8] = {0}, gstride[8] = {0};
+    int grank = 0;
+    int axis = 0;
+    std::string describe;
+};
+
+struct DeviceState;   // per-device runtime state of a plan (runtime.cpp)
+
+struct Plan {
+    int id = -1;
+    std::string graph_hash;
+    std::string key;               // graph hash + lowering options
+    int n_inputs = 0;
+    std::vector<int> in_dtypes;
+    std::vector<int64_t> in_bytes;
+    int out_dtype = BAFE_DTYPE_F32;
+    int64_t out_bytes = 0;
+    std::vector<int64_t> tmp_bytes;
+    std::vector<Step> steps;
+    std::string source;            // generated CUDA for every step's kernel
+    std::string source_hash;       // key of the cubin
+    std::string cubin;             // compiled image (kept for lazy per-device loads)
+    std::string describe;
+    std::vector<DeviceState*> dev; // indexed by device ordinal
+};
+
+// Lower a parsed graph into steps + generated source.  Host-only: needs no
+// GPU.  Returns 0 or a nonzero code with a message in err.
+int lower_graph(const Graph& g, const Options& opt, Plan& plan, std::string& err);
+
+// Embedded kernel headers (generated at build time from csrc/kernels/*.cuh).
+struct EmbeddedHeader { const char* name; const char* text; };
+extern const EmbeddedHeader kEmbeddedHeaders[];
+extern const int kNumEmbeddedHeaders;
+
+// NVRTC compile with on-disk cache.  Returns 0, or nonzero with err set.
+int compile_cubin(const std::string& source, const std::string& source_hash,
+                  std::string& cubin, bool& from_cache, std::string& err);
+std::string cache_dir();
+void set_cache_dir(const std::string& d);
+
+// SHA-256 of a byte string, lowercase hex.
+std::string sha256_hex(const void* data, size_t len);
+
+// Runtime (runtime.cpp).
+int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs);
+void release_plan_device_state(Plan& p);
+
+// Error slot shared by every entry point.
+void set_error(int code, const std::string& msg);
+int  get_error(std::string& msg);
+void clear_error();
+
+extern int64_t g_launch_count;
+
+}  // namespace bafe_cuda

@@ -1,0 +1,118 @@
+// gemm_exact.cuh -- CUDA-core GEMM that reproduces BAFE's summation order
+// bit for bit, with a generated elementwise epilogue.
+//
+// BAFE's matmul (codegen.c:240-290) accumulates each output as
+//     v = 0; for each 32-wide k chunk c (increasing k): acc = 0;
+//     acc += A*B over the chunk (left to right); v += acc
+// with every multiply and add rounded separately (no FMA).  The fused
+// forms (codegen.c:477-517) use one plain loop over all K: v = acc.
+// Each thread here owns a 4x4 block of outputs and walks k in exactly that
+// order with __fmul_rn/__fadd_rn, so the result equals the reference's
+// compiled C for any shape.  This is the path for shapes the tensor-core
+// kernel cannot take (TMA stride alignment), for integer and f64 graphs,
+// and for gemm_precision=exact.
+//
+// Tiling: 64x64 output tile per 256-thread block, k staged 32 at a time
+// through shared memory (the chunk width, so a chunk never spans two
+// stages).  Thread (tx, ty) owns rows ty + 16r and columns tx + 16c.
+#pragma once
+#include "bafe_dev.cuh"
+
+namespace bafe {
+
+struct GemmArgs {
+    const void* a;
+    const void* b;
+    void* out;
+    i64 M, N, K, batch;
+    i64 a_bstride, b_bstride, o_bstride;   // elements between batch items
+    int a_col, b_col;                      // operand stored column-major
+    const void* ep[8];                     // epilogue operands
+};
+
+// Spec (generated per step) provides the operand value types TA/TB, the
+// accumulator type T (the matmul node's buffer type), the C product and sum
+// types P = TA*TB and S = T+P, loaders that read and convert one stored
+// element, and apply(acc, g, batch, i, j) -> stored output element (the
+// fused elementwise epilogue).  With all-f32 operands P = S = T = float.
+template <class Spec, bool DIRECT>
+__device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
+    typedef typename Spec::TA TA;
+    typedef typename Spec::TB TB;
+    typedef typename Spec::T T;
+    typedef typename Spec::P P;
+    typedef typename Spec::S S;
+    __shared__ TA As[32][65];   // As[k][m]
+    __shared__ TB Bs[32][65];   // Bs[k][n]
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const i64 bz = blockIdx.z;
+    const i64 m0 = (i64)blockIdx.y * 64, n0 = (i64)blockIdx.x * 64;
+    const i64 M = g.M, N = g.N, K = g.K;
+    const i64 aoff = bz * g.a_bstride, boff = bz * g.b_bstride;
+
+    T v[4][4], acc[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { v[r][c] = (T)0; acc[r][c] = (T)0; }
+
+    for (i64 k0 = 0; k0 < K; k0 += 32) {
+        // Stage A[m0:m0+64, k0:k0+32] and B[k0:k0+32, n0:n0+64].  Elements
+        // outside the matrices are zero on BOTH sides, so padded products
+        // are +0 and leave every partial sum unchanged (an accumulator that
+        // starts at +0 never holds -0, and x + +0 == x for every other x).
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int e = tid + 256 * t;
+            int mm, kk;
+            if (g.a_col) { mm = e & 63; kk = e >> 6; } else { kk = e & 31; mm = e >> 5; }
+            const i64 gm = m0 + mm, gk = k0 + kk;
+            TA val = (TA)0;
+            if (gm < M && gk < K) val = Spec::loadA(g.a, aoff + (g.a_col ? gm + M * gk : gm * K + gk));
+            As[kk][mm] = val;
+            int nn, kb;
+            if (g.b_col) { kb = e & 31; nn = e >> 5; } else { nn = e & 63; kb = e >> 6; }
+            const i64 gn = n0 + nn, gkb = k0 + kb;
+            TB bv = (TB)0;
+            if (gn < N && gkb < K) bv = Spec::loadB(g.b, boff + (g.b_col ? K * gn + gkb : gkb * N + gn));
+            Bs[kb][nn] = bv;
+        }
+        __syncthreads();
+#pragma unroll 4
+        for (int k = 0; k < 32; ++k) {
+            TA a[4];
+            TB b[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) a[r] = As[k][ty + 16 * r];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) b[c] = Bs[k][tx + 16 * c];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    acc[r][c] = (T)add((S)acc[r][c], (S)mul((P)a[r], (P)b[c]));
+        }
+        __syncthreads();
+        if (!DIRECT) {
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) { v[r][c] = add(v[r][c], acc[r][c]); acc[r][c] = (T)0; }
+        }
+    }
+    typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out) + bz * g.o_bstride;
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const i64 i = m0 + ty + 16 * r;
+        if (i >= M) continue;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const i64 j = n0 + tx + 16 * c;
+            if (j >= N) continue;
+            out[i * N + j] = Spec::apply(DIRECT ? acc[r][c] : v[r][c], g, bz, i, j);
+        }
+    }
+}
+
+}  // namespace bafe

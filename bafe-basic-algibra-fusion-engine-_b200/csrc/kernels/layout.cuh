@@ -1,0 +1,97 @@
+// layout.cuh -- data-movement kernels: rank-2 transpose, strided gather
+// (rank-N transpose / broadcast), single-axis reductions.
+//
+// Instantiated by generated code with the element type; results are bit
+// copies (transpose, gather) or follow BAFE's sequential summation order
+// (reductions), so they match the reference exactly.
+#pragma once
+#include "bafe_dev.cuh"
+
+namespace bafe {
+
+// Rank-2 transpose materialisation: out has shape (M, N) and
+// out[i*N + j] = x[j*M + i] (codegen.c:363-369; x is (N, M) row-major).
+// 32x32 tiles staged through shared memory so that both the global read
+// (along x's rows) and the global write (along out's rows) are coalesced;
+// the +1 column pad keeps the transposed shared-memory read conflict-free.
+// Block (32, 8): each thread moves 4 elements per tile.  Grid covers
+// (ceil(N/32), ceil(M/32)) tiles, batched over blockIdx.z.
+template <class T>
+__device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restrict__ out,
+                                            i64 M, i64 N) {
+    __shared__ T tile[32][33];
+    const i64 b = blockIdx.z;
+    x += b * M * N;
+    out += b * M * N;
+    const i64 j0 = (i64)blockIdx.x * 32;   // output column block == x row block
+    const i64 i0 = (i64)blockIdx.y * 32;   // output row block == x column block
+    const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+    for (int r = 0; r < 32; r += 8) {
+        const i64 xr = j0 + ty + r, xc = i0 + tx;       // x[xr][xc], x is (N, M)
+        if (xr < N && xc < M) tile[ty + r][tx] = x[xr * M + xc];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 32; r += 8) {
+        const i64 oi = i0 + ty + r, oj = j0 + tx;       // out[oi][oj] = x[oj][oi]
+        if (oi < M && oj < N) out[oi * N + oj] = tile[tx][ty + r];
+    }
+}
+
+// Strided gather over a rank-R output: out[o] = x[sum_d coord_d(o) * stride[d]]
+// where coord_d is o's row-major coordinate.  Used for rank-N transposes
+// (stride = input stride of the permuted axis) and for broadcast_to
+// (stride 0 on broadcast axes).  Grid-stride, one element per step.
+struct GatherArgs {
+    i64 numel;
+    int rank;
+    i64 dims[8];
+    i64 stride[8];
+};
+
+template <class T>
+__device__ __forceinline__ void gather_nd(const T* __restrict__ x, T* __restrict__ out,
+                                          const GatherArgs& g) {
+    for (i64 o = (i64)blockIdx.x * blockDim.x + threadIdx.x; o < g.numel;
+         o += (i64)gridDim.x * blockDim.x) {
+        i64 rem = o, src = 0;
+        for (int d = g.rank - 1; d >= 0; --d) {
+            const i64 c = rem % g.dims[d];
+            rem /= g.dims[d];
+            src += c * g.stride[d];
+        }
+        out[o] = x[src];
+    }
+}
+
+// Single-axis reduction of an (M, N) tensor, sequential per output element
+// exactly as codegen.c:410-445 loops: axis 0 -> one output per column j
+// (consecutive threads read consecutive columns: coalesced), axis 1 -> one
+// output per row i.  Sum starts from 0; max starts from the first element
+// and replaces on a strict `>`.
+template <class T, bool IS_MAX>
+__device__ __forceinline__ void reduce_axis(const T* __restrict__ x, T* __restrict__ out,
+                                            i64 M, i64 N, int axis) {
+    const i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+    if (axis == 0) {
+        if (t >= N) return;
+        T v = IS_MAX ? x[t] : (T)0;
+        for (i64 i = IS_MAX ? 1 : 0; i < M; ++i) {
+            const T e = x[i * N + t];
+            if (IS_MAX) { if (e > v) v = e; } else { v = add(v, e); }
+        }
+        out[t] = v;
+    } else {
+        if (t >= M) return;
+        const T* row = x + t * N;
+        T v = IS_MAX ? row[0] : (T)0;
+        for (i64 j = IS_MAX ? 1 : 0; j < N; ++j) {
+            const T e = row[j];
+            if (IS_MAX) { if (e > v) v = e; } else { v = add(v, e); }
+        }
+        out[t] = v;
+    }
+}
+
+}  // namespace bafe

@@ -1,0 +1,52 @@
+// kernels_check.cu -- nvcc sm_100a compile check of the device templates
+// that NVRTC instantiates at run time (built by `make check`, never loaded).
+// It instantiates each template once with a representative generated spec
+// so that `-Xptxas -v` reports registers / spills / shared memory.
+#include "bafe_dev.cuh"
+#include "layout.cuh"
+#include "gemm_exact.cuh"
+#include "gemm_tc.cuh"
+
+// relu(matmul(A,B) + C), all f32, as the lowering emits it.
+struct CheckSpec {
+    typedef float TA; typedef float TB; typedef float T; typedef float P; typedef float S;
+    typedef float Out;
+    static __device__ __forceinline__ TA loadA(const void* p, i64 i) { return reinterpret_cast<const float*>(p)[i]; }
+    static __device__ __forceinline__ TB loadB(const void* p, i64 i) { return reinterpret_cast<const float*>(p)[i]; }
+    template <class G> static __device__ __forceinline__ Out apply(T acc, const G& g, i64 b, i64 i, i64 j) {
+        const i64 flat = b * g.o_bstride + i * g.N + j;
+        const float x0 = reinterpret_cast<const float*>(g.ep[0])[flat];
+        return bafe::relu(bafe::add(acc, x0));
+    }
+};
+
+extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
+    bafe::gemm_exact<CheckSpec, false>(g);
+}
+extern "C" __global__ void __launch_bounds__(BAFE_TC_THREADS, 1) check_gemm_tc3(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc<CheckSpec, 3>(g);
+}
+extern "C" __global__ void __launch_bounds__(BAFE_TC_THREADS, 1) check_gemm_tc1(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc<CheckSpec, 1>(g);
+}
+extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
+    bafe::transpose2d<float>(x, out, M, N);
+}
+extern "C" __global__ void __launch_bounds__(256) check_gather(const float* x, float* out, const bafe::GatherArgs g) {
+    bafe::gather_nd<float>(x, out, g);
+}
+extern "C" __global__ void __launch_bounds__(256) check_reduce(const float* x, float* out, i64 M, i64 N, int axis) {
+    bafe::reduce_axis<float, false>(x, out, M, N, axis);
+}
+// relu(add(mul(X,Y),Z)) streaming kernel body as generated (4-wide).
+extern "C" __global__ void __launch_bounds__(256) check_ew(const float* __restrict__ x, const float* __restrict__ y,
+                                                          const float* __restrict__ z, float* __restrict__ o, i64 n) {
+    const i64 ng = n >> 2;
+    for (i64 g = (i64)blockIdx.x * blockDim.x + threadIdx.x; g < ng; g += (i64)gridDim.x * blockDim.x) {
+        const auto a = bafe::ld4(x + 4 * g), b = bafe::ld4(y + 4 * g), c = bafe::ld4(z + 4 * g);
+        bafe::Vec4<float> r;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) r.v[l] = bafe::relu(bafe::add(bafe::mul(a.v[l], b.v[l]), c.v[l]));
+        bafe::st4(o + 4 * g, r);
+    }
+}

@@ -1,0 +1,585 @@
+// runtime.cpp -- compile (NVRTC, on-disk cubin cache), load (CUDA driver
+// API), run (launch steps on device buffers; host calls stage through
+// device buffers the plan owns).
+//
+// The CUDA runtime is linked statically and loads the driver lazily, so the
+// library loads -- and plans compile -- on a machine without a GPU; the
+// first launch then fails with a recorded error instead.
+#include "internal.h"
+#include "tc_launch.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <nvrtc.h>
+
+#include <cerrno>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <fstream>
+#include <mutex>
+#include <sstream>
+#include <sys/stat.h>
+#include <unistd.h>
+
+namespace bafe_cuda {
+
+int64_t g_launch_count = 0;
+
+// --------------------------------------------------------------- errors --
+
+namespace {
+int g_err_code = 0;
+std::string g_err_msg;
+}  // namespace
+
+void set_error(int code, const std::string& msg) {
+    g_err_code = code;
+    g_err_msg = msg;
+}
+int get_error(std::string& msg) {
+    msg = g_err_msg;
+    return g_err_code;
+}
+void clear_error() {
+    g_err_code = 0;
+    g_err_msg.clear();
+}
+
+// ----------------------------------------------------------- cache dir --
+
+namespace {
+std::string g_cache_dir;
+bool g_cache_dir_set = false;
+
+void mkdirs(const std::string& path) {
+    std::string cur;
+    for (size_t i = 0; i < path.size(); ++i) {
+        cur += path[i];
+        if (path[i] == '/' && cur.size() > 1) mkdir(cur.c_str(), 0755);
+    }
+    mkdir(path.c_str(), 0755);
+}
+}  // namespace
+
+// $BAFE_CACHE_DIR, else $HOME/.bafecache, else ./.bafecache (jit.c:173-189).
+std::string cache_dir() {
+    if (g_cache_dir_set) return g_cache_dir;
+    const char* env = getenv("BAFE_CACHE_DIR");
+    if (env && *env) g_cache_dir = env;
+    else if (const char* home = getenv("HOME")) g_cache_dir = std::string(home) + "/.bafecache";
+    else g_cache_dir = ".bafecache";
+    g_cache_dir_set = true;
+    return g_cache_dir;
+}
+void set_cache_dir(const std::string& d) {
+    g_cache_dir = d;
+    g_cache_dir_set = true;
+}
+
+// --------------------------------------------------------------- NVRTC --
+
+namespace {
+std::string headers_digest() {
+    static std::string d;
+    if (d.empty()) {
+        std::string all;
+        for (int i = 0; i < kNumEmbeddedHeaders; ++i) {
+            all += kEmbeddedHeaders[i].name;
+            all += '\0';
+            all += kEmbeddedHeaders[i].text;
+            all += '\0';
+        }
+        d = sha256_hex(all.data(), all.size());
+    }
+    return d;
+}
+
+const char* kNvrtcOpts[] = {
+    "--gpu-architecture=sm_100a",
+    "-std=c++17",
+    // No contraction anywhere: the reference's C rounds every op.
+    "--fmad=false",
+    "-lineinfo",
+    "-DBAFE_NVRTC=1",
+};
+}  // namespace
+
+int compile_cubin(const std::string& source, const std::string& source_hash, std::string& cubin,
+                  bool& from_cache, std::string& err) {
+    from_cache = false;
+    int major = 0, minor = 0;
+    nvrtcVersion(&major, &minor);
+    std::string keysrc = source_hash + "|" + headers_digest() + "|nvrtc" + std::to_string(major) + "." +
+                         std::to_string(minor);
+    for (const char* o : kNvrtcOpts) keysrc += std::string("|") + o;
+    const std::string key = sha256_hex(keysrc.data(), keysrc.size());
+    const std::string dir = cache_dir() + "/cuda";
+    const std::string path = dir + "/" + key + ".cubin";
+    {
+        std::ifstream f(path, std::ios::binary);
+        if (f) {
+            std::ostringstream ss;
+            ss << f.rdbuf();
+            cubin = ss.str();
+            if (cubin.size() > 16 && memcmp(cubin.data(), "\x7f" "ELF", 4) == 0) {
+                from_cache = true;
+                return 0;
+            }
+            cubin.clear();   // corrupt entry: recompile and overwrite
+        }
+    }
+    std::vector<const char*> names, texts;
+    for (int i = 0; i < kNumEmbeddedHeaders; ++i) {
+        names.push_back(kEmbeddedHeaders[i].name);
+        texts.push_back(kEmbeddedHeaders[i].text);
+    }
+    nvrtcProgram prog;
+    nvrtcResult r = nvrtcCreateProgram(&prog, source.c_str(), "bafe_plan.cu", (int)names.size(), texts.data(),
+                                       names.data());
+    if (r != NVRTC_SUCCESS) {
+        err = std::string("nvrtcCreateProgram: ") + nvrtcGetErrorString(r);
+        return 3;
+    }
+    std::vector<const char*> opts(std::begin(kNvrtcOpts), std::end(kNvrtcOpts));
+    if (getenv("BAFE_PTXAS_VERBOSE")) opts.push_back("--ptxas-options=-v");
+    r = nvrtcCompileProgram(prog, (int)opts.size(), opts.data());
+    size_t log_size = 0;
+    nvrtcGetProgramLogSize(prog, &log_size);
+    std::string log(log_size, '\0');
+    if (log_size) nvrtcGetProgramLog(prog, &log[0]);
+    if (getenv("BAFE_PTXAS_VERBOSE") && log_size > 1) fprintf(stderr, "[bafe_cuda] nvrtc log:\n%s\n", log.c_str());
+    if (r != NVRTC_SUCCESS) {
+        err = std::string("compile failed: ") + nvrtcGetErrorString(r) + "\n" + log.substr(0, 4000);
+        nvrtcDestroyProgram(&prog);
+        return 3;
+    }
+    size_t n = 0;
+    nvrtcGetCUBINSize(prog, &n);
+    cubin.assign(n, '\0');
+    nvrtcGetCUBIN(prog, &cubin[0]);
+    nvrtcDestroyProgram(&prog);
+    // Atomic publish: concurrent ranks may compile the same key.
+    mkdirs(dir);
+    const std::string tmp = path + ".tmp." + std::to_string((long long)getpid());
+    {
+        std::ofstream f(tmp, std::ios::binary);
+        f.write(cubin.data(), (std::streamsize)cubin.size());
+    }
+    if (rename(tmp.c_str(), path.c_str()) != 0) unlink(tmp.c_str());
+    return 0;
+}
+
+// -------------------------------------------------------- driver table --
+
+namespace {
+struct Driver {
+    bool ok = false;
+    std::string why;
+    decltype(&cuModuleLoadData) moduleLoadData = nullptr;
+    decltype(&cuModuleUnload) moduleUnload = nullptr;
+    decltype(&cuModuleGetFunction) moduleGetFunction = nullptr;
+    decltype(&cuFuncSetAttribute) funcSetAttribute = nullptr;
+    decltype(&cuLaunchKernelEx) launchKernelEx = nullptr;
+    decltype(&cuTensorMapEncodeTiled) tensorMapEncodeTiled = nullptr;
+    decltype(&cuGetErrorString) getErrorString = nullptr;
+};
+
+Driver& driver() {
+    static Driver d;
+    static bool init = false;
+    if (init) return d;
+    init = true;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess || count == 0) {
+        d.why = std::string("no CUDA device available (") + cudaGetErrorString(e) + ")";
+        cudaGetLastError();
+        return d;
+    }
+    auto get = [&](const char* name, void** fn) {
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint(name, fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || !*fn) {
+            d.why = std::string("driver entry point missing: ") + name;
+            return false;
+        }
+        return true;
+    };
+    if (!get("cuModuleLoadData", (void**)&d.moduleLoadData)) return d;
+    if (!get("cuModuleUnload", (void**)&d.moduleUnload)) return d;
+    if (!get("cuModuleGetFunction", (void**)&d.moduleGetFunction)) return d;
+    if (!get("cuFuncSetAttribute", (void**)&d.funcSetAttribute)) return d;
+    if (!get("cuLaunchKernelEx", (void**)&d.launchKernelEx)) return d;
+    if (!get("cuTensorMapEncodeTiled", (void**)&d.tensorMapEncodeTiled)) return d;
+    if (!get("cuGetErrorString", (void**)&d.getErrorString)) return d;
+    d.ok = true;
+    return d;
+}
+
+std::string cu_err(CUresult r) {
+    const char* s = nullptr;
+    if (driver().getErrorString) driver().getErrorString(r, &s);
+    return s ? s : ("CUresult " + std::to_string((int)r));
+}
+
+int sm_count(int dev) {
+    static int cache[64] = {0};
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = v > 0 ? v : 148;
+    }
+    return cache[dev];
+}
+}  // namespace
+
+// Driver calls used by the tensor-core launcher (tc_launch.cpp).
+int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle128, std::string& err) {
+    Driver& d = driver();
+    if (!d.ok) { err = d.why; return 4; }
+    cuuint64_t gd[5], gs[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) { gd[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
+    for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
+    CUresult r = d.tensorMapEncodeTiled(
+        reinterpret_cast<CUtensorMap*>(map), dtype_is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+        (cuuint32_t)rank, gaddr, gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) { err = "cuTensorMapEncodeTiled: " + cu_err(r); return 4; }
+    return 0;
+}
+
+// ------------------------------------------------------ device state --
+
+struct DeviceState {
+    int device = -1;
+    CUmodule module = nullptr;
+    std::vector<CUfunction> fn, fn_vec;
+    std::vector<void*> tmp;
+    std::vector<void*> in_stage;
+    void* out_stage = nullptr;
+    cudaStream_t stream = nullptr;
+};
+
+namespace {
+
+int ensure_device_state(Plan& p, int dev, DeviceState*& out) {
+    Driver& d = driver();
+    if (!d.ok) { set_error(4, d.why); return 4; }
+    if ((int)p.dev.size() <= dev) p.dev.resize(dev + 1, nullptr);
+    if (p.dev[dev]) { out = p.dev[dev]; return 0; }
+    DeviceState* s = new DeviceState();
+    s->device = dev;
+    cudaFree(nullptr);   // make the device's primary context current
+    CUresult r = d.moduleLoadData(&s->module, p.cubin.data());
+    if (r != CUDA_SUCCESS) {
+        set_error(5, "cuModuleLoadData: " + cu_err(r));
+        delete s;
+        return 5;
+    }
+    for (auto& st : p.steps) {
+        CUfunction f = nullptr, fv = nullptr;
+        if (!st.kernel.empty()) {
+            r = d.moduleGetFunction(&f, s->module, st.kernel.c_str());
+            if (r != CUDA_SUCCESS) {
+                set_error(5, "cuModuleGetFunction(" + st.kernel + "): " + cu_err(r));
+                d.moduleUnload(s->module);
+                delete s;
+                return 5;
+            }
+            if (st.kind == StepKind::GemmTc) {
+                r = d.funcSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, tc_smem_bytes(st.tc_variant));
+                if (r != CUDA_SUCCESS) {
+                    set_error(5, "cuFuncSetAttribute(smem): " + cu_err(r));
+                    d.moduleUnload(s->module);
+                    delete s;
+                    return 5;
+                }
+            }
+        }
+        if (!st.kernel_vec.empty()) d.moduleGetFunction(&fv, s->module, st.kernel_vec.c_str());
+        s->fn.push_back(f);
+        s->fn_vec.push_back(fv);
+    }
+    p.dev[dev] = s;
+    out = s;
+    return 0;
+}
+
+int alloc(void** ptr, int64_t bytes) {
+    *ptr = nullptr;
+    if (bytes <= 0) return 0;
+    cudaError_t e = cudaMalloc(ptr, (size_t)bytes);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(6, "cudaMalloc(" + std::to_string((long long)bytes) + "): " + cudaGetErrorString(e));
+        return 6;
+    }
+    return 0;
+}
+
+int launch(CUfunction f, unsigned gx, unsigned gy, unsigned gz, unsigned bx, unsigned by, unsigned bz,
+           unsigned smem, cudaStream_t stream, void** params) {
+    CUlaunchConfig cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDimX = gx; cfg.gridDimY = gy; cfg.gridDimZ = gz;
+    cfg.blockDimX = bx; cfg.blockDimY = by; cfg.blockDimZ = bz;
+    cfg.sharedMemBytes = smem;
+    cfg.hStream = (CUstream)stream;
+    CUresult r = driver().launchKernelEx(&cfg, f, params, nullptr);
+    if (r != CUDA_SUCCESS) {
+        set_error(7, "kernel launch failed: " + cu_err(r));
+        return 7;
+    }
+    ++g_launch_count;
+    return 0;
+}
+
+unsigned grid_for(int64_t units, int dev) {
+    int64_t g = (units + 255) / 256;
+    int64_t cap = (int64_t)sm_count(dev) * 8;
+    if (g > cap) g = cap;
+    if (g < 1) g = 1;
+    return (unsigned)g;
+}
+
+// Host mirrors of the kernels' by-value argument structs (layouts must
+// match csrc/kernels/*.cuh).
+struct GemmArgsHost {
+    const void* a; const void* b; void* out;
+    int64_t M, N, K, batch;
+    int64_t a_bstride, b_bstride, o_bstride;
+    int32_t a_col, b_col;
+    const void* ep[8];
+};
+static_assert(sizeof(GemmArgsHost) == 152, "GemmArgs layout");
+struct GatherArgsHost {
+    int64_t numel;
+    int32_t rank;
+    int64_t dims[8];
+    int64_t stride[8];
+};
+static_assert(sizeof(GatherArgsHost) == 144, "GatherArgs layout");
+
+}  // namespace
+
+int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
+    if (n_ptrs != p.n_inputs + 1) {
+        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
+        return 8;
+    }
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, std::string("no CUDA device available (") + cudaGetErrorString(ce) + ")");
+        return 4;
+    }
+    DeviceState* ds = nullptr;
+    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+    if (ds->tmp.size() != p.tmp_bytes.size()) {
+        ds->tmp.assign(p.tmp_bytes.size(), nullptr);
+        for (size_t t = 0; t < p.tmp_bytes.size(); ++t)
+            if (int rc = alloc(&ds->tmp[t], p.tmp_bytes[t])) return rc;
+    }
+    cudaStream_t stream = (cudaStream_t)stream_v;
+    auto ptr_of = [&](const BufRef& b) -> void* {
+        switch (b.kind) {
+            case BufRef::In: return ptrs[b.idx];
+            case BufRef::Tmp: return ds->tmp[b.idx];
+            default: return ptrs[p.n_inputs];
+        }
+    };
+    for (size_t si = 0; si < p.steps.size(); ++si) {
+        Step& s = p.steps[si];
+        void* dst = ptr_of(s.dst);
+        switch (s.kind) {
+            case StepKind::Zero: {
+                if (s.dst_bytes > 0) {
+                    cudaError_t e = cudaMemsetAsync(dst, 0, (size_t)s.dst_bytes, stream);
+                    if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e)); return 7; }
+                }
+                break;
+            }
+            case StepKind::Ew: {
+                if (s.n == 0) break;
+                std::vector<uint64_t> args;
+                bool vec = ds->fn_vec[si] != nullptr;
+                for (size_t k = 0; k < s.srcs.size(); ++k) {
+                    void* q = ptr_of(s.srcs[k]);
+                    args.push_back((uint64_t)(uintptr_t)q);
+                    uintptr_t need = s.src_esize[k] == 2 ? 8 : 16;
+                    if ((uintptr_t)q % need) vec = false;
+                    if (s.src_row[k] && (s.ncols % 4)) vec = false;
+                }
+                if ((uintptr_t)dst % (s.dst_esize == 2 ? 8 : 16)) vec = false;
+                args.push_back((uint64_t)(uintptr_t)dst);
+                args.push_back((uint64_t)s.n);
+                args.push_back((uint64_t)s.ncols);
+                void* params[] = {args.data()};
+                int64_t units = vec ? s.n / 4 : s.n;
+                if (int rc = launch(vec ? ds->fn_vec[si] : ds->fn[si], grid_for(units, dev), 1, 1, 256, 1, 1, 0,
+                                    stream, params))
+                    return rc;
+                break;
+            }
+            case StepKind::GemmExact: {
+                if (s.M == 0 || s.N == 0 || s.batch == 0) break;
+                GemmArgsHost g;
+                memset(&g, 0, sizeof(g));
+                g.a = ptr_of(s.srcs[0]);
+                g.b = ptr_of(s.srcs[1]);
+                g.out = dst;
+                g.M = s.M; g.N = s.N; g.K = s.K; g.batch = s.batch;
+                g.a_bstride = s.a_bstride; g.b_bstride = s.b_bstride; g.o_bstride = s.o_bstride;
+                g.a_col = s.a_col; g.b_col = s.b_col;
+                for (int k = 0; k < s.n_epi; ++k) g.ep[k] = ptr_of(s.srcs[2 + k]);
+                void* params[] = {&g};
+                if (s.batch > 65535 || (s.M + 63) / 64 > 65535) { set_error(8, "GEMM grid too large"); return 8; }
+                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 63) / 64), (unsigned)((s.M + 63) / 64),
+                                    (unsigned)s.batch, 256, 1, 1, 0, stream, params))
+                    return rc;
+                break;
+            }
+            case StepKind::GemmTc: {
+                std::vector<const void*> ep;
+                for (int k = 0; k < s.n_epi; ++k) ep.push_back(ptr_of(s.srcs[2 + k]));
+                TcLaunch L;
+                std::string err;
+                if (int rc = tc_prepare(s, ptr_of(s.srcs[0]), ptr_of(s.srcs[1]), dst, ep, sm_count(dev), L, err)) {
+                    set_error(rc, err);
+                    return rc;
+                }
+                void* params[] = {L.args};
+                CUlaunchConfig cfg;
+                memset(&cfg, 0, sizeof(cfg));
+                cfg.gridDimX = L.grid; cfg.gridDimY = 1; cfg.gridDimZ = 1;
+                cfg.blockDimX = L.block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
+                cfg.sharedMemBytes = L.smem;
+                cfg.hStream = (CUstream)stream;
+                CUresult r = driver().launchKernelEx(&cfg, ds->fn[si], params, nullptr);
+                if (r != CUDA_SUCCESS) { set_error(7, "tensor-core GEMM launch failed: " + cu_err(r)); return 7; }
+                ++g_launch_count;
+                break;
+            }
+            case StepKind::Transpose2d: {
+                if (s.M == 0 || s.N == 0) break;
+                const void* x = ptr_of(s.srcs[0]);
+                int64_t M = s.M, Nn = s.N;
+                void* params[] = {&x, &dst, &M, &Nn};
+                if ((s.M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
+                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((s.M + 31) / 32), 1, 32, 8, 1,
+                                    0, stream, params))
+                    return rc;
+                break;
+            }
+            case StepKind::Gather: {
+                if (s.n == 0) break;
+                const void* x = ptr_of(s.srcs[0]);
+                GatherArgsHost g;
+                memset(&g, 0, sizeof(g));
+                g.numel = s.n;
+                g.rank = s.grank;
+                for (int d = 0; d < s.grank; ++d) { g.dims[d] = s.gdims[d]; g.stride[d] = s.gstride[d]; }
+                void* params[] = {&x, &dst, &g};
+                if (int rc = launch(ds->fn[si], grid_for(s.n, dev), 1, 1, 256, 1, 1, 0, stream, params)) return rc;
+                break;
+            }
+            case StepKind::Reduce: {
+                const void* x = ptr_of(s.srcs[0]);
+                int64_t M = s.M, Nn = s.N;
+                int axis = s.axis;
+                int64_t outs = axis == 0 ? s.N : s.M;
+                if (outs == 0) break;
+                void* params[] = {&x, &dst, &M, &Nn, &axis};
+                if (int rc = launch(ds->fn[si], (unsigned)((outs + 255) / 256), 1, 1, 256, 1, 1, 0, stream, params))
+                    return rc;
+                break;
+            }
+        }
+    }
+    return 0;
+}
+
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
+    if (n_ptrs != p.n_inputs + 1) {
+        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
+        return 8;
+    }
+    int dev = options().device;
+    if (dev < 0) {
+        if (cudaGetDevice(&dev) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(4, "no CUDA device available");
+            return 4;
+        }
+    }
+    if (cudaSetDevice(dev) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, "cannot select CUDA device " + std::to_string(dev));
+        return 4;
+    }
+    DeviceState* ds = nullptr;
+    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+    if (!ds->stream) {
+        if (cudaStreamCreateWithFlags(&ds->stream, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(6, "cudaStreamCreate failed");
+            return 6;
+        }
+    }
+    if (ds->in_stage.size() != (size_t)p.n_inputs) {
+        ds->in_stage.assign(p.n_inputs, nullptr);
+        for (int k = 0; k < p.n_inputs; ++k)
+            if (int rc = alloc(&ds->in_stage[k], p.in_bytes[k])) return rc;
+        if (int rc = alloc(&ds->out_stage, p.out_bytes)) return rc;
+    }
+    for (int k = 0; k < p.n_inputs; ++k) {
+        if (p.in_bytes[k] == 0) continue;
+        cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], ptrs[k], (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
+        if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e)); return 7; }
+    }
+    std::vector<void*> dptrs(ds->in_stage);
+    dptrs.push_back(ds->out_stage);
+    if (int rc = run_plan_device(p, dptrs.data(), (int)dptrs.size(), ds->stream)) {
+        cudaStreamSynchronize(ds->stream);
+        return rc;
+    }
+    if (p.out_bytes) {
+        cudaError_t e = cudaMemcpyAsync(ptrs[p.n_inputs], ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
+        if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e)); return 7; }
+    }
+    cudaError_t e = cudaStreamSynchronize(ds->stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(9, std::string("device error: ") + cudaGetErrorString(e));
+        return 9;
+    }
+    return 0;
+}
+
+void release_plan_device_state(Plan& p) {
+    Driver& d = driver();
+    int prev = -1;
+    cudaGetDevice(&prev);
+    for (DeviceState* s : p.dev) {
+        if (!s) continue;
+        cudaSetDevice(s->device);
+        if (s->stream) cudaStreamSynchronize(s->stream);
+        for (void* t : s->tmp) if (t) cudaFree(t);
+        for (void* t : s->in_stage) if (t) cudaFree(t);
+        if (s->out_stage) cudaFree(s->out_stage);
+        if (s->stream) cudaStreamDestroy(s->stream);
+        if (s->module && d.ok) d.moduleUnload(s->module);
+        delete s;
+    }
+    p.dev.clear();
+    if (prev >= 0) cudaSetDevice(prev);
+    cudaGetLastError();
+}
+
+}  // namespace bafe_cuda

@@ -1,0 +1,20 @@
+// tc_launch.h -- host side of the tensor-core GEMM: tensor maps, grid and
+// the by-value argument block of bafe::gemm_tc (kernels/gemm_tc.cuh).
+#pragma once
+#include "internal.h"
+
+namespace bafe_cuda {
+
+struct TcLaunch {
+    alignas(64) unsigned char args[1024];
+    unsigned grid = 0, block = 0, smem = 0;
+};
+
+bool tc_kernel_enabled();
+int tc_smem_bytes(int variant);
+int tc_prepare(const Step& s, const void* a, const void* b, void* out, const std::vector<const void*>& ep,
+               int sm_count, TcLaunch& L, std::string& err);
+int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle128, std::string& err);
+
+}  // namespace bafe_cuda

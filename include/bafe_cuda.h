@@ -1,0 +1,199 @@
+/* bafe_cuda.h -- C ABI of libbafe_cuda.so, the B200 execution backend for BAFE.
+ *
+ * The backend sits behind BAFE's JIT entry point.  BAFE's optimizer hands
+ * the extracted graph to bafe_jit_get_or_compile (bafe/include/bafe/jit.h:45)
+ * and calls the returned function as
+ *     void f(const void *in_0, ..., const void *in_{n-1}, void *out)
+ * with HOST pointers (bafe/python/bafe/__init__.py:369-383,522).
+ * bafe_cuda_jit_get_or_compile has the same signature and contract: it
+ * returns a function pointer of the same calling convention, which copies
+ * the inputs to the GPU, runs the sm_100a kernels the graph was lowered to,
+ * copies the result back and returns when `out` holds it.
+ *
+ * Every declaration below names the reference interface it replaces
+ * (file:line within the reference project), or says that it is new.
+ * All entry points are plain C: pointers, sizes and ints, no C++ or torch
+ * types.  Nothing here is thread-safe beyond what the reference promises
+ * (jit.c:160-171 keeps unsynchronised globals; callers serialise).
+ */
+#ifndef BAFE_CUDA_H
+#define BAFE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <stdbool.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------
+ * Graph ABI.  The backend consumes BAFE's graph struct by pointer, so its
+ * layout must be byte-identical to the reference's (types.h:28-94,
+ * ops.h:236-250, ir.h:128-155; mirrored in Python at _binding.py:62-112).
+ * If the reference headers were included first, their definitions are used.
+ * ---------------------------------------------------------------------- */
+#ifndef BAFE_TYPES_H
+typedef enum {
+    BAFE_DTYPE_F32 = 0, BAFE_DTYPE_F64 = 1, BAFE_DTYPE_I32 = 2,
+    BAFE_DTYPE_I64 = 3, BAFE_DTYPE_F16 = 4, BAFE_DTYPE_BF16 = 5
+} bafe_dtype;
+#define BAFE_MAX_RANK 8
+typedef struct { int32_t dims[BAFE_MAX_RANK]; int32_t rank; } bafe_shape;
+typedef enum {
+    BAFE_LAYOUT_ROW_MAJOR = 0, BAFE_LAYOUT_COL_MAJOR = 1,
+    BAFE_LAYOUT_BLOCKED = 2, BAFE_LAYOUT_TENSOR_CORE = 3
+} bafe_layout;
+#endif /* BAFE_TYPES_H */
+
+#ifndef BAFE_OPS_H
+#define BAFE_MAX_ATTR_LEN 32
+typedef struct {
+    int32_t n_axes;  int32_t axes[BAFE_MAX_ATTR_LEN];
+    int32_t n_perm;  int32_t perm[BAFE_MAX_ATTR_LEN];
+    int32_t n_shape; int32_t shape[BAFE_MAX_ATTR_LEN];
+    bool    keepdims;
+    double  scalar_value;
+    bool    has_scalar;
+    char    name[BAFE_MAX_ATTR_LEN];
+} bafe_op_attrs;
+#endif /* BAFE_OPS_H */
+
+#ifndef BAFE_IR_H
+#define BAFE_MAX_CHILDREN 4
+#define BAFE_MAX_NODES    4096
+typedef int32_t bafe_node_id;
+typedef struct {
+    bafe_node_id  id;
+    const char   *op_name;
+    bafe_op_attrs attrs;
+    int           n_children;
+    bafe_node_id  children[BAFE_MAX_CHILDREN];
+    bafe_shape    shape;
+    bafe_dtype    dtype;
+    bafe_layout   layout;
+    char          input_name[BAFE_MAX_ATTR_LEN];
+    bool          is_input;
+    bool          is_constant;
+    double        const_value;
+} bafe_node;
+typedef struct {
+    bafe_node    nodes[BAFE_MAX_NODES];
+    int          n_nodes;
+    bafe_node_id inputs[BAFE_MAX_NODES];
+    int          n_inputs;
+    bafe_node_id outputs[BAFE_MAX_NODES];
+    int          n_outputs;
+} bafe_graph;
+#endif /* BAFE_IR_H */
+
+#ifndef BAFE_JIT_H
+/* jit.h:35 -- callers cast to void (*)(void *in..., void *out). */
+typedef void (*bafe_kernel_fn)(void);
+/* jit.h:56-61 */
+typedef struct { int hits; int misses; int compiles; int compile_failures; } bafe_jit_stats;
+#endif /* BAFE_JIT_H */
+
+/* ------------------------------------------------------------------------
+ * Drop-in replacements for bafe/include/bafe/jit.h
+ * ---------------------------------------------------------------------- */
+
+/* Replaces bafe_jit_hash_graph (jit.h:39, jit.c:131-154): SHA-256 over the
+ * same canonical byte stream, so both backends key a graph identically.
+ * Returns 0, or -1 when out_size < 65. */
+int bafe_cuda_jit_hash_graph(const bafe_graph *g, char *out, size_t out_size);
+
+/* Replaces bafe_jit_get_or_compile (jit.h:45-46, jit.c:204-328).
+ * Lowers the graph to a plan of sm_100a kernels (generated CUDA compiled
+ * once by NVRTC into a cubin, cached on disk by key), and returns a host
+ * function pointer f(in_0, ..., in_{n-1}, out) taking host pointers, in the
+ * graph's input order (g->inputs).  Returns NULL and writes a message into
+ * err_buf on failure (unsupported graph, compile failure, no CUDA device).
+ * The pointer stays valid until bafe_cuda_jit_clear /
+ * bafe_cuda_jit_invalidate_memory_cache, like the reference's. */
+bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph *g,
+                                            char *err_buf, size_t err_buf_size);
+
+/* Replaces bafe_jit_set_cache_dir / bafe_jit_cache_dir (jit.h:50,53,
+ * jit.c:173-196): $BAFE_CACHE_DIR, else $HOME/.bafecache.  Cubins live in
+ * <dir>/cuda/<key>.cubin. */
+void bafe_cuda_jit_set_cache_dir(const char *dir);
+const char *bafe_cuda_jit_cache_dir(void);
+
+/* Replaces bafe_jit_get_stats (jit.h:63, jit.c:330-332).  hits counts
+ * in-memory and on-disk cubin hits, compiles counts NVRTC compiles. */
+bafe_jit_stats bafe_cuda_jit_get_stats(void);
+
+/* Replaces bafe_jit_clear (jit.h:66, jit.c:334-340): drops every plan,
+ * unloads modules, frees device buffers, zeroes the stats. */
+void bafe_cuda_jit_clear(void);
+
+/* Replaces bafe_jit_invalidate_memory_cache (jit.h:71, jit.c:342-354):
+ * drops plans but keeps on-disk cubins and the stats. */
+void bafe_cuda_jit_invalidate_memory_cache(void);
+
+/* ------------------------------------------------------------------------
+ * Backend extensions (no counterpart in the reference).
+ * ---------------------------------------------------------------------- */
+
+/* Backend/ABI version (major*1000 + minor). */
+int bafe_cuda_version(void);
+
+/* Plan id behind a function returned by bafe_cuda_jit_get_or_compile,
+ * or -1 if fn is not one of ours. */
+int bafe_cuda_plan_of(bafe_kernel_fn fn);
+
+/* Number of graph inputs the plan's function takes (the output pointer is
+ * one more).  -1 for an unknown plan. */
+int bafe_cuda_plan_num_inputs(int plan);
+
+/* Human-readable lowering of the plan: one line per launch step, e.g.
+ * "gemm.tc3xtf32 m=4096 n=4096 k=4096 a=row b=row epi=relu(add(acc,mul(in2,in3)))".
+ * Returns the full length (like snprintf). */
+int bafe_cuda_plan_describe(int plan, char *buf, size_t buf_size);
+
+/* Number of bytes of the output and of input i (in graph input order). */
+int64_t bafe_cuda_plan_output_bytes(int plan);
+int64_t bafe_cuda_plan_input_bytes(int plan, int i);
+
+/* Run a plan on device-resident buffers: ptrs[0..n_inputs-1] are the
+ * inputs, ptrs[n_inputs] the output, all device pointers on the current
+ * device; `stream` is a cudaStream_t (NULL = the legacy default stream).
+ * Asynchronous: returns once the launches are enqueued.  Returns 0, or a
+ * nonzero code with the message available from bafe_cuda_last_error. */
+int bafe_cuda_run_device(int plan, void *const *ptrs, int n_ptrs, void *stream);
+
+/* Same as calling the plan's function: host pointers, synchronous.
+ * Returns 0 or a nonzero code. */
+int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);
+
+/* Last error raised by any entry point (including the host function
+ * pointers, which return void like the reference's kernels and so cannot
+ * report failure themselves).  Copies the message, returns the code
+ * (0 = none).  bafe_cuda_clear_error resets it. */
+int bafe_cuda_last_error(char *buf, size_t buf_size);
+void bafe_cuda_clear_error(void);
+
+/* Backend options (strings, process-wide, read when a plan is built):
+ *   "gemm_precision": "auto" (default) | "3xtf32" | "tf32" | "exact"
+ *   "device":         CUDA device ordinal used by new plans (default:
+ *                     the current device)
+ * Environment variables BAFE_GEMM_PRECISION and BAFE_DEVICE set the
+ * initial values.  Returns 0, or -1 for an unknown key or value. */
+int bafe_cuda_set_option(const char *key, const char *value);
+int bafe_cuda_get_option(const char *key, char *buf, size_t buf_size);
+
+/* Number of kernel launches the library has enqueued since load (all
+ * plans, all devices).  Used to report launch counts. */
+int64_t bafe_cuda_launch_count(void);
+
+/* sizeof() of the graph ABI structs as this library was compiled:
+ * which = 0 bafe_graph, 1 bafe_node, 2 bafe_op_attrs, 3 bafe_shape.
+ * Lets a binding check its struct mirror against the library. */
+int64_t bafe_cuda_abi_size(int which);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BAFE_CUDA_H */

@@ -1,0 +1,247 @@
+"""Golden cases: the reference's own numeric tests and the workload configs,
+with seeded inputs.  make_golden.py runs each through the reference
+(optimizer + generated C kernel) and stores the optimized graph and the
+output in <name>.npz; the tests rebuild that exact graph and feed it to the
+backend.
+
+Each case: name, cite (the reference test or config it restates), build
+(GraphBuilder -> root, using the builder's input order = the arguments'),
+inputs [(name, shape, dtype, fortran, layout, spec)], optional panel
+(rows [r0, r1) of a large problem: the reference runs the same expression
+on the row panel, whose per-row results equal the full problem's because
+matmul's summation order does not depend on M).
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+
+GOLDEN_DIR = Path(__file__).resolve().parent
+
+N01 = lambda seed, std=1.0: {"kind": "normal", "seed": seed, "std": std}
+U11 = lambda seed: {"kind": "uniform", "seed": seed}
+RINT = lambda seed: {"kind": "randint", "seed": seed, "lo": -100, "hi": 100}
+SPECIAL = lambda seed: {"kind": "special", "seed": seed}
+
+
+def _ew3(g, X, Y, Z):
+    return g.add("relu", [g.add("add", [g.add("mul", [X, Y]), Z])])
+
+
+CASES = [
+    # ---- bafe/tests/test_e2e.py -------------------------------------------
+    dict(name="e2e_matmul", cite="bafe/tests/test_e2e.py:14",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(101)), ("B", (32, 24), "float32", False, 0, N01(102))]),
+    dict(name="e2e_relu", cite="bafe/tests/test_e2e.py:26",
+         build=lambda g, X: g.add("relu", [X]),
+         inputs=[("X", (32, 32), "float32", False, 0, N01(103, 2.0))]),
+    dict(name="e2e_add", cite="bafe/tests/test_e2e.py:37",
+         build=lambda g, A, B: g.add("add", [A, B]),
+         inputs=[("A", (16, 16), "float32", False, 0, N01(104)), ("B", (16, 16), "float32", False, 0, N01(105))]),
+    dict(name="e2e_relu_matmul", cite="bafe/tests/test_e2e.py:49",
+         build=lambda g, A, B: g.add("relu", [g.add("matmul", [A, B])]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(106)), ("B", (32, 24), "float32", False, 0, N01(107))]),
+    dict(name="e2e_relu_matmul_plus_c", cite="bafe/tests/test_e2e.py:61",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(108)), ("B", (32, 24), "float32", False, 0, N01(109)),
+                 ("C", (16, 24), "float32", False, 0, N01(110))]),
+    dict(name="e2e_relu_matmul_bias", cite="bafe/tests/test_e2e.py:75",
+         build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(111)), ("B", (32, 24), "float32", False, 0, N01(112)),
+                 ("bias", (24,), "float32", False, 0, N01(113))]),
+    dict(name="e2e_matmul_bias", cite="bafe/tests/test_e2e.py:92",
+         build=lambda g, A, B, b: g.add("add", [g.add("matmul", [A, B]), b]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(114)), ("B", (32, 24), "float32", False, 0, N01(115)),
+                 ("bias", (24,), "float32", False, 0, N01(116))]),
+    dict(name="e2e_relu_sigmoid_tanh", cite="bafe/tests/test_e2e.py:196",
+         build=lambda g, X: g.add("tanh", [g.add("sigmoid", [g.add("relu", [X])])]),
+         inputs=[("X", (32, 32), "float32", False, 0, N01(117, 2.0))]),
+    dict(name="e2e_bias_add", cite="bafe/tests/test_e2e.py:207",
+         build=lambda g, X, b: g.add("bias_add", [X, b]),
+         inputs=[("X", (16, 32), "float32", False, 0, N01(118)), ("bias", (32,), "float32", False, 0, N01(119))]),
+    # ---- bafe/tests/test_layout.py ----------------------------------------
+    dict(name="layout_col_b", cite="bafe/tests/test_layout.py:214",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(120)), ("B", (32, 24), "float32", True, 1, N01(121))]),
+    dict(name="layout_both_col", cite="bafe/tests/test_layout.py:231",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (16, 32), "float32", True, 1, N01(122)), ("B", (32, 24), "float32", True, 1, N01(123))]),
+    # ---- bafe/tests/test_dtypes.py ----------------------------------------
+    dict(name="f16_matmul", cite="bafe/tests/test_dtypes.py:11",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (8, 8), "float16", False, 0, N01(124)), ("B", (8, 8), "float16", False, 0, N01(125))]),
+    dict(name="f16_relu", cite="bafe/tests/test_dtypes.py:23",
+         build=lambda g, X: g.add("relu", [X]),
+         inputs=[("X", (16, 16), "float16", False, 0, N01(126, 2.0))]),
+    dict(name="f16_matmul_relu", cite="bafe/tests/test_dtypes.py:34",
+         build=lambda g, A, B: g.add("relu", [g.add("matmul", [A, B])]),
+         inputs=[("A", (8, 8), "float16", False, 0, N01(127)), ("B", (8, 8), "float16", False, 0, N01(128))]),
+    dict(name="f16_add", cite="bafe/tests/test_dtypes.py:46",
+         build=lambda g, A, B: g.add("add", [A, B]),
+         inputs=[("A", (16, 16), "float16", False, 0, N01(129)), ("B", (16, 16), "float16", False, 0, N01(130))]),
+    dict(name="f16_matmul_bias_relu", cite="bafe/tests/test_dtypes.py:58",
+         build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+         inputs=[("A", (8, 8), "float16", False, 0, N01(131)), ("B", (8, 8), "float16", False, 0, N01(132)),
+                 ("bias", (8,), "float16", False, 0, N01(133))]),
+    dict(name="f64_matmul", cite="bafe/tests/test_dtypes.py:77",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (8, 8), "float64", False, 0, N01(134)), ("B", (8, 8), "float64", False, 0, N01(135))]),
+    dict(name="f64_relu", cite="bafe/tests/test_dtypes.py:89",
+         build=lambda g, X: g.add("relu", [X]),
+         inputs=[("X", (16, 16), "float64", False, 0, N01(136, 2.0))]),
+    dict(name="f64_sigmoid", cite="bafe/tests/test_dtypes.py:100",
+         build=lambda g, X: g.add("sigmoid", [X]),
+         inputs=[("X", (8, 8), "float64", False, 0, N01(137))]),
+    dict(name="batched_matmul_3d", cite="bafe/tests/test_dtypes.py:133",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (2, 4, 8), "float32", False, 0, N01(138)), ("B", (2, 8, 6), "float32", False, 0, N01(139))]),
+    dict(name="batched_matmul_relu_3d", cite="bafe/tests/test_dtypes.py:146",
+         build=lambda g, A, B: g.add("relu", [g.add("matmul", [A, B])]),
+         inputs=[("A", (2, 4, 8), "float32", False, 0, N01(140)), ("B", (2, 8, 6), "float32", False, 0, N01(141))]),
+    dict(name="dot_1x8_8x1", cite="bafe/tests/test_dtypes.py:158",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (1, 8), "float32", False, 0, N01(142)), ("B", (8, 1), "float32", False, 0, N01(143))]),
+    dict(name="tall_matmul", cite="bafe/tests/test_dtypes.py:172",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (64, 4), "float32", False, 0, N01(144)), ("B", (4, 64), "float32", False, 0, N01(145))]),
+    dict(name="wide_matmul", cite="bafe/tests/test_dtypes.py:185",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (4, 64), "float32", False, 0, N01(146)), ("B", (64, 4), "float32", False, 0, N01(147))]),
+    dict(name="i32_add", cite="bafe/tests/test_dtypes.py:202",
+         build=lambda g, A, B: g.add("add", [A, B]),
+         inputs=[("A", (8, 8), "int32", False, 0, RINT(148)), ("B", (8, 8), "int32", False, 0, RINT(149))]),
+    dict(name="i64_add", cite="bafe/tests/test_dtypes.py:213",
+         build=lambda g, A, B: g.add("add", [A, B]),
+         inputs=[("A", (8, 8), "int64", False, 0, RINT(150)), ("B", (8, 8), "int64", False, 0, RINT(151))]),
+    # ---- scripts/test_smoke.c (deterministic pattern) ----------------------
+    dict(name="smoke_c_pattern", cite="scripts/test_smoke.c:11-24,54-56",
+         build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+         inputs=[("A", (32, 32), "float32", False, 0, {"kind": "pattern", "mod": 7, "scale": 0.1}),
+                 ("B", (32, 32), "float32", False, 0, {"kind": "pattern", "mod": 5, "scale": 0.1}),
+                 ("bias", (32,), "float32", False, 0, {"kind": "pattern", "mod": 1 << 30, "scale": 0.01})]),
+    # ---- fused forms the extractor picks at tiny sizes ----------------------
+    dict(name="fused_matmul_relu_8", cite="bafe/src/rewrite.c:207-220, codegen.c:467-486",
+         build=lambda g, A, B: g.add("relu", [g.add("matmul", [A, B])]),
+         inputs=[("A", (8, 8), "float32", False, 0, N01(152)), ("B", (8, 8), "float32", False, 0, N01(153))]),
+    dict(name="fused_matmul_bias_relu_8", cite="bafe/src/rewrite.c:258-278, codegen.c:502-517",
+         build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+         inputs=[("A", (8, 8), "float32", False, 0, N01(154)), ("B", (8, 8), "float32", False, 0, N01(155)),
+                 ("bias", (8,), "float32", False, 0, N01(156))]),
+    # ---- transpose materialisation ------------------------------------------
+    dict(name="transpose_64x48", cite="bafe/src/codegen.c:360-369",
+         build=lambda g, X: g.add("transpose", [X], perm=[1, 0]),
+         inputs=[("X", (64, 48), "float32", False, 0, N01(157))]),
+    dict(name="transpose_then_relu", cite="bafe/src/codegen.c:360-369,338-344",
+         build=lambda g, X: g.add("relu", [g.add("transpose", [X], perm=[1, 0])]),
+         inputs=[("X", (40, 72), "float32", False, 0, N01(158))]),
+    # ---- elementwise edge values (relu of NaN/-0, inf arithmetic) -----------
+    dict(name="ew_special_values", cite="bafe/src/codegen.c:294-344",
+         build=_ew3,
+         inputs=[("X", (4096,), "float32", False, 0, SPECIAL(159)), ("Y", (4096,), "float32", False, 0, SPECIAL(160)),
+                 ("Z", (4096,), "float32", False, 0, SPECIAL(161))]),
+    # ---- workload configs -----------------------------------------------------
+    dict(name="cfg1_seed0", cite="relu(matmul(A,B)+C) 64x64x64 (configs[0])",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (64, 64), "float32", False, 0, N01(0)), ("B", (64, 64), "float32", False, 0, N01(1)),
+                 ("C", (64, 64), "float32", False, 0, N01(2))]),
+    dict(name="cfg2_row_col", cite="matmul 256^3, B Fortran order (configs[1])",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (256, 256), "float32", False, 0, N01(10)), ("B", (256, 256), "float32", True, 1, N01(11))],
+         store_inputs=False),
+    dict(name="cfg2_row_row", cite="matmul 256^3, B row-major (configs[1])",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (256, 256), "float32", False, 0, N01(10)), ("B", (256, 256), "float32", False, 0, N01(11))],
+         store_inputs=False),
+    dict(name="cfg3_panel_top", cite="relu(add(matmul(A,B), mul(C,D))) 4096^3 rows 0:8 (configs[2])",
+         build=lambda g, A, B, C, D: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), g.add("mul", [C, D])])]),
+         inputs=[("A", (4096, 4096), "float32", False, 0, N01(20)), ("B", (4096, 4096), "float32", False, 0, N01(21)),
+                 ("C", (4096, 4096), "float32", False, 0, N01(22)), ("D", (4096, 4096), "float32", False, 0, N01(23))],
+         panel=(0, 8), panel_inputs=("A", "C", "D"), store_inputs=False),
+    dict(name="cfg3_panel_bottom", cite="relu(add(matmul(A,B), mul(C,D))) 4096^3 rows 4088:4096 (configs[2])",
+         build=lambda g, A, B, C, D: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), g.add("mul", [C, D])])]),
+         inputs=[("A", (4096, 4096), "float32", False, 0, N01(20)), ("B", (4096, 4096), "float32", False, 0, N01(21)),
+                 ("C", (4096, 4096), "float32", False, 0, N01(22)), ("D", (4096, 4096), "float32", False, 0, N01(23))],
+         panel=(4088, 4096), panel_inputs=("A", "C", "D"), store_inputs=False),
+    dict(name="cfg4_chunk", cite="relu(add(mul(X,Y),Z)) U(-1,1) (configs[3]); first 2^17 of each vector",
+         build=_ew3,
+         inputs=[("X", (1 << 17,), "float32", False, 0, U11(30)), ("Y", (1 << 17,), "float32", False, 0, U11(31)),
+                 ("Z", (1 << 17,), "float32", False, 0, U11(32))],
+         store_inputs=False),
+    dict(name="cfg5_panel_top", cite="relu(matmul(A,B)+C) 16384^3, B BLOCKED, std 1/sqrt(K), rows 0:4 (configs[4])",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (16384, 16384), "float32", False, 0, N01(40, 0.0078125)),
+                 ("B", (16384, 16384), "float32", False, 2, N01(41, 0.0078125)),
+                 ("C", (16384, 16384), "float32", False, 0, N01(42, 0.0078125))],
+         panel=(0, 4), panel_inputs=("A", "C"), store_inputs=False),
+    dict(name="cfg5_panel_mid", cite="relu(matmul(A,B)+C) 16384^3, B TENSOR_CORE, rows 8190:8194 (configs[4])",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (16384, 16384), "float32", False, 0, N01(40, 0.0078125)),
+                 ("B", (16384, 16384), "float32", False, 3, N01(41, 0.0078125)),
+                 ("C", (16384, 16384), "float32", False, 0, N01(42, 0.0078125))],
+         panel=(8190, 8194), panel_inputs=("A", "C"), store_inputs=False),
+]
+
+CASE_BY_NAME = {c["name"]: c for c in CASES}
+
+
+def make_input(name_shape_spec, full: bool = True) -> np.ndarray:
+    """Materialise one input of a case from its spec (seeded)."""
+    from inputs import generate, special_values
+    name, shape, dtype, fortran, layout, spec = name_shape_spec
+    kind = spec["kind"]
+    if kind == "pattern":
+        n = int(np.prod(shape))
+        a = ((np.arange(n) % spec["mod"]).astype(np.float32) * np.float32(spec["scale"])).reshape(shape)
+        return a.astype(dtype)
+    if kind == "special":
+        return special_values(int(np.prod(shape)), spec["seed"]).reshape(shape).astype(dtype)
+    return generate(spec, shape, dtype, fortran)
+
+
+def load(name: str):
+    """-> (meta dict, {input name: array or None}, golden output)."""
+    z = np.load(GOLDEN_DIR / f"{name}.npz", allow_pickle=False)
+    meta = json.loads(str(z["meta"]))
+    ins = {k[3:]: z[k] for k in z.files if k.startswith("in_")}
+    return meta, ins, z["out"]
+
+
+def graph_from_nodes(nodes: list, input_ids: list, root: int):
+    """Rebuild a BafeGraph struct from a node list (reference-optimized graph)."""
+    import ctypes
+    from bafe_b200._binding import BafeGraph
+    from bafe_b200.graph import _OPNAME
+    g = BafeGraph()
+    ctypes.memset(ctypes.byref(g), 0, ctypes.sizeof(g))
+    for i, n in enumerate(nodes):
+        x = g.nodes[i]
+        x.id = i
+        x.op_name = _OPNAME[n["op"]]
+        x.n_children = len(n["children"])
+        for k, c in enumerate(n["children"]):
+            x.children[k] = c
+        x.shape.rank = len(n["shape"])
+        for d, v in enumerate(n["shape"]):
+            x.shape.dims[d] = v
+        x.dtype = n["dtype"]
+        x.layout = n["layout"]
+        x.is_input = n["is_input"]
+        if n["is_input"]:
+            x.input_name = n["name"].encode()
+        for f, key in (("perm", "perm"), ("axes", "axes"), ("shape", "tshape")):
+            vals = n.get(key, [])
+            setattr(x.attrs, "n_" + f, len(vals))
+            for k, v in enumerate(vals):
+                getattr(x.attrs, f)[k] = v
+        x.attrs.keepdims = n.get("keepdims", False)
+        x.attrs.name = n.get("attr_name", n["name"] if n["is_input"] else "").encode()
+    g.n_nodes = len(nodes)
+    for k, i in enumerate(input_ids):
+        g.inputs[k] = i
+    g.n_inputs = len(input_ids)
+    g.outputs[0] = root
+    g.n_outputs = 1
+    return g

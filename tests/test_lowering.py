@@ -1,0 +1,141 @@
+"""Host-side lowering: which kernels a graph becomes, compile of every
+generated module (NVRTC, sm_100a) and the JIT-cache contract.  CPU only:
+plans are built and compiled without a GPU."""
+import numpy as np
+import pytest
+
+import bafe_b200 as bafe
+import cases
+from conftest import gpu_available
+from bafe_b200.graph import GraphBuilder
+
+
+def _kernel(build, *inputs):
+    g = GraphBuilder()
+    ids = [g.add_input(n, s, dt, lay) for (n, s, dt, lay) in inputs]
+    g.set_output(build(g, *ids))
+    return bafe.compile_graph(g)
+
+
+def test_cfg1_is_one_fused_gemm():
+    k = _kernel(lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+                ("A", (64, 64), 0, 0), ("B", (64, 64), 0, 0), ("C", (64, 64), 0, 0))
+    steps = k.describe().strip().splitlines()
+    assert len(steps) == 1
+    assert steps[0].startswith("gemm.") and "epi=relu(add(acc,C))" in steps[0] and steps[0].endswith("-> out")
+
+
+def test_cfg3_epilogue_holds_the_product():
+    k = _kernel(lambda g, A, B, C, D: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), g.add("mul", [C, D])])]),
+                ("A", (128, 64), 0, 0), ("B", (64, 96), 0, 0), ("C", (128, 96), 0, 0), ("D", (128, 96), 0, 0))
+    steps = k.describe().strip().splitlines()
+    assert len(steps) == 1 and "epi=relu(add(acc,mul(C,D)))" in steps[0]
+
+
+def test_cfg4_is_one_streaming_kernel():
+    k = _kernel(lambda g, X, Y, Z: g.add("relu", [g.add("add", [g.add("mul", [X, Y]), Z])]),
+                ("X", (1 << 12,), 0, 0), ("Y", (1 << 12,), 0, 0), ("Z", (1 << 12,), 0, 0))
+    steps = k.describe().strip().splitlines()
+    assert steps == ["ew n=4096 float relu(add(mul(X,Y),Z)) -> out"]
+
+
+def test_bias_epilogue_reads_row_vector():
+    k = _kernel(lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+                ("A", (64, 32), 0, 0), ("B", (32, 48), 0, 0), ("b", (48,), 0, 0))
+    assert "epi=relu(add(acc,b[j]))" in k.describe()
+
+
+def test_transpose_materialisation_and_consumer():
+    k = _kernel(lambda g, X: g.add("relu", [g.add("transpose", [X], perm=[1, 0])]), ("X", (40, 72), 0, 0))
+    steps = k.describe().strip().splitlines()
+    assert steps[0].startswith("transpose2d m=72 n=40") and steps[1].startswith("ew n=2880")
+
+
+def test_shared_matmul_is_materialised():
+    """A product read twice is computed once into a temporary."""
+    k = _kernel(lambda g, A, B: (lambda m: g.add("add", [g.add("relu", [m]), g.add("neg", [m])]))(g.add("matmul", [A, B])),
+                ("A", (32, 32), 0, 0), ("B", (32, 32), 0, 0))
+    steps = k.describe().strip().splitlines()
+    assert steps[0].startswith("gemm.") and "-> tmp0" in steps[0]
+    assert steps[1].startswith("ew ") and steps[1].endswith("-> out")
+
+
+def test_unsupported_broadcast_is_an_error():
+    g = GraphBuilder()
+    a = g.add_input("A", (4, 8), 0, 0)
+    b = g.add_input("B", (1, 8), 0, 0)
+    g.set_output(g.add("add", [a, b]))
+    with pytest.raises(RuntimeError, match="unsupported broadcast"):
+        bafe.compile_graph(g)
+    assert bafe.jit_stats()["compile_failures"] == 1
+
+
+def test_unknown_op_zero_fills_like_the_emitter():
+    g = GraphBuilder()
+    a = g.add_input("A", (4, 8), 0, 0)
+    b = g.add_input("s", (1,), 0, 0)
+    g.set_output(g.add("scale", [a, b]))
+    k = bafe.compile_graph(g)
+    assert "zero-fill" in k.describe()
+
+
+def test_jit_cache_contract():
+    """Same graph -> memory hit; jit_clear -> disk hit; stats like jit.c."""
+    build = lambda g, X: g.add("relu", [X])
+    k1 = _kernel(build, ("X", (32, 32), 0, 0))
+    k2 = _kernel(build, ("X", (32, 32), 0, 0))
+    assert k1.fn_ptr == k2.fn_ptr and k1.plan == k2.plan
+    s = bafe.jit_stats()
+    assert s["misses"] == 1 and s["hits"] >= 1
+    bafe.jit_clear()
+    _kernel(build, ("X", (32, 32), 0, 0))
+    s = bafe.jit_stats()
+    assert s == {"hits": 1, "misses": 1, "compiles": 0, "compile_failures": 0}   # cubin came from disk
+    _kernel(build, ("X", (32, 33), 0, 0))
+    assert bafe.jit_stats()["misses"] == 2
+
+
+def test_precision_option_changes_the_plan():
+    build = lambda g, A, B: g.add("matmul", [A, B])
+    bafe.set_option("gemm_precision", "exact")
+    k = _kernel(build, ("A", (256, 256), 0, 0), ("B", (256, 256), 0, 0))
+    assert k.describe().startswith("gemm.exact")
+
+
+def test_stale_function_reports_an_error():
+    k = _kernel(lambda g, X: g.add("relu", [X]), ("X", (8,), 0, 0))
+    bafe.jit_clear()
+    x = np.ones(8, np.float32)
+    with pytest.raises(RuntimeError, match="stale kernel function"):
+        k(x)
+
+
+@pytest.mark.skipif(gpu_available(), reason="checks the no-device error path")
+def test_no_device_fails_loudly():
+    k = _kernel(lambda g, X: g.add("relu", [X]), ("X", (8,), 0, 0))
+    with pytest.raises(RuntimeError, match="no CUDA device"):
+        k(np.ones(8, np.float32))
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES])
+def test_every_golden_graph_lowers_and_compiles(name):
+    """The reference-optimized graph of every golden case lowers and its
+    generated module compiles for sm_100a (NVRTC) -- no GPU needed."""
+    meta, _, _ = cases.load(name)
+    g = cases.graph_from_nodes(meta["nodes"], meta["input_ids"], meta["root"])
+    for prec in ("exact", "auto"):
+        bafe.set_option("gemm_precision", prec)
+
+        class B:  # minimal builder facade for compile_graph
+            graph = g
+            output = meta["root"]
+
+            @staticmethod
+            def shape(i):
+                return tuple(meta["nodes"][i]["shape"])
+
+            @staticmethod
+            def dtype(i):
+                return meta["nodes"][i]["dtype"]
+        k = bafe.compile_graph(B)
+        assert k.describe()
