@@ -91,6 +91,12 @@ def launch_count() -> int:
     return int(lib.bafe_cuda_launch_count())
 
 
+def synchronize() -> None:
+    """Wait for the current device; raise if a kernel reported an error
+    (e.g. a tensor-core pipeline wait that ran past its deadline)."""
+    check(lib.bafe_cuda_synchronize(), "synchronize")
+
+
 class Kernel:
     """A compiled plan: the host function BAFE's ABI returns, plus device entry."""
 
@@ -354,5 +360,5 @@ __all__ = [
     "Tensor", "jit", "input", "matmul", "add", "sub", "mul", "relu", "sigmoid", "tanh", "neg", "bias_add",
     "transpose", "reduce_sum", "reduce_max", "reshape", "broadcast_to", "GraphBuilder", "compile_graph",
     "Kernel", "set_option", "get_option", "jit_stats", "jit_clear", "jit_invalidate_memory_cache",
-    "set_cache_dir", "cache_dir", "graph_hash", "launch_count", "last_error",
+    "set_cache_dir", "cache_dir", "graph_hash", "launch_count", "last_error", "synchronize",
 ]

@@ -327,3 +327,8 @@ BAFE_API int64_t bafe_cuda_abi_size(int which) {
     }
     return -1;
 }
+
+BAFE_API int bafe_cuda_synchronize(void) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    return synchronize_current_device();
+}

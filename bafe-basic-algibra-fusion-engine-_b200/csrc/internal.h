@@ -106,6 +106,7 @@ struct Step {
     int n_epi = 0;                 // epilogue operands are srcs[2..2+n_epi)
     bool direct = false;           // fused-form summation order (one chunk)
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
+    std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
     // Transpose2d (output M x N), Gather, Reduce
     int64_t gdims[8] = {0}, gstride[8] = {0};
     int grank = 0;
@@ -154,6 +155,8 @@ std::string sha256_hex(const void* data, size_t len);
 // Runtime (runtime.cpp).
 int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
 int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs);
+// Synchronises the current device and reports a kernel-raised error word.
+int synchronize_current_device();
 void release_plan_device_state(Plan& p);
 
 // Error slot shared by every entry point.

@@ -1,21 +1,426 @@
-// gemm_tc.cuh -- tensor-core (tcgen05) GEMM with a generated epilogue.
+// gemm_tc.cuh -- tcgen05 tensor-core GEMM (sm_100a) with a generated
+// elementwise epilogue: out = epi(A . B), fp32 in/out.
+//
+// Structure (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0        TMA producer: k-blocks of A and B (and, for 3xTF32, of
+//                 their residuals A_lo, B_lo) into a STAGES-deep ring of
+//                 swizzled shared-memory stages.  No multicast.
+//   warp 1        allocates TMEM; one lane issues tcgen05.mma (kind::tf32,
+//                 M=128, N=256, K=8 per instruction).  The K loop is cut
+//                 into chunks (KC = 128 for 1xTF32, 64 for 3xTF32); each
+//                 chunk accumulates into one of two TMEM buffers, starting
+//                 from zero.
+//   warps 2-9     accumulate: each thread owns one tile row (TMEM lane) and
+//                 128 columns; after every chunk it tcgen05.ld's the chunk
+//                 partial sums and adds them into 128 fp32 registers with
+//                 round-to-nearest, then releases the TMEM buffer to the
+//                 MMA warp.  After the last chunk it applies the generated
+//                 epilogue (Spec::apply: relu(acc + C), ...) and stores.
+//
+// Why chunks: the tensor core's fp32 accumulator truncates at every
+// accumulation step, which biases long sums (measured: the 3xTF32 error
+// grew like K^1.5 with a single TMEM accumulator, 1.1e-2 at K=4096).
+// Summing short partial sums in registers with round-to-nearest keeps the
+// error a random walk over chunks (~KC * K^0.5), inside the 3xTF32 bound.
+//
+// kind::tf32 reads the top 19 bits of each fp32 operand (the low 13
+// mantissa bits are ignored), so for 3xTF32 the raw operand is its own
+// "hi" part; a streaming pre-pass (bafe::tf32_residual) writes
+// lo = x - trunc_tf32(x), and each k-step issues
+//     A.B += A.B + A.B_lo + A_lo.B        (three MMAs, all on the tensor core)
+//
+// Operand layouts (BAFE layout tags): A row-major = K-major, A col-major =
+// M-major; B col-major = K-major, B row-major = N-major.  K-major tiles are
+// loaded as one [rows x 32] box (128 B per row, 128B swizzle); MN-major
+// tiles as 32-wide boxes [k 32 x mn 32] side by side, written by TMA with
+// the 128B-swizzle-32B-atom mode that MN-major tf32 UMMA operands require.
+//
+// Every wait is bounded by a wall-clock deadline (globaltimer): a role that
+// times out raises the CTA's abort flag and the caller-visible error word,
+// every role then leaves its loop, in-flight TMA copies and MMAs are drained
+// (bounded again), TMEM is freed and the kernel returns.
 #pragma once
 #include "bafe_dev.cuh"
 
-#define BAFE_TC_THREADS 256
-
 namespace bafe {
 
+struct __align__(64) TmaDesc { unsigned long long v[16]; };   // CUtensorMap
+
 struct TcArgs {
-    const void* a;
-    const void* b;
+    TmaDesc tmap_a;
+    TmaDesc tmap_b;
+    TmaDesc tmap_a_lo;             // 3xTF32 residuals (same layouts as A, B)
+    TmaDesc tmap_b_lo;
     void* out;
     i64 M, N, K;
     i64 o_bstride;
     const void* ep[8];
+    unsigned* err;                 // error word (0 = ok); set on timeout
+    int a_mn, b_mn;                // operand is MN-major
+    int num_m, num_n, num_tiles;
+    int group_m;                   // rasterisation group along M
+    unsigned long long timeout_ns; // per-wait deadline
 };
 
+template <int VARIANT> struct TcCfg;
+// KB_PER_CHUNK k-blocks (of 32) per TMEM partial sum: the 3xTF32 variant,
+// whose accuracy bound is tight, promotes twice as often.
+template <> struct TcCfg<1> {      // 1xTF32
+    static constexpr int BN = 256, STAGES = 4, THREADS = 320, KB_PER_CHUNK = 4;
+};
+template <> struct TcCfg<3> {      // 3xTF32
+    static constexpr int BN = 256, STAGES = 2, THREADS = 320, KB_PER_CHUNK = 2;
+};
+
+// Residual of the tf32 truncation: x - (x with the low 13 mantissa bits
+// cleared), exact in fp32; 0 for inf / NaN (whose hi part carries them).
+__device__ __forceinline__ float tf32_lo(float x) {
+    const u32 bits = __float_as_uint(x);
+    if ((bits & 0x7F800000u) == 0x7F800000u) return 0.0f;
+    return __fsub_rn(x, __uint_as_float(bits & 0xFFFFE000u));
+}
+
+namespace tc {
+
+constexpr int BM = 128, BK = 32;
+
+__device__ __forceinline__ u32 smem_u32(const void* p) {
+    return static_cast<u32>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ u64 now_ns() {
+    u64 t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(u32 bar, u32 count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ bool mbar_try(u32 bar, u32 parity) {
+    u32 ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void mbar_arrive(u32 bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(u32 bar, u32 bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(u32 dst, const TmaDesc* map, u32 bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(u32 bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma_tf32(u32 tmem_d, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
+          "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
+}
+// 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets row
+// (lane base + t), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// UMMA shared-memory descriptor, version 1; lbo / sbo in bytes.
+// K-major operands use the 128B swizzle (layout type 2): 8-row groups
+// (SBO = 1024 B), K advances inside the 128-byte row.  MN-major tf32
+// operands must use the 128B swizzle with 32-byte atoms (layout type 1,
+// "128B_BASE32B"): 32 elements along MN per 128-byte row, 4-row K groups
+// (SBO = 512 B), MN atoms LBO apart.
+__device__ __forceinline__ u64 smem_desc(u32 addr, u32 lbo, u32 sbo, u32 layout) {
+    u64 d = 0;
+    d |= (u64)((addr >> 4) & 0x3FFFu);
+    d |= (u64)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (u64)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (u64)1 << 46;
+    d |= (u64)(layout & 7u) << 61;
+    return d;
+}
+
+// Instruction descriptor: D f32, A/B tf32, majors, N, M=128.
+__device__ __forceinline__ u32 instr_desc(int a_mn, int b_mn, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((u32)a_mn << 15) | ((u32)b_mn << 16) |
+           ((u32)(n >> 3) << 17) | ((u32)(BM >> 4) << 24);
+}
+
+// Shared state of one CTA.
+struct Shared {
+    u32 abort;
+    u32 tmem_base;
+};
+
+// Bounded wait on an mbarrier phase; returns false (and raises the abort
+// flag / error word) on timeout or when another role has aborted.
+__device__ __forceinline__ bool wait(u32 bar, u32 parity, volatile Shared* sh, const TcArgs& g, u32 code) {
+    if (mbar_try(bar, parity)) return true;
+    const u64 t0 = now_ns();
+    while (true) {
+        if (mbar_try(bar, parity)) return true;
+        if (sh->abort) return false;
+        if (now_ns() - t0 > g.timeout_ns) {
+            sh->abort = 1u;
+            atomicCAS(g.err, 0u, code);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int& nb) {
+    const int per_group = g.group_m * g.num_n;
+    const int group = t / per_group;
+    const int first_m = group * g.group_m;
+    int gsize = g.num_m - first_m;
+    if (gsize > g.group_m) gsize = g.group_m;
+    const int local = t - group * per_group;
+    mb = first_m + local % gsize;
+    nb = local / gsize;
+}
+
+}  // namespace tc
+
 template <class Spec, int VARIANT>
-__device__ __forceinline__ void gemm_tc(const TcArgs& g) {}
+__device__ __forceinline__ void gemm_tc(const TcArgs& g) {
+    using namespace tc;
+    typedef TcCfg<VARIANT> Cfg;
+    constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES;
+    constexpr bool SPLIT = VARIANT == 3;
+    constexpr int KB_PER_CHUNK = Cfg::KB_PER_CHUNK;
+    constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB
+    constexpr u32 B_BYTES = BN * BK * 4;            // 32 KB
+    constexpr u32 STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
+    constexpr u32 TMEM_COLS = 2 * BN;
+    constexpr int ACC_THREADS = 256;
+
+    extern __shared__ unsigned char smem_raw[];
+    // 1024-byte aligned stage ring (the swizzle pattern is address based)
+    const u32 raw_addr = smem_u32(smem_raw);
+    const u32 base = (raw_addr + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw_addr);
+    const u32 bars = base + STAGES * STAGE_BYTES;   // mbarriers follow the ring
+    // barrier layout: full[S], empty[S], tfull[2], tempty[2], drain
+    auto FULL = [&](int s) { return bars + 8u * s; };
+    auto EMPTY = [&](int s) { return bars + 8u * (STAGES + s); };
+    auto TFULL = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+    auto TEMPTY = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+    const u32 DRAIN = bars + 8u * (2 * STAGES + 4);
+    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(FULL(s), 1);
+            mbar_init(EMPTY(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(TFULL(b), 1);
+            mbar_init(TEMPTY(b), ACC_THREADS);
+        }
+        mbar_init(DRAIN, 1);
+        sh->abort = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32((const void*)&sh->tmem_base)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const u32 tmem = sh->tmem_base;
+    const int k_blocks = (int)((g.K + BK - 1) / BK);
+    const int n_chunks = (k_blocks + KB_PER_CHUNK - 1) / KB_PER_CHUNK;
+
+    if (warp == 0) {
+        // ------------------------------------------------ TMA producer --
+        if (lane == 0) {
+            int s = 0;
+            u32 phase = 0;
+            u32 armed[STAGES];
+            for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+                int mb, nb;
+                tile_coords(g, t, mb, nb);
+                const int m0 = mb * BM, n0 = nb * BN;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
+                    const u32 a_dst = base + s * STAGE_BYTES;
+                    const u32 b_dst = a_dst + A_BYTES;
+                    mbar_expect_tx(FULL(s), STAGE_BYTES);
+                    armed[s] = phase;
+                    const int k0 = kb * BK;
+#pragma unroll
+                    for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
+                        const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
+                        const TmaDesc* mbp = part ? &g.tmap_b_lo : &g.tmap_b;
+                        const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
+                        const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
+                        if (g.a_mn) {
+                            for (int j = 0; j < BM / 32; ++j)
+                                tma_load_2d(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                        } else {
+                            tma_load_2d(ad, ma, FULL(s), k0, m0);
+                        }
+                        if (g.b_mn) {
+                            for (int j = 0; j < BN / 32; ++j)
+                                tma_load_2d(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                        } else {
+                            tma_load_2d(bd, mbp, FULL(s), k0, n0);
+                        }
+                    }
+                    if (++s == STAGES) { s = 0; phase ^= 1u; }
+                }
+            }
+            // Drain: wait for every copy this thread issued (bounded).
+            for (int i = 0; i < STAGES; ++i) {
+                if (armed[i] == 0xFFFFFFFFu) continue;
+                const u64 t0 = now_ns();
+                while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < g.timeout_ns) {}
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------- MMA issuer --
+        if (lane == 0) {
+            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN);
+            const u32 a_lbo = g.a_mn ? 32u * BK * 4u : 16u, b_lbo = g.b_mn ? 32u * BK * 4u : 16u;
+            const u32 a_sbo = g.a_mn ? 512u : 1024u, b_sbo = g.b_mn ? 512u : 1024u;
+            const u32 a_lt = g.a_mn ? 1u : 2u, b_lt = g.b_mn ? 1u : 2u;
+            int s = 0;
+            u32 phase = 0;
+            u32 chunk = 0;                              // chunks issued by this CTA
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+                for (int c = 0; ok && c < n_chunks; ++c, ++chunk) {
+                    const int buf = (int)(chunk & 1u);
+                    const u32 use = (chunk >> 1) & 1u;
+                    if (!wait(TEMPTY(buf), use ^ 1u, sh, g, 2u)) { ok = false; break; }
+                    tc_fence_after();
+                    const u32 d = tmem + (u32)(buf * BN);
+                    const int kb_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                    for (int kb = c * KB_PER_CHUNK; kb < kb_end; ++kb) {
+                        if (!wait(FULL(s), phase, sh, g, 3u)) { ok = false; break; }
+                        tc_fence_after();
+                        const u32 a_hi = base + s * STAGE_BYTES;
+                        const u32 b_hi = a_hi + A_BYTES;
+                        const u32 a_lo = a_hi + A_BYTES + B_BYTES;
+                        const u32 b_lo = a_lo + A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            // K-major: 8 tf32 = 32 B further along the row;
+                            // MN-major: the next 8 k-rows (1024 B).
+                            const u32 ao = g.a_mn ? kk * 1024u : kk * 32u;
+                            const u32 bo = g.b_mn ? kk * 1024u : kk * 32u;
+                            const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
+                            const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
+                            const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                            tc_mma_tf32(d, ah, bh, idesc, acc);
+                            if (SPLIT) {
+                                const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
+                                const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
+                                tc_mma_tf32(d, ah, bl, idesc, 1u);
+                                tc_mma_tf32(d, al, bh, idesc, 1u);
+                            }
+                        }
+                        tc_commit(EMPTY(s));           // stage free once these MMAs finish
+                        if (++s == STAGES) { s = 0; phase ^= 1u; }
+                    }
+                    if (!ok) break;
+                    tc_commit(TFULL(buf));             // chunk partial sums ready
+                }
+            }
+            // Drain outstanding MMAs before TMEM is released (bounded).
+            tc_commit(DRAIN);
+            const u64 t0 = now_ns();
+            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < g.timeout_ns) {}
+        }
+    } else {
+        // ------------------------------------ accumulate + epilogue --
+        const int q = warp & 3;                        // TMEM lane quadrant
+        const int half = (warp - 2) >> 2;              // column half of the tile
+        const int row_in_tile = q * 32 + lane;
+        const u32 lane_addr = (u32)(q * 32) << 16;
+        typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
+        u32 chunk = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+            float acc[128];
+#pragma unroll
+            for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
+            for (int c = 0; c < n_chunks; ++c, ++chunk) {
+                const int buf = (int)(chunk & 1u);
+                const u32 use = (chunk >> 1) & 1u;
+                // warp-uniform: tcgen05.ld below needs all 32 lanes converged
+                const bool ready = wait(TFULL(buf), use, sh, g, 4u);
+                if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    u32 r[32];
+                    tmem_ld32(tmem + lane_addr + (u32)(buf * BN + half * 128 + 32 * j), r);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) acc[32 * j + e] = __fadd_rn(acc[32 * j + e], __uint_as_float(r[e]));
+                }
+                tc_fence_before();
+                mbar_arrive(TEMPTY(buf));
+            }
+            if (!ok) break;
+            int mb, nb;
+            tile_coords(g, t, mb, nb);
+            const i64 i = (i64)mb * BM + row_in_tile;
+            const i64 n0 = (i64)nb * BN + half * 128;
+            if (i < g.M) {
+#pragma unroll
+                for (int v = 0; v < 128; v += 4) {
+                    const i64 j = n0 + v;
+                    if (j < g.N) {
+                        Vec4<typename Spec::Out> o;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, 0, i, j + e);
+                        st4(out + i * g.N + j, o);
+                    }
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------- teardown --
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
 
 }  // namespace bafe

@@ -23,10 +23,10 @@ struct CheckSpec {
 extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
     bafe::gemm_exact<CheckSpec, false>(g);
 }
-extern "C" __global__ void __launch_bounds__(BAFE_TC_THREADS, 1) check_gemm_tc3(const __grid_constant__ bafe::TcArgs g) {
+extern "C" __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1) check_gemm_tc3(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc<CheckSpec, 3>(g);
 }
-extern "C" __global__ void __launch_bounds__(BAFE_TC_THREADS, 1) check_gemm_tc1(const __grid_constant__ bafe::TcArgs g) {
+extern "C" __global__ void __launch_bounds__(bafe::TcCfg<1>::THREADS, 1) check_gemm_tc1(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc<CheckSpec, 1>(g);
 }
 extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {

@@ -597,14 +597,20 @@ struct Lowerer {
         src << "    return " << store_convert(out_store, rv_dtype, rv) << ";\n  }\n};\n";
         for (auto& l : leaves) s.srcs.push_back(buf[l.node]);
         s.n_epi = (int)leaves.size();
+        if (s.kind == StepKind::GemmTc && s.tc_variant == 3) {
+            // 3xTF32 residual operands lo = x - trunc_tf32(x), written once
+            // per call by a streaming pre-pass into plan scratch.
+            s.aux.push_back(emit_residual(s.srcs[0], M * K * a_items, "A"));
+            s.aux.push_back(emit_residual(s.srcs[1], K * Nn * b_items, "B"));
+        }
         if (s.kind == StepKind::GemmExact) {
             src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel
                 << "(const bafe::GemmArgs g) { bafe::gemm_exact<" << S_ << ", " << (s.direct ? "true" : "false")
                 << ">(g); }\n";
         } else {
-            src << "extern \"C\" __global__ void __launch_bounds__(BAFE_TC_THREADS, 1) " << s.kernel
-                << "(const __grid_constant__ bafe::TcArgs g) { bafe::gemm_tc<" << S_ << ", " << s.tc_variant
-                << ">(g); }\n";
+            src << "extern \"C\" __global__ void __launch_bounds__(bafe::TcCfg<" << s.tc_variant << ">::THREADS, 1) "
+                << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::gemm_tc<" << S_ << ", "
+                << s.tc_variant << ">(g); }\n";
         }
         char geo[256];
         snprintf(geo, sizeof(geo), " batch=%lld m=%lld n=%lld k=%lld a=%s b=%s", (long long)batch, (long long)M,
@@ -629,6 +635,38 @@ struct Lowerer {
         return true;
     }
     static bool tc_available();
+
+    // Streaming pre-pass writing the tf32 residual of an f32 buffer.
+    BufRef emit_residual(const BufRef& from, int64_t n, const char* what) {
+        Step s;
+        s.kind = StepKind::Ew;
+        s.n = n;
+        s.ncols = 1;
+        s.dst = new_tmp(n * 4);
+        s.dst_esize = 4;
+        s.dst_bytes = n * 4;
+        s.srcs.push_back(from);
+        s.src_esize.push_back(4);
+        s.src_row.push_back(false);
+        s.kernel = kname("tf32_residual");
+        s.kernel_vec = s.kernel + "_v4";
+        src << "\nstruct P_" << s.kernel << " { const float* __restrict__ in0; float* __restrict__ out; i64 n; i64 ncols; };\n"
+            << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const P_" << s.kernel << " p) {\n"
+            << "  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += (i64)gridDim.x * blockDim.x)\n"
+            << "    p.out[i] = bafe::tf32_lo(p.in0[i]);\n}\n"
+            << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel_vec << "(const P_" << s.kernel << " p) {\n"
+            << "  const i64 ng = p.n >> 2;\n"
+            << "  for (i64 g = (i64)blockIdx.x * blockDim.x + threadIdx.x; g < ng; g += (i64)gridDim.x * blockDim.x) {\n"
+            << "    const auto v = bafe::ld4(p.in0 + 4 * g);\n    bafe::Vec4<float> r;\n"
+            << "#pragma unroll\n    for (int l = 0; l < 4; ++l) r.v[l] = bafe::tf32_lo(v.v[l]);\n"
+            << "    bafe::st4(p.out + 4 * g, r);\n  }\n"
+            << "  const i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x;\n"
+            << "  if (t < 4 && (ng << 2) + t < p.n) p.out[(ng << 2) + t] = bafe::tf32_lo(p.in0[(ng << 2) + t]);\n}\n";
+        s.describe = std::string("ew n=") + std::to_string((long long)n) + " float tf32_residual(" + what + ") -> " +
+                     bufname(s.dst);
+        P.steps.push_back(s);
+        return s.dst;
+    }
 
     // Converts a half-precision buffer to f32 for steps that read compute
     // types only (transpose, gather, reduce).

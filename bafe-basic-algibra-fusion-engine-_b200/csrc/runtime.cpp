@@ -237,7 +237,7 @@ int sm_count(int dev) {
 
 // Driver calls used by the tensor-core launcher (tc_launch.cpp).
 int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
-                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle128, std::string& err) {
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err) {
     Driver& d = driver();
     if (!d.ok) { err = d.why; return 4; }
     cuuint64_t gd[5], gs[4];
@@ -247,7 +247,9 @@ int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, con
     CUresult r = d.tensorMapEncodeTiled(
         reinterpret_cast<CUtensorMap*>(map), dtype_is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
         (cuuint32_t)rank, gaddr, gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        swizzle == 2 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                     : (swizzle == 1 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE),
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) { err = "cuTensorMapEncodeTiled: " + cu_err(r); return 4; }
     return 0;
@@ -264,6 +266,22 @@ struct DeviceState {
     void* out_stage = nullptr;
     cudaStream_t stream = nullptr;
 };
+
+// One device word per GPU that kernels with bounded waits report a timeout
+// into (0 = ok).  Allocated on first use of the device.
+namespace {
+unsigned* g_err_word[64] = {nullptr};
+}
+unsigned* device_error_word(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    if (!g_err_word[dev]) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, 4) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        cudaMemset(p, 0, 4);
+        g_err_word[dev] = static_cast<unsigned*>(p);
+    }
+    return g_err_word[dev];
+}
 
 namespace {
 
@@ -448,9 +466,14 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
             case StepKind::GemmTc: {
                 std::vector<const void*> ep;
                 for (int k = 0; k < s.n_epi; ++k) ep.push_back(ptr_of(s.srcs[2 + k]));
+                unsigned* err_word = device_error_word(dev);
+                if (!err_word) { set_error(6, "cannot allocate the device error word"); return 6; }
                 TcLaunch L;
                 std::string err;
-                if (int rc = tc_prepare(s, ptr_of(s.srcs[0]), ptr_of(s.srcs[1]), dst, ep, sm_count(dev), L, err)) {
+                const void* a_lo = s.aux.size() > 0 ? ptr_of(s.aux[0]) : nullptr;
+                const void* b_lo = s.aux.size() > 1 ? ptr_of(s.aux[1]) : nullptr;
+                if (int rc = tc_prepare(s, ptr_of(s.srcs[0]), ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev),
+                                        err_word, L, err)) {
                     set_error(rc, err);
                     return rc;
                 }
@@ -503,6 +526,39 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
         }
     }
     return 0;
+}
+
+// A kernel whose bounded wait expired wrote a nonzero code into the
+// device's error word: report it (the output is not valid) and reset it.
+// The caller has synchronised the work in question.
+int check_device_error_word(int dev) {
+    if (dev < 0 || dev >= 64 || !g_err_word[dev]) return 0;
+    unsigned code = 0;
+    if (cudaMemcpy(&code, g_err_word[dev], 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    if (!code) return 0;
+    cudaMemset(g_err_word[dev], 0, 4);
+    set_error(13, "tensor-core GEMM timed out waiting on a pipeline barrier (role code " + std::to_string(code) +
+                      "); the output is invalid");
+    return 13;
+}
+
+int synchronize_current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, "no CUDA device available");
+        return 4;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(9, std::string("device error: ") + cudaGetErrorString(e));
+        return 9;
+    }
+    return check_device_error_word(dev);
 }
 
 int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
@@ -559,7 +615,7 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
         set_error(9, std::string("device error: ") + cudaGetErrorString(e));
         return 9;
     }
-    return 0;
+    return check_device_error_word(ds->device);
 }
 
 void release_plan_device_state(Plan& p) {

@@ -1,14 +1,129 @@
-// tc_launch.cpp -- host side of the tensor-core GEMM.
+// tc_launch.cpp -- host side of the tensor-core GEMM (kernels/gemm_tc.cuh):
+// TMA tensor maps for the operand layouts, the by-value argument block,
+// persistent grid size.
 #include "tc_launch.h"
+
+#include <cuda.h>
+
+#include <cstdlib>
+#include <cstring>
 
 namespace bafe_cuda {
 
-bool tc_kernel_enabled() { return false; }
-int tc_smem_bytes(int) { return 0; }
-int tc_prepare(const Step&, const void*, const void*, void*, const std::vector<const void*>&, int, TcLaunch&,
+namespace {
+
+constexpr int BM = 128, BK = 32, BN = 256;
+
+// Mirror of bafe::TcArgs (kernels/gemm_tc.cuh); field order and types must match.
+struct alignas(64) TcArgsHost {
+    CUtensorMap tmap_a;
+    CUtensorMap tmap_b;
+    CUtensorMap tmap_a_lo;
+    CUtensorMap tmap_b_lo;
+    void* out;
+    int64_t M, N, K;
+    int64_t o_bstride;
+    const void* ep[8];
+    unsigned* err;
+    int32_t a_mn, b_mn;
+    int32_t num_m, num_n, num_tiles;
+    int32_t group_m;
+    unsigned long long timeout_ns;
+};
+static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
+static_assert(sizeof(TcArgsHost) == 704, "TcArgs layout");
+static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the launch block");
+
+int threads_of(int) { return 320; }
+int stages_of(int variant) { return variant == 3 ? 2 : 4; }
+int stage_bytes(int variant) { return (BM * BK * 4 + BN * BK * 4) * (variant == 3 ? 2 : 1); }
+
+}  // namespace
+
+bool tc_kernel_enabled() {
+    const char* e = getenv("BAFE_DISABLE_TC");
+    return !(e && *e && *e != '0');
+}
+
+int tc_smem_bytes(int variant) {
+    // alignment slack + stage ring + mbarriers + shared words
+    return 1024 + stages_of(variant) * stage_bytes(variant) + 256;
+}
+
+int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
+               const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,
                std::string& err) {
-    err = "tensor-core GEMM not available";
-    return 11;
+    const bool split = s.tc_variant == 3;
+    if (split && (!a_lo || !b_lo)) {
+        err = "tensor-core GEMM: 3xTF32 needs the residual operands";
+        return 12;
+    }
+    if (((uintptr_t)a | (uintptr_t)b | (uintptr_t)a_lo | (uintptr_t)b_lo) % 16) {
+        err = "tensor-core GEMM: A and B must be 16-byte aligned (TMA)";
+        return 12;
+    }
+    if ((uintptr_t)out % 16) {
+        err = "tensor-core GEMM: the output must be 16-byte aligned";
+        return 12;
+    }
+    TcArgsHost h;
+    memset(&h, 0, sizeof(h));
+    const uint64_t M = (uint64_t)s.M, N = (uint64_t)s.N, K = (uint64_t)s.K;
+    // A: row-major = K-major (box 32 k x 128 rows, 128B swizzle); col-major =
+    // M-major (stored [K][M]; boxes of 32 m x 32 k, 128B swizzle, 32B atoms).
+    auto map_a = [&](CUtensorMap* m, const void* p) {
+        if (s.a_col) {
+            uint64_t dims[2] = {M, K}, strides[1] = {M * 4};
+            uint32_t box[2] = {32, 32};
+            return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 2, err);
+        }
+        uint64_t dims[2] = {K, M}, strides[1] = {K * 4};
+        uint32_t box[2] = {32, (uint32_t)BM};
+        return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 1, err);
+    };
+    // B: col-major = K-major (stored [N][K]; box 32 k x 256 cols);
+    // row-major = N-major (stored [K][N]; boxes of 32 n x 32 k, 32B atoms).
+    auto map_b = [&](CUtensorMap* m, const void* p) {
+        if (s.b_col) {
+            uint64_t dims[2] = {K, N}, strides[1] = {K * 4};
+            uint32_t box[2] = {32, (uint32_t)BN};
+            return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 1, err);
+        }
+        uint64_t dims[2] = {N, K}, strides[1] = {N * 4};
+        uint32_t box[2] = {32, 32};
+        return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 2, err);
+    };
+    if (int rc = map_a(&h.tmap_a, a)) return rc;
+    if (int rc = map_b(&h.tmap_b, b)) return rc;
+    if (split) {
+        if (int rc = map_a(&h.tmap_a_lo, a_lo)) return rc;
+        if (int rc = map_b(&h.tmap_b_lo, b_lo)) return rc;
+    }
+    h.out = out;
+    h.M = s.M;
+    h.N = s.N;
+    h.K = s.K;
+    h.o_bstride = s.M * s.N;
+    for (size_t k = 0; k < ep.size() && k < 8; ++k) h.ep[k] = ep[k];
+    h.err = err_word;
+    h.a_mn = s.a_col ? 1 : 0;
+    h.b_mn = s.b_col ? 0 : 1;
+    h.num_m = (int)((s.M + BM - 1) / BM);
+    h.num_n = (int)((s.N + BN - 1) / BN);
+    int64_t tiles = (int64_t)h.num_m * h.num_n;
+    if (tiles > (1LL << 30)) {
+        err = "tensor-core GEMM: too many tiles";
+        return 12;
+    }
+    h.num_tiles = (int)tiles;
+    h.group_m = 16;
+    const char* to = getenv("BAFE_TC_TIMEOUT_MS");
+    h.timeout_ns = (unsigned long long)(to ? atof(to) : 2000.0) * 1000000ull;
+    memcpy(L.args, &h, sizeof(h));
+    L.grid = (unsigned)(tiles < sm_count ? tiles : sm_count);
+    L.block = (unsigned)threads_of(s.tc_variant);
+    L.smem = (unsigned)tc_smem_bytes(s.tc_variant);
+    return 0;
 }
 
 }  // namespace bafe_cuda

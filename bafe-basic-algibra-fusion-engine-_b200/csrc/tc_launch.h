@@ -12,9 +12,12 @@ struct TcLaunch {
 
 bool tc_kernel_enabled();
 int tc_smem_bytes(int variant);
-int tc_prepare(const Step& s, const void* a, const void* b, void* out, const std::vector<const void*>& ep,
-               int sm_count, TcLaunch& L, std::string& err);
+// a_lo / b_lo: 3xTF32 residual operands (same layouts as a / b), or null.
+int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
+               const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,
+               std::string& err);
+// swizzle: 0 none, 1 = 128B, 2 = 128B with 32-byte atoms
 int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
-                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle128, std::string& err);
+                         const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err);
 
 }  // namespace bafe_cuda

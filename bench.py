@@ -60,8 +60,12 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--precision", default=os.environ.get("BAFE_GEMM_PRECISION", "auto"))
-    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=3, help="0 skips the host-pointer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--only", choices=["gemm", "ew"], default=None,
+                   help="run one workload (profiling); prints its own line")
+    p.add_argument("--gemm-size", type=int, default=GEMM_M, help="M=N=K (profiling smaller cases)")
+    p.add_argument("--ew-elements", type=int, default=EW_N)
     return p.parse_args()
 
 
@@ -129,12 +133,12 @@ class Clocks:
 
 # ------------------------------------------------------------ workloads --
 
-def gemm_graph(m_rows: int):
+def gemm_graph(m_rows: int, size: int = GEMM_N):
     import bafe_b200 as bafe
     g = bafe.GraphBuilder()
-    a = g.add_input("A", (m_rows, GEMM_K), 0, 0)
-    b = g.add_input("B", (GEMM_K, GEMM_N), 0, 2)      # BLOCKED tag, row-major storage
-    c = g.add_input("C", (m_rows, GEMM_N), 0, 0)
+    a = g.add_input("A", (m_rows, size), 0, 0)
+    b = g.add_input("B", (size, size), 0, 2)      # BLOCKED tag, row-major storage
+    c = g.add_input("C", (m_rows, size), 0, 0)
     g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
     return g
 
@@ -153,6 +157,7 @@ def time_steps(torch, kernel, ins, out, steps, warmup):
     for _ in range(warmup):
         kernel.run_torch(ins, out, s)
     torch.cuda.synchronize()
+    time.sleep(0.3)   # let the clock sampler (started by the caller) take its first samples
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
     launches0 = __import__("bafe_b200").launch_count()
     ev[0].record(s)
@@ -273,159 +278,171 @@ def cpu_baseline_ew(x: np.ndarray, y: np.ndarray, z: np.ndarray):
 
 # ------------------------------------------------------------ our arm --
 
-def run_ours(args):
-    import torch
+class Ctx:
+    def __init__(self, args):
+        import torch
+        self.torch = torch
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if args.gpus != self.world:
+            raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={self.world}")
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        self.dist = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist_mod
+            dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
+            self.dist = dist_mod
+        self.hbm_peak, self.bf16_peak, self.peak_src = peaks()
+        self.gen = torch.Generator(device=self.dev).manual_seed(1234 + self.rank)
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max(self, x):
+        return reduce_max(self.torch, self.dist, x, self.dev)
+
+    def sum(self, x):
+        return reduce_sum(self.torch, self.dist, x, self.dev)
+
+
+def bench_gemm(c: Ctx) -> dict:
     import bafe_b200 as bafe
-
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if args.gpus != world:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist_mod
-        dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-        dist = dist_mod
-    bafe.set_option("gemm_precision", args.precision)
-    hbm_peak, bf16_peak, peak_src = peaks()
-    tf32_peak = bf16_peak / 2.0
-
-    def barrier():
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    # ---------------- fused GEMM: M-row panels ----------------
-    rows = GEMM_M // world
-    r0 = rank * rows
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    A = torch.randn(rows, GEMM_K, device=dev, generator=gen) * STD
-    C = torch.randn(rows, GEMM_N, device=dev, generator=gen) * STD
-    B = torch.empty(GEMM_K, GEMM_N, device=dev)
-    if rank == 0:
-        B.copy_(torch.randn(GEMM_K, GEMM_N, device=dev, generator=torch.Generator(device=dev).manual_seed(99)) * STD)
+    torch, args = c.torch, c.args
+    S = args.gemm_size
+    std = 1.0 / math.sqrt(S)
+    rows = S // c.world
+    A = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
+    C = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
+    B = torch.empty(S, S, device=c.dev)
+    if c.rank == 0:
+        B.copy_(torch.randn(S, S, device=c.dev, generator=torch.Generator(device=c.dev).manual_seed(99)) * std)
     bcast_ms = 0.0
-    if dist is not None:
-        barrier()
+    if c.dist is not None:
+        c.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        dist.broadcast(B, src=0)
+        c.dist.broadcast(B, src=0)
         e1.record()
         torch.cuda.synchronize()
-        bcast_ms = reduce_max(torch, dist, e0.elapsed_time(e1), dev)
-    out = torch.empty(rows, GEMM_N, device=dev)
+        bcast_ms = c.max(e0.elapsed_time(e1))
+    out = torch.empty(rows, S, device=c.dev)
     t_compile = time.perf_counter()
-    k = bafe.compile_graph(gemm_graph(rows))
+    k = bafe.compile_graph(gemm_graph(rows, S))
     t_compile = time.perf_counter() - t_compile
-    plan_desc = k.describe().strip()
-    barrier()
-    with Clocks(local) as ck:
+    plan = k.describe().strip()
+    c.barrier()
+    with Clocks(c.local) as ck:
         per, total_ms, launches = time_steps(torch, k, [A, B, C], out, args.steps, args.warmup)
-    barrier()
+    c.barrier()
     clocks = ck.summary()
-    total_ms = reduce_max(torch, dist, total_ms, dev)
-    launches = int(reduce_sum(torch, dist, launches, dev))
+    total_ms = c.max(total_ms)
+    launches = int(c.sum(launches))
     ms_step = total_ms / args.steps
-    flops_total = 2.0 * GEMM_M * GEMM_N * GEMM_K
-    value = flops_total / (ms_step * 1e-3) / 1e12
+    flops_total = 2.0 * S * S * S
     kern_ms = statistics.mean(per)
-    achieved = 2.0 * rows * GEMM_N * GEMM_K / (kern_ms * 1e-3) / 1e12
-    tc3 = "3xtf32" in plan_desc
+    achieved = 2.0 * rows * S * S / (kern_ms * 1e-3) / 1e12
+    tc3 = "3xtf32" in plan
+    tf32_peak = c.bf16_peak / 2.0
     peak = tf32_peak / 3.0 if tc3 else tf32_peak
+    res = {
+        "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C))",
+        "value": round(flops_total / (ms_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+        "ms_per_step": round(ms_step, 4),
+        "dtype": "fp32 via 3xtf32" if tc3 else ("tf32" if "tc.tf32" in plan else "fp32"),
+        "config": {"workload": f"relu(matmul(A,B)+C) M=N=K={S} fp32, A row-major, B BLOCKED tag",
+                   "parallelism": f"M-row panels x{c.world}, B broadcast once (outside timed region)",
+                   "l2": "inputs larger than L2 (1 GiB each); no flush" if S >= 8192 else "inputs smaller than L2",
+                   "plan": plan, "precision_option": args.precision},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(f"gemm_{S}"),
+                     "peak_basis": f"{c.peak_src} bf16 {c.bf16_peak} TFLOP/s / 2 (tf32 rate)"
+                                   + (" / 3 (three products)" if tc3 else "")},
+        "gpu_launches": launches, "clocks": clocks, "b_broadcast_ms": round(bcast_ms, 3),
+        "compile_s": round(t_compile, 2),
+    }
+    if args.e2e_steps > 0:
+        hA, hB, hC = A.cpu().pin_memory(), B.cpu().pin_memory(), C.cpu().pin_memory()
+        hO = torch.empty(rows, S).pin_memory()
+        c.barrier()
+        e2e_ms = c.max(time_e2e(torch, k, [hA, hB, hC], hO, args.e2e_steps))
+        res["e2e"] = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                      "h2d_bytes_per_step": float(4 * (A.numel() + B.numel() + C.numel())) * c.world,
+                      "d2h_bytes_per_step": float(4 * out.numel()) * c.world, "ms_per_step": round(e2e_ms, 2),
+                      "path": "bafe_cuda_jit_get_or_compile host function, pinned host buffers"}
+        if c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
+            res["cpu_baseline"] = cpu_baseline_gemm(hA[:8].numpy(), hB.numpy(), hC[:8].numpy())
+        del hA, hB, hC, hO
+    elif c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
+        res["cpu_baseline"] = cpu_baseline_gemm(A[:8].cpu().numpy(), B.cpu().numpy(), C[:8].cpu().numpy())
+    return res
 
-    # e2e through the host-pointer ABI (pinned host buffers)
-    hA = A.cpu().pin_memory()
-    hB = B.cpu().pin_memory()
-    hC = C.cpu().pin_memory()
-    hO = torch.empty(rows, GEMM_N).pin_memory()
-    barrier()
-    e2e_ms = time_e2e(torch, k, [hA, hB, hC], hO, args.e2e_steps)
-    e2e_ms = reduce_max(torch, dist, e2e_ms, dev)
-    h2d = float(4 * (A.numel() + B.numel() + C.numel())) * world
-    d2h = float(4 * out.numel()) * world
 
-    cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        cpu = cpu_baseline_gemm(hA[:8].numpy(), hB.numpy(), hC[:8].numpy())
-    del hA, hB, hC, hO
+def bench_ew(c: Ctx) -> dict:
+    import bafe_b200 as bafe
+    torch, args = c.torch, c.args
+    n_total = args.ew_elements
+    n_local = n_total // c.world
+    X, Y, Z = (torch.rand(n_local, device=c.dev, generator=c.gen) * 2 - 1 for _ in range(3))
+    O = torch.empty(n_local, device=c.dev)
+    k = bafe.compile_graph(ew_graph(n_local))
+    steps = max(args.steps, 200)
+    c.barrier()
+    with Clocks(c.local) as ck:
+        per, total, launches = time_steps(torch, k, [X, Y, Z], O, steps, args.warmup)
+    c.barrier()
+    total = c.max(total)
+    ms = total / steps
+    achieved = 16.0 * n_local / (statistics.mean(per) * 1e-3) / 1e9
+    res = {
+        "metric": f"GB/s (relu(add(mul(X,Y),Z)) {n_total} fp32)", "value": round(16.0 * n_total / (ms * 1e-3) / 1e9, 1),
+        "unit": "GB/s", "ms_per_step": round(ms, 4), "steps": steps,
+        "config": {"workload": f"relu(add(mul(X,Y),Z)) over {n_total} fp32 elements, U(-1,1)",
+                   "parallelism": f"contiguous ranges x{c.world}, no collective",
+                   "l2": "inputs larger than L2; no flush" if n_local * 4 > (126 << 20) else "inputs smaller than L2",
+                   "plan": k.describe().strip()},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": c.hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / c.hbm_peak, 4),
+                     "traffic": traffic_from_profiles(f"ew_{n_total}"), "peak_basis": f"{c.peak_src} hbm_gbs"},
+        "gpu_launches": int(c.sum(launches)), "clocks": ck.summary(),
+    }
+    if args.e2e_steps > 0:
+        hX, hY, hZ = X.cpu().pin_memory(), Y.cpu().pin_memory(), Z.cpu().pin_memory()
+        hO = torch.empty(n_local).pin_memory()
+        c.barrier()
+        e2e_ms = c.max(time_e2e(torch, k, [hX, hY, hZ], hO, args.e2e_steps))
+        res["e2e"] = {"value": round(16.0 * n_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                      "h2d_bytes_per_step": 12.0 * n_total, "d2h_bytes_per_step": 4.0 * n_total,
+                      "ms_per_step": round(e2e_ms, 2)}
+        if c.rank == 0 and not args.no_cpu_baseline:
+            m = min(1 << 24, n_local)
+            res["cpu_baseline"] = cpu_baseline_ew(hX[:m].numpy(), hY[:m].numpy(), hZ[:m].numpy())
+    return res
 
-    # ---------------- elementwise chain: range split ----------------
-    n_local = EW_N // world
-    X = torch.rand(n_local, device=dev, generator=gen) * 2 - 1
-    Y = torch.rand(n_local, device=dev, generator=gen) * 2 - 1
-    Z = torch.rand(n_local, device=dev, generator=gen) * 2 - 1
-    O = torch.empty(n_local, device=dev)
-    ke = bafe.compile_graph(ew_graph(n_local))
-    barrier()
-    with Clocks(local) as ck2:
-        eper, etotal, elaunch = time_steps(torch, ke, [X, Y, Z], O, max(args.steps, 20), args.warmup)
-    barrier()
-    etotal = reduce_max(torch, dist, etotal, dev)
-    ems = etotal / max(args.steps, 20)
-    ew_value = 16.0 * EW_N / (ems * 1e-3) / 1e9
-    ew_achieved = 16.0 * n_local / (statistics.mean(eper) * 1e-3) / 1e9
-    hX, hY, hZ = X.cpu().pin_memory(), Y.cpu().pin_memory(), Z.cpu().pin_memory()
-    hOe = torch.empty(n_local).pin_memory()
-    barrier()
-    ew_e2e_ms = reduce_max(torch, dist, time_e2e(torch, ke, [hX, hY, hZ], hOe, args.e2e_steps), dev)
-    ew_cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
-        m = 1 << 24
-        ew_cpu = cpu_baseline_ew(hX[:m].numpy(), hY[:m].numpy(), hZ[:m].numpy())
 
-    if rank == 0:
-        line = {
-            "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C))",
-            "value": round(value, 3),
-            "unit": "TFLOP/s",
-            "n_gpus": world,
-            "steps": args.steps,
-            "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True,
-            "scaling": "strong",
-            "vs_baseline": None,
-            "dtype": "fp32 via 3xtf32" if tc3 else ("tf32" if "tc.tf32" in plan_desc else "fp32"),
-            "data": "synthetic N(0,1/sqrt(K)) fp32, generated on device",
-            "config": {"workload": "relu(matmul(A,B)+C) M=N=K=16384 fp32, A row-major, B BLOCKED tag",
-                       "parallelism": f"M-row panels x{world}, B broadcast once (outside timed region)",
-                       "l2": "inputs larger than L2 (1 GiB each); no flush",
-                       "plan": plan_desc, "precision_option": args.precision},
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 2),
-                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic_from_profiles("gemm_16384"),
-                         "peak_basis": f"{peak_src} bf16 {bf16_peak} TFLOP/s / 2 (tf32 rate)"
-                                       + (" / 3 (three products)" if tc3 else "")},
-            "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": round(e2e_ms, 2), "path": "bafe_cuda_jit_get_or_compile host function, pinned"},
-            "cpu_baseline": cpu,
-            "gpu_launches": launches,
-            "clocks": clocks,
-            "b_broadcast_ms": round(bcast_ms, 3),
-            "compile_s": round(t_compile, 2),
-            "ew": {
-                "metric": "GB/s (relu(add(mul(X,Y),Z)) 2^28 fp32)", "value": round(ew_value, 1), "unit": "GB/s",
-                "ms_per_step": round(ems, 4),
-                "roofline": {"bound": "hbm", "achieved": round(ew_achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                             "frac": round(ew_achieved / hbm_peak, 4), "traffic": traffic_from_profiles("ew_2p28"),
-                             "peak_basis": f"{peak_src} hbm_gbs"},
-                "e2e": {"value": round(16.0 * EW_N / (ew_e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                        "h2d_bytes_per_step": 12.0 * EW_N, "d2h_bytes_per_step": 4.0 * EW_N,
-                        "ms_per_step": round(ew_e2e_ms, 2)},
-                "cpu_baseline": ew_cpu,
-                "gpu_launches": elaunch,
-                "clocks": ck2.summary(),
-            },
-        }
+def run_ours(args):
+    import bafe_b200 as bafe
+    c = Ctx(args)
+    bafe.set_option("gemm_precision", args.precision)
+    common = {"n_gpus": c.world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+              "scaling": "strong", "vs_baseline": None, "data": "synthetic, generated on device"}
+    if args.only == "ew":
+        line = dict(bench_ew(c), **{k: v for k, v in common.items() if k != "steps"})
+        line["scaling"] = "strong"
+    else:
+        line = dict(common, **bench_gemm(c))
+        if args.only is None:
+            line["ew"] = bench_ew(c)
+    if c.rank == 0:
         print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    if c.dist is not None:
+        c.dist.barrier()
+        c.dist.destroy_process_group()
 
 
 # ------------------------------------------------------ reference arm --

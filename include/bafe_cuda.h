@@ -167,6 +167,13 @@ int bafe_cuda_run_device(int plan, void *const *ptrs, int n_ptrs, void *stream);
  * Returns 0 or a nonzero code. */
 int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);
 
+/* Waits for all work on the current device and reports an error a kernel
+ * raised asynchronously (a pipeline wait that exceeded its deadline; the
+ * outputs of that launch are then invalid).  Returns 0 or a nonzero code
+ * with the message in bafe_cuda_last_error.  Host-pointer calls check this
+ * themselves; callers of bafe_cuda_run_device call it after their work. */
+int bafe_cuda_synchronize(void);
+
 /* Last error raised by any entry point (including the host function
  * pointers, which return void like the reference's kernels and so cannot
  * report failure themselves).  Copies the message, returns the code

@@ -1,0 +1,165 @@
+"""Tensor-core GEMM (tcgen05, kind::tf32) parity.
+
+Bounds (inputs N(0,1) unless stated; K = inner dimension):
+  * 3xTF32: max |out - reference| <= 1e-4 * sqrt(K/64), the north-star
+    bound, against both an fp64 evaluation and the reference's own fp32
+    result (golden row panels, exact reference summation order);
+  * 1xTF32: max |out - fp64| <= TF32_TOL * sqrt(K/64) with
+    TF32_TOL = 4e-2 (measured maxima are printed by the tests).
+Operands are device-resident (torch); column-major operands are passed as
+their transposed row-major storage with the COL_MAJOR tag.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import bafe_b200 as bafe
+import cases
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 4e-2
+
+
+def _graph(M, N, K, a_col, b_col, epi):
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", (M, K), 0, 1 if a_col else 0)
+    b = g.add_input("B", (K, N), 0, 1 if b_col else 0)
+    mm = g.add("matmul", [a, b])
+    if epi == "none":
+        root = mm
+    elif epi == "relu_add_c":
+        c = g.add_input("C", (M, N), 0, 0)
+        root = g.add("relu", [g.add("add", [mm, c])])
+    elif epi == "relu_add_mul":
+        c = g.add_input("C", (M, N), 0, 0)
+        d = g.add_input("D", (M, N), 0, 0)
+        root = g.add("relu", [g.add("add", [mm, g.add("mul", [c, d])])])
+    elif epi == "relu_bias":
+        c = g.add_input("bias", (N,), 0, 0)
+        root = g.add("relu", [g.add("add", [mm, c])])
+    else:
+        raise ValueError(epi)
+    g.set_output(root)
+    return g
+
+
+def _run(torch, M, N, K, a_col, b_col, epi, prec, seed=0, scale=1.0):
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn(M, K, device="cuda", generator=gen) * scale
+    B = torch.randn(K, N, device="cuda", generator=gen) * scale
+    extra = []
+    if epi in ("relu_add_c", "relu_add_mul"):
+        extra.append(torch.randn(M, N, device="cuda", generator=gen))
+    if epi == "relu_add_mul":
+        extra.append(torch.randn(M, N, device="cuda", generator=gen))
+    if epi == "relu_bias":
+        extra.append(torch.randn(N, device="cuda", generator=gen))
+    bafe.set_option("gemm_precision", prec)
+    k = bafe.compile_graph(_graph(M, N, K, a_col, b_col, epi))
+    a_store = A.t().contiguous() if a_col else A
+    b_store = B.t().contiguous() if b_col else B
+    out = torch.empty(M, N, device="cuda")
+    k.run_torch([a_store, b_store] + extra, out)
+    bafe.synchronize()
+    ref = A.double() @ B.double()
+    if epi == "relu_add_c":
+        ref = torch.relu(ref + extra[0].double())
+    elif epi == "relu_add_mul":
+        ref = torch.relu(ref + (extra[0] * extra[1]).double())
+    elif epi == "relu_bias":
+        ref = torch.relu(ref + extra[0].double())
+    err = float((out.double() - ref).abs().max())
+    return k, out, err
+
+
+SHAPES = [(128, 256, 32), (256, 256, 256), (300, 520, 100), (1000, 768, 1024), (132, 260, 36)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("a_col,b_col", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_3xtf32_layouts_and_shapes(cuda, shape, a_col, b_col):
+    M, N, K = shape
+    k, out, err = _run(cuda, M, N, K, a_col, b_col, "none", "3xtf32")
+    assert "gemm.tc.3xtf32" in k.describe()
+    bound = 1e-4 * math.sqrt(K / 64)
+    print(f"3xtf32 {shape} a_col={a_col} b_col={b_col}: max err {err:.3e} (bound {bound:.1e})")
+    assert err <= bound
+
+
+@pytest.mark.parametrize("epi", ["relu_add_c", "relu_add_mul", "relu_bias"])
+def test_3xtf32_fused_epilogues(cuda, epi):
+    k, out, err = _run(cuda, 512, 512, 512, 0, 0, epi, "3xtf32", seed=3)
+    steps = k.describe().strip().splitlines()
+    # residual pre-passes for A and B, then one GEMM carrying the epilogue
+    assert [l.split()[0] for l in steps] == ["ew", "ew", "gemm.tc.3xtf32"], steps
+    assert "tf32_residual(A)" in steps[0] and "tf32_residual(B)" in steps[1]
+    bound = 1e-4 * math.sqrt(512 / 64)
+    print(f"3xtf32 epilogue {epi}: max err {err:.3e}")
+    assert err <= bound
+
+
+@pytest.mark.parametrize("shape", [(256, 256, 256), (1000, 768, 1024), (2048, 2048, 2048)])
+@pytest.mark.parametrize("a_col,b_col", [(0, 0), (1, 1)])
+def test_tf32(cuda, shape, a_col, b_col):
+    M, N, K = shape
+    k, out, err = _run(cuda, M, N, K, a_col, b_col, "relu_add_c", "tf32", seed=5)
+    assert "gemm.tc.tf32" in k.describe()
+    bound = TF32_TOL * math.sqrt(K / 64)
+    print(f"tf32 {shape} a_col={a_col} b_col={b_col}: max err {err:.3e} (bound {bound:.1e})")
+    assert err <= bound
+
+
+def test_3xtf32_large_many_tiles(cuda):
+    """4096^3 (512 tiles over 148 persistent CTAs, both accumulators cycling)."""
+    k, out, err = _run(cuda, 4096, 4096, 4096, 0, 0, "relu_add_mul", "3xtf32", seed=9)
+    bound = 1e-4 * math.sqrt(4096 / 64)
+    print(f"3xtf32 4096^3 relu(add(mm, C*D)): max err {err:.3e} (bound {bound:.1e})")
+    assert err <= bound
+
+
+@pytest.mark.parametrize("name", [c["name"] for c in cases.CASES if c.get("panel")])
+def test_3xtf32_matches_reference_panels(cuda, name):
+    """Full-size 4096^3 / 16384^3 configs on the tensor cores vs the
+    reference's own fp32 rows (golden panels): within 1e-4*sqrt(K/64)."""
+    torch = cuda
+    meta, stored, golden = cases.load(name)
+    c = cases.CASE_BY_NAME[name]
+    arrays = {s[0]: cases.make_input(s) for s in c["inputs"]}
+    bafe.set_option("gemm_precision", "auto")
+    g = bafe.GraphBuilder()
+    ids = [g.add_input(s[0], arrays[s[0]].shape, 0, s[4]) for s in c["inputs"]]
+    g.set_output(c["build"](g, *ids))
+    k = bafe.compile_graph(g)
+    assert "gemm.tc.3xtf32" in k.describe(), k.describe()
+    dev = [torch.from_numpy(arrays[s[0]]).cuda() for s in c["inputs"]]
+    M = arrays["A"].shape[0]
+    out = torch.empty(M, arrays["B"].shape[1], device="cuda")
+    k.run_torch(dev, out)
+    bafe.synchronize()
+    r0, r1 = meta["panel"]
+    got = out[r0:r1].cpu().numpy()
+    K = arrays["A"].shape[1]
+    err = float(np.max(np.abs(got.astype(np.float64) - golden.astype(np.float64))))
+    bound = 1e-4 * math.sqrt(K / 64)
+    print(f"{name}: 3xtf32 vs reference max err {err:.3e} (bound {bound:.1e})")
+    assert err <= bound
+
+
+def test_host_pointer_path_tensor_cores(cuda):
+    """The legacy host-pointer function on a tensor-core plan."""
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((512, 384), dtype=np.float32)
+    B = np.asfortranarray(rng.standard_normal((384, 640), dtype=np.float32))
+    C = rng.standard_normal((512, 640), dtype=np.float32)
+
+    @bafe.jit
+    def f(A, B, C):
+        return bafe.relu(bafe.matmul(A, B) + C)
+
+    bafe.set_option("gemm_precision", "3xtf32")
+    out = f(A, B, C)
+    ref = np.maximum(A.astype(np.float64) @ B.astype(np.float64) + C, 0)
+    assert "a=row b=col" in f.kernel_for(A, B, C).describe()
+    assert np.max(np.abs(out - ref)) <= 1e-4 * math.sqrt(384 / 64)
