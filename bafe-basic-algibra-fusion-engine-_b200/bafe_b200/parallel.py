@@ -1,0 +1,87 @@
+"""Multi-GPU execution of the hot path: one process per GPU.
+
+* GEMM-rooted graphs (relu(matmul(A,B)+C), ...) shard by contiguous M-row
+  panels: rank r owns rows [r0, r1) of A, of every full-size epilogue
+  operand and of the output, and runs the plan of its panel graph on its own
+  device.  B is needed whole on every rank: it is broadcast once from the
+  root over NCCL and stays resident.  Row-vector operands (bias) are small
+  and replicated.  The output stays sharded; `gather_rows` all-gathers it
+  when a single copy is needed.
+* Elementwise graphs shard by contiguous element ranges with no collective
+  (range starts are multiples of 4 elements so every shard keeps 16-byte
+  vector access).
+Panel boundaries are multiples of 128 rows (the tensor-core tile height)
+where the size allows, so no rank carries a partial tile in the middle.
+
+The collectives go through torch.distributed (NCCL on GPUs, gloo in the
+CPU tests).  The kernel work per rank is bafe_b200.compile_graph(...) of
+the panel graph.
+"""
+from __future__ import annotations
+
+from typing import Callable, List, Sequence, Tuple
+
+
+def row_panels(M: int, world: int, align: int = 128) -> List[Tuple[int, int]]:
+    """Contiguous row panels covering [0, M): as equal as possible, with
+    boundaries rounded to multiples of `align` when M allows."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    unit = align if M >= align * world else 1
+    units = (M + unit - 1) // unit
+    out = []
+    for r in range(world):
+        a = (units * r) // world * unit
+        b = (units * (r + 1)) // world * unit
+        out.append((min(a, M), min(b, M)))
+    return out
+
+
+def element_ranges(n: int, world: int, align: int = 4) -> List[Tuple[int, int]]:
+    """Contiguous element ranges covering [0, n), starts multiples of `align`."""
+    return row_panels(n, world, align)
+
+
+def broadcast_resident(tensor, dist, src: int = 0):
+    """Broadcast `tensor` from `src` in place (B of a sharded GEMM)."""
+    if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.broadcast(tensor, src=src)
+    return tensor
+
+
+def gather_rows(panel, full_rows: int, dist, panels: Sequence[Tuple[int, int]]):
+    """All-gather row panels into the full (full_rows, N) tensor on every rank.
+    Panels may differ in height, so each rank pads to the largest panel."""
+    import torch
+    if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
+        return panel
+    h = max(b - a for a, b in panels)
+    padded = torch.zeros((h,) + tuple(panel.shape[1:]), dtype=panel.dtype, device=panel.device)
+    padded[: panel.shape[0]] = panel
+    parts = [torch.empty_like(padded) for _ in panels]
+    dist.all_gather(parts, padded)
+    return torch.cat([p[: b - a] for p, (a, b) in zip(parts, panels)], dim=0)[:full_rows]
+
+
+class RowPanelGemm:
+    """A GEMM-rooted graph sharded over the ranks by M-row panels.
+
+    build(rows) must return a GraphBuilder for a problem with `rows` rows of
+    A / C / output (the other shapes fixed); inputs are given as full-size
+    names -> tensors on the caller side and sliced here.
+    """
+
+    def __init__(self, build: Callable[[int], object], M: int, dist=None):
+        import bafe_b200
+        self.dist = dist
+        world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+        rank = dist.get_rank() if dist is not None and dist.is_initialized() else 0
+        self.panels = row_panels(M, world)
+        self.r0, self.r1 = self.panels[rank]
+        self.rows = self.r1 - self.r0
+        self.kernel = bafe_b200.compile_graph(build(self.rows))
+
+    def run(self, inputs: Sequence, out, stream=None) -> None:
+        """inputs: this rank's operands in graph order (panels for row-sharded
+        operands, the resident B whole); out: this rank's output panel."""
+        self.kernel.run_torch(list(inputs), out, stream)

@@ -1,0 +1,129 @@
+"""Multi-rank host logic on CPU (gloo, world_size 2): row-panel sharding of
+the fused GEMM, broadcast of the resident B, all-gather of the output, range
+split of the elementwise chain, and a rank failure surfacing as an error on
+the other rank.  Each rank computes its panel with the CPU oracle (the
+product is the GPU kernel; here the sharding plumbing is under test)."""
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from bafe_b200.parallel import element_ranges, row_panels
+
+ROOT = Path(__file__).resolve().parent.parent
+PATHS = [str(ROOT / "bafe-basic-algibra-fusion-engine-_b200"), str(ROOT), str(ROOT / "tests" / "golden")]
+
+
+def test_row_panels_cover_and_align():
+    for M, W in [(16384, 8), (16384, 3), (300, 2), (5, 4), (128, 1), (1000, 7)]:
+        p = row_panels(M, W)
+        assert p[0][0] == 0 and p[-1][1] == M
+        assert all(a <= b for a, b in p)
+        assert all(p[i][1] == p[i + 1][0] for i in range(W - 1))
+        if M >= 128 * W:
+            assert all(a % 128 == 0 for a, _ in p)
+            sizes = [b - a for a, b in p]
+            assert max(sizes) - min(sizes) <= 128
+
+
+def test_element_ranges_keep_vector_alignment():
+    for n, W in [(1 << 28, 8), (1 << 28, 3), (1001, 2)]:
+        r = element_ranges(n, W)
+        assert r[0][0] == 0 and r[-1][1] == n
+        if n >= 4 * W:
+            assert all(a % 4 == 0 for a, _ in r)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, mode, q):
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from bafe_b200.graph import GraphBuilder
+    from bafe_b200.parallel import broadcast_resident, gather_rows, row_panels
+    from oracle import oracle
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        M, N, K = 300, 72, 40
+        rng = np.random.default_rng(3)
+        A = rng.standard_normal((M, K), dtype=np.float32)
+        Bfull = rng.standard_normal((K, N), dtype=np.float32)
+        C = rng.standard_normal((M, N), dtype=np.float32)
+        if mode == "fail" and rank == 1:
+            raise RuntimeError("rank 1 fails before the broadcast")
+        B = torch.from_numpy(Bfull.copy()) if rank == 0 else torch.zeros(K, N)
+        broadcast_resident(B, dist)
+        panels = row_panels(M, world)
+        r0, r1 = panels[rank]
+
+        def graph(rows):
+            g = GraphBuilder()
+            a = g.add_input("A", (rows, K), 0, 0)
+            b = g.add_input("B", (K, N), 0, 2)
+            c = g.add_input("C", (rows, N), 0, 0)
+            g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
+            return g
+
+        gp = graph(r1 - r0)
+        ids = gp.inputs
+        mine = oracle.evaluate(gp.to_list(), {ids[0]: A[r0:r1], ids[1]: B.numpy(), ids[2]: C[r0:r1]}, gp.output)
+        full = gather_rows(torch.from_numpy(mine.reshape(r1 - r0, N)), M, dist, panels)
+        if rank == 0:
+            gf = graph(M)
+            want = oracle.evaluate(gf.to_list(), dict(zip(gf.inputs, (A, Bfull, C))), gf.output)
+            q.put(("ok", full.numpy().tobytes() == want.tobytes()))
+    except Exception as e:   # reported to the parent
+        q.put(("error", f"rank {rank}: {type(e).__name__}: {e}"))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _spawn(mode):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    return out
+
+
+def test_sharded_gemm_equals_full_problem():
+    res = _spawn("ok")
+    assert ("ok", True) in res, res
+
+
+def test_failed_rank_surfaces_as_error_on_the_other_rank():
+    """Rank 1 raises before the collective; rank 0's broadcast ends with an
+    error (short process-group timeout) instead of hanging."""
+    res = _spawn("fail")
+    errs = [m for kind, m in res if kind == "error"]
+    assert any(m.startswith("rank 1") for m in errs), res
+    assert any(m.startswith("rank 0") for m in errs), res
