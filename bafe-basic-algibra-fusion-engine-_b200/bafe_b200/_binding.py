@@ -103,6 +103,8 @@ def _load() -> ctypes.CDLL:
         "bafe_cuda_get_option": ([c_char_p, c_char_p, c_size_t], c_int),
         "bafe_cuda_launch_count": ([], c_int64),
         "bafe_cuda_abi_size": ([c_int], c_int64),
+        "bafe_cuda_gemm_3xtf32_static_scratch": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                                                  c_int, c_void_p], c_int),
     }
     for name, (args, res) in proto.items():
         fn = getattr(lib, name)
@@ -121,7 +123,7 @@ EXPORTED_SYMBOLS = (
     "bafe_cuda_plan_num_inputs", "bafe_cuda_plan_describe", "bafe_cuda_plan_output_bytes",
     "bafe_cuda_plan_input_bytes", "bafe_cuda_run_device", "bafe_cuda_run_host", "bafe_cuda_synchronize", "bafe_cuda_last_error",
     "bafe_cuda_clear_error", "bafe_cuda_set_option", "bafe_cuda_get_option", "bafe_cuda_launch_count",
-    "bafe_cuda_abi_size",
+    "bafe_cuda_abi_size", "bafe_cuda_gemm_3xtf32_static_scratch",
 )
 
 

@@ -194,6 +194,31 @@ int bafe_cuda_get_option(const char *key, char *buf, size_t buf_size);
  * plans, all devices).  Used to report launch counts. */
 int64_t bafe_cuda_launch_count(void);
 
+/* out = A . B (fp32, 3xTF32 tensor cores, M x N row-major out) without any
+ * device allocation.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: code running during stream
+ * capture, code with a strict memory budget or its own allocator that
+ * forbids hidden device allocations, and code that must avoid the implicit
+ * synchronisation of cudaMalloc / cudaFree.  The planned entry points keep
+ * GEMM scratch (the tf32 residuals of A and B) in device buffers allocated
+ * on first use; this one uses a 64 MiB array compiled into the library
+ * (present on every GPU that loads it, until exit), so M*K + K*N must stay
+ * below ~16.7M floats -- larger problems return an error without running.
+ * A is M x K and B is K x N, each row-major or (a_col / b_col = 1) stored
+ * column-major; row strides must be multiples of 16 bytes, N % 4 == 0 and
+ * all pointers 16-byte aligned (device memory on the current device).
+ * Runs on `stream` (a cudaStream_t, NULL = legacy default stream) and
+ * returns when `out` holds the result; 0 or a nonzero code with the
+ * message in bafe_cuda_last_error.
+ * All calls share the one scratch array: calls that overlap on the GPU
+ * (other streams or host threads) race on it.  The first call on a device
+ * looks the array up and configures the kernel for that device; make it
+ * before any stream capture. */
+int bafe_cuda_gemm_3xtf32_static_scratch(const float *A, const float *B, float *out,
+                                         int64_t M, int64_t N, int64_t K,
+                                         int a_col, int b_col, void *stream);
+
 /* sizeof() of the graph ABI structs as this library was compiled:
  * which = 0 bafe_graph, 1 bafe_node, 2 bafe_op_attrs, 3 bafe_shape.
  * Lets a binding check its struct mirror against the library. */
