@@ -23,6 +23,7 @@ Options& options() {
         init = true;
         if (const char* p = getenv("BAFE_GEMM_PRECISION")) o.gemm_precision = p;
         if (const char* d = getenv("BAFE_DEVICE")) o.device = atoi(d);
+        if (const char* t = getenv("BAFE_TC_PAIR")) o.tc_pair = atoi(t) != 0;
     }
     return o;
 }
@@ -127,7 +128,7 @@ BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* 
         return nullptr;
     }
     const Options& opt = options();
-    std::string key = std::string(hash) + "|prec=" + opt.gemm_precision;
+    std::string key = std::string(hash) + "|prec=" + opt.gemm_precision + (opt.tc_pair ? "|pair" : "|single");
     auto it = g_by_key.find(key);
     if (it != g_by_key.end() && plan_ptr(it->second)) {
         int slot = slot_of_plan(it->second);
@@ -294,6 +295,11 @@ BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
         o.gemm_precision = v;
         return 0;
     }
+    if (k == "tc_pair") {
+        if (v != "0" && v != "1") return -1;
+        o.tc_pair = v == "1";
+        return 0;
+    }
     if (k == "device") {
         char* end = nullptr;
         long d = strtol(value, &end, 10);
@@ -311,6 +317,7 @@ BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
     std::string k = key, v;
     if (k == "gemm_precision") v = o.gemm_precision;
     else if (k == "device") v = std::to_string(o.device);
+    else if (k == "tc_pair") v = o.tc_pair ? "1" : "0";
     else return -1;
     if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());
     return 0;

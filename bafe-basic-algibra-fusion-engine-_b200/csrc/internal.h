@@ -75,6 +75,7 @@ const char* dtype_ctype(int dtype);   // device C type of the STORAGE (u16 for h
 struct Options {
     std::string gemm_precision = "auto";   // auto | 3xtf32 | tf32 | exact
     int device = -1;                        // -1: current device
+    bool tc_pair = true;                    // tensor-core GEMM on CTA pairs (cta_group::2)
 };
 Options& options();
 
@@ -106,6 +107,7 @@ struct Step {
     int n_epi = 0;                 // epilogue operands are srcs[2..2+n_epi)
     bool direct = false;           // fused-form summation order (one chunk)
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
+    bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
     std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
     // Transpose2d (output M x N), Gather, Reduce
     int64_t gdims[8] = {0}, gstride[8] = {0};

@@ -71,6 +71,16 @@ template <> struct TcCfg<1> {      // 1xTF32
 template <> struct TcCfg<3> {      // 3xTF32
     static constexpr int BN = 256, STAGES = 2, THREADS = 320, KB_PER_CHUNK = 2;
 };
+// CTA-pair variants (gemm_tc_pair): each CTA stages its 128 rows of A and
+// half (128 columns) of B per k-block, so a stage is a third smaller and
+// the ring deeper.
+template <int VARIANT> struct TcPairCfg;
+template <> struct TcPairCfg<1> {
+    static constexpr int STAGES = 6, THREADS = 320, KB_PER_CHUNK = 8;
+};
+template <> struct TcPairCfg<3> {
+    static constexpr int STAGES = 3, THREADS = 320, KB_PER_CHUNK = 2;
+};
 
 // Residual of the tf32 truncation: x - (x with the low 13 mantissa bits
 // cleared), exact in fp32; 0 for inf / NaN (whose hi part carries them).
@@ -136,8 +146,9 @@ __device__ __forceinline__ void tc_mma_tf32(u32 tmem_d, u64 adesc, u64 bdesc, u3
           "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
 }
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets row
-// (lane base + t), columns [col, col+32).
-__device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&r)[32]) {
+// (lane base + t), columns [col, col+32).  tmem_ld32_nowait issues the load
+// only; tmem_wait_ld waits for every load issued before it.
+__device__ __forceinline__ void tmem_ld32_nowait(u32 taddr, u32 (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
         "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
@@ -146,7 +157,18 @@ __device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&r)[32]) {
           "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// The wait names the loaded registers as operands so that no use of them can
+// be scheduled between the asynchronous load and its completion.
+__device__ __forceinline__ void tmem_wait_ld(u32 (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]) :: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld(u32 (&a)[32], u32 (&b)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]), "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]), "+r"(a[29]), "+r"(a[30]), "+r"(a[31]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31]) :: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(u32 taddr, u32 (&r)[32]) {
+    tmem_ld32_nowait(taddr, r);
+    tmem_wait_ld(r);
 }
 
 // UMMA shared-memory descriptor, version 1; lbo / sbo in bytes.
@@ -165,10 +187,11 @@ __device__ __forceinline__ u64 smem_desc(u32 addr, u32 lbo, u32 sbo, u32 layout)
     return d;
 }
 
-// Instruction descriptor: D f32, A/B tf32, majors, N, M=128.
-__device__ __forceinline__ u32 instr_desc(int a_mn, int b_mn, int n) {
+// Instruction descriptor: D f32, A/B tf32, majors, N, M (128, or 256 for
+// a CTA pair).
+__device__ __forceinline__ u32 instr_desc(int a_mn, int b_mn, int n, int m = BM) {
     return (1u << 4) | (2u << 7) | (2u << 10) | ((u32)a_mn << 15) | ((u32)b_mn << 16) |
-           ((u32)(n >> 3) << 17) | ((u32)(BM >> 4) << 24);
+           ((u32)(n >> 3) << 17) | ((u32)(m >> 4) << 24);
 }
 
 // Shared state of one CTA.
@@ -191,6 +214,45 @@ __device__ __forceinline__ bool wait(u32 bar, u32 parity, volatile Shared* sh, c
             return false;
         }
     }
+}
+
+__device__ __forceinline__ u32 cluster_rank() {
+    u32 r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrive on the mbarrier at the same shared-memory offset in CTA `rank` of
+// the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(u32 bar, u32 rank) {
+    u32 remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(bar), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+// TMA load into this CTA's shared memory whose completion is counted on the
+// pair leader's mbarrier (same offset); no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(u32 dst, const TmaDesc* map, u32 bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar & 0xFEFFFFFFu), "r"(x), "r"(y) : "memory");
+}
+__device__ __forceinline__ void tc_mma_tf32_pair(u32 tmem_d, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
+          "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
+}
+// Completion of the pair's prior MMAs signalled on the barrier at offset
+// `bar` in both CTAs of the pair (tcgen05.commit, not a load).
+__device__ __forceinline__ void tc_commit_pair(u32 bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}"
+        ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int& nb) {
@@ -420,6 +482,244 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     if (warp == 1) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+
+// CTA-pair (cta_group::2) variant.  A cluster of two CTAs on two SMs
+// computes a 256 x 256 output tile: CTA r owns rows [128r, 128r+128) of the
+// tile (its A tile and TMEM accumulator) and stages columns [128r, 128r+128)
+// of B; one tcgen05.mma.cta_group::2 (M=256, N=256, K=8) issued by the
+// leader (CTA 0) reads A from each CTA's shared memory and both halves of B,
+// so per SM a k-block moves 32 KB (1xTF32) instead of 48 KB.  Both CTAs'
+// TMA loads complete on the leader's FULL barrier; MMA completion is
+// committed to the barriers of both CTAs; the accumulate warps of both
+// CTAs release a TMEM chunk buffer by arriving on the leader's barrier.
+// Roles, chunked register accumulation, bounded waits as in gemm_tc.
+template <class Spec, int VARIANT>
+__device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
+    using namespace tc;
+    typedef TcPairCfg<VARIANT> Cfg;
+    constexpr int BN = 256, STAGES = Cfg::STAGES;
+    constexpr bool SPLIT = VARIANT == 3;
+    constexpr int KB_PER_CHUNK = Cfg::KB_PER_CHUNK;
+    constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB: this CTA's 128 rows
+    constexpr u32 B_BYTES = (BN / 2) * BK * 4;      // 16 KB: this CTA's half of B
+    constexpr u32 STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
+    constexpr u32 TMEM_COLS = 2 * BN;
+    constexpr int ACC_THREADS = 256;
+
+    extern __shared__ unsigned char smem_raw[];
+    const u32 raw_addr = smem_u32(smem_raw);
+    const u32 base = (raw_addr + 1023u) & ~1023u;
+    unsigned char* smem = smem_raw + (base - raw_addr);
+    const u32 bars = base + STAGES * STAGE_BYTES;
+    auto FULL = [&](int s) { return bars + 8u * s; };
+    auto EMPTY = [&](int s) { return bars + 8u * (STAGES + s); };
+    auto TFULL = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+    auto TEMPTY = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+    const u32 DRAIN = bars + 8u * (2 * STAGES + 4);
+    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5));
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const u32 cta = cluster_rank();
+    const int pair = (int)(blockIdx.x >> 1);
+    const int num_pairs = (int)(gridDim.x >> 1);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(FULL(s), 1);
+            mbar_init(EMPTY(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(TFULL(b), 1);
+            mbar_init(TEMPTY(b), 2 * ACC_THREADS);
+        }
+        mbar_init(DRAIN, 1);
+        sh->abort = 0u;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32((const void*)&sh->tmem_base)), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                                  // both CTAs' barriers exist
+    tc_fence_after();
+    const u32 tmem = sh->tmem_base;
+    const int k_blocks = (int)((g.K + BK - 1) / BK);
+    const int n_chunks = (k_blocks + KB_PER_CHUNK - 1) / KB_PER_CHUNK;
+
+    if (warp == 0) {
+        // ---------------------------------------- TMA producer (both CTAs) --
+        if (lane == 0) {
+            int s = 0;
+            u32 phase = 0;
+            u32 armed[STAGES];
+            for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
+            bool ok = true;
+            for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+                int mb, nb;
+                tile_coords(g, t, mb, nb);
+                const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
+                    const u32 a_dst = base + s * STAGE_BYTES;
+                    const u32 b_dst = a_dst + A_BYTES;
+                    if (cta == 0) {
+                        mbar_expect_tx(FULL(s), 2 * STAGE_BYTES);   // both CTAs' bytes
+                        armed[s] = phase;
+                    }
+                    const int k0 = kb * BK;
+#pragma unroll
+                    for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
+                        const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
+                        const TmaDesc* mbp = part ? &g.tmap_b_lo : &g.tmap_b;
+                        const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
+                        const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
+                        if (g.a_mn) {
+                            for (int j = 0; j < BM / 32; ++j)
+                                tma_load_2d_pair(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                        } else {
+                            tma_load_2d_pair(ad, ma, FULL(s), k0, m0);
+                        }
+                        if (g.b_mn) {
+                            for (int j = 0; j < (BN / 2) / 32; ++j)
+                                tma_load_2d_pair(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                        } else {
+                            tma_load_2d_pair(bd, mbp, FULL(s), k0, n0);
+                        }
+                    }
+                    if (++s == STAGES) { s = 0; phase ^= 1u; }
+                }
+            }
+            // Drain (bounded): the leader's FULL phases count both CTAs'
+            // copies; the peer waits until the MMAs released its last stages.
+            for (int i = 0; i < STAGES; ++i) {
+                const u64 t0 = now_ns();
+                if (cta == 0) {
+                    if (armed[i] == 0xFFFFFFFFu) continue;
+                    while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < g.timeout_ns) {}
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // --------------------------------------- MMA issuer (leader CTA) --
+        if (lane == 0 && cta == 0) {
+            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN, 2 * BM);
+            const u32 a_lbo = g.a_mn ? 32u * BK * 4u : 16u, b_lbo = g.b_mn ? 32u * BK * 4u : 16u;
+            const u32 a_sbo = g.a_mn ? 512u : 1024u, b_sbo = g.b_mn ? 512u : 1024u;
+            const u32 a_lt = g.a_mn ? 1u : 2u, b_lt = g.b_mn ? 1u : 2u;
+            int s = 0;
+            u32 phase = 0;
+            u32 chunk = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+                for (int c = 0; ok && c < n_chunks; ++c, ++chunk) {
+                    const int buf = (int)(chunk & 1u);
+                    const u32 use = (chunk >> 1) & 1u;
+                    if (!wait(TEMPTY(buf), use ^ 1u, sh, g, 2u)) { ok = false; break; }
+                    tc_fence_after();
+                    const u32 d = tmem + (u32)(buf * BN);
+                    const int kb_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                    for (int kb = c * KB_PER_CHUNK; kb < kb_end; ++kb) {
+                        if (!wait(FULL(s), phase, sh, g, 3u)) { ok = false; break; }
+                        tc_fence_after();
+                        const u32 a_hi = base + s * STAGE_BYTES;
+                        const u32 b_hi = a_hi + A_BYTES;
+                        const u32 a_lo = a_hi + A_BYTES + B_BYTES;
+                        const u32 b_lo = a_lo + A_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 8; ++kk) {
+                            const u32 ao = g.a_mn ? kk * 1024u : kk * 32u;
+                            const u32 bo = g.b_mn ? kk * 1024u : kk * 32u;
+                            const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
+                            const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
+                            const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                            tc_mma_tf32_pair(d, ah, bh, idesc, acc);
+                            if (SPLIT) {
+                                const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
+                                const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
+                                tc_mma_tf32_pair(d, ah, bl, idesc, 1u);
+                                tc_mma_tf32_pair(d, al, bh, idesc, 1u);
+                            }
+                        }
+                        tc_commit_pair(EMPTY(s));      // both CTAs' stage s is free
+                        if (++s == STAGES) { s = 0; phase ^= 1u; }
+                    }
+                    if (!ok) break;
+                    tc_commit_pair(TFULL(buf));        // both CTAs' partial sums ready
+                }
+            }
+            tc_commit_pair(DRAIN);
+            const u64 t0 = now_ns();
+            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < g.timeout_ns) {}
+        }
+    } else {
+        // ------------------------- accumulate + epilogue (both CTAs) --
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int row_in_tile = q * 32 + lane;
+        const u32 lane_addr = (u32)(q * 32) << 16;
+        typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
+        u32 chunk = 0;
+        bool ok = true;
+        for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+            float acc[128];
+#pragma unroll
+            for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
+            for (int c = 0; c < n_chunks; ++c, ++chunk) {
+                const int buf = (int)(chunk & 1u);
+                const u32 use = (chunk >> 1) & 1u;
+                const bool ready = wait(TFULL(buf), use, sh, g, 4u);
+                if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int j = 0; j < 4; j += 2) {
+                    u32 r0[32], r1[32];
+                    tmem_ld32_nowait(tmem + lane_addr + (u32)(buf * BN + half * 128 + 32 * j), r0);
+                    tmem_ld32_nowait(tmem + lane_addr + (u32)(buf * BN + half * 128 + 32 * (j + 1)), r1);
+                    tmem_wait_ld(r0, r1);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        acc[32 * j + e] = __fadd_rn(acc[32 * j + e], __uint_as_float(r0[e]));
+                        acc[32 * (j + 1) + e] = __fadd_rn(acc[32 * (j + 1) + e], __uint_as_float(r1[e]));
+                    }
+                }
+                tc_fence_before();
+                if (cta == 0) mbar_arrive(TEMPTY(buf));
+                else mbar_arrive_cluster(TEMPTY(buf), 0u);
+            }
+            if (!ok) break;
+            int mb, nb;
+            tile_coords(g, t, mb, nb);
+            const i64 i = (i64)mb * 2 * BM + (i64)cta * BM + row_in_tile;
+            const i64 n0 = (i64)nb * BN + half * 128;
+            if (i < g.M) {
+#pragma unroll
+                for (int v = 0; v < 128; v += 4) {
+                    const i64 j = n0 + v;
+                    if (j < g.N) {
+                        Vec4<typename Spec::Out> o;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, 0, i, j + e);
+                        st4(out + i * g.N + j, o);
+                    }
+                }
+            }
+        }
+    }
+
+    // ------------------------------------------------------- teardown --
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                                  // the peer is done with our barriers / TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }
 }
 

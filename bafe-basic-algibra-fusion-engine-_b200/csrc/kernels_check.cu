@@ -29,6 +29,12 @@ extern "C" __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1) check_g
 extern "C" __global__ void __launch_bounds__(bafe::TcCfg<1>::THREADS, 1) check_gemm_tc1(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc<CheckSpec, 1>(g);
 }
+extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) check_gemm_tc3_pair(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_pair<CheckSpec, 3>(g);
+}
+extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_tc1_pair(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_pair<CheckSpec, 1>(g);
+}
 extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
     bafe::transpose2d<float>(x, out, M, N);
 }

@@ -540,6 +540,7 @@ struct Lowerer {
             if (prec == "tf32" || prec == "3xtf32" || big) {
                 s.kind = StepKind::GemmTc;
                 s.tc_variant = prec == "tf32" ? 1 : 3;
+                s.tc_pair = opt.tc_pair;
             }
         }
 
@@ -608,14 +609,17 @@ struct Lowerer {
                 << "(const bafe::GemmArgs g) { bafe::gemm_exact<" << S_ << ", " << (s.direct ? "true" : "false")
                 << ">(g); }\n";
         } else {
-            src << "extern \"C\" __global__ void __launch_bounds__(bafe::TcCfg<" << s.tc_variant << ">::THREADS, 1) "
-                << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::gemm_tc<" << S_ << ", "
-                << s.tc_variant << ">(g); }\n";
+            const char* cfg = s.tc_pair ? "TcPairCfg" : "TcCfg";
+            const char* fn = s.tc_pair ? "gemm_tc_pair" : "gemm_tc";
+            src << "extern \"C\" __global__ void __launch_bounds__(bafe::" << cfg << "<" << s.tc_variant
+                << ">::THREADS, 1) " << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::" << fn << "<"
+                << S_ << ", " << s.tc_variant << ">(g); }\n";
         }
         char geo[256];
         snprintf(geo, sizeof(geo), " batch=%lld m=%lld n=%lld k=%lld a=%s b=%s", (long long)batch, (long long)M,
                  (long long)Nn, (long long)K, s.a_col ? "col" : "row", s.b_col ? "col" : "row");
-        std::string kindname = s.kind == StepKind::GemmTc ? (s.tc_variant == 1 ? "gemm.tc.tf32" : "gemm.tc.3xtf32")
+        std::string kindname = s.kind == StepKind::GemmTc ? std::string(s.tc_variant == 1 ? "gemm.tc.tf32" : "gemm.tc.3xtf32") +
+                                                                (s.tc_pair ? ".pair" : "")
                                                           : (s.direct ? "gemm.exact.direct" : "gemm.exact.chunk32");
         s.describe = kindname + geo + " epi=" + epi_desc + " -> " + bufname(s.dst);
         P.steps.push_back(s);

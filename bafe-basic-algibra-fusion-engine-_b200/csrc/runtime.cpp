@@ -310,7 +310,8 @@ int ensure_device_state(Plan& p, int dev, DeviceState*& out) {
                 return 5;
             }
             if (st.kind == StepKind::GemmTc) {
-                r = d.funcSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES, tc_smem_bytes(st.tc_variant));
+                r = d.funcSetAttribute(f, CU_FUNC_ATTRIBUTE_MAX_DYNAMIC_SHARED_SIZE_BYTES,
+                                       tc_smem_bytes(st.tc_variant, st.tc_pair));
                 if (r != CUDA_SUCCESS) {
                     set_error(5, "cuFuncSetAttribute(smem): " + cu_err(r));
                     d.moduleUnload(s->module);
@@ -484,6 +485,16 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
                 cfg.blockDimX = L.block; cfg.blockDimY = 1; cfg.blockDimZ = 1;
                 cfg.sharedMemBytes = L.smem;
                 cfg.hStream = (CUstream)stream;
+                CUlaunchAttribute attr;
+                memset(&attr, 0, sizeof(attr));
+                if (L.cluster > 1) {
+                    attr.id = CU_LAUNCH_ATTRIBUTE_CLUSTER_DIMENSION;
+                    attr.value.clusterDim.x = L.cluster;
+                    attr.value.clusterDim.y = 1;
+                    attr.value.clusterDim.z = 1;
+                    cfg.attrs = &attr;
+                    cfg.numAttrs = 1;
+                }
                 CUresult r = driver().launchKernelEx(&cfg, ds->fn[si], params, nullptr);
                 if (r != CUDA_SUCCESS) { set_error(7, "tensor-core GEMM launch failed: " + cu_err(r)); return 7; }
                 ++g_launch_count;

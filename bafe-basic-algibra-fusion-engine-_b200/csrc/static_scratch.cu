@@ -93,7 +93,7 @@ int setup_device(int dev, DeviceSetup*& out) {
             return fail(14, std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
         }
         e = cudaFuncSetAttribute(bafe_gemm_tc3_static_scratch, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 bafe_cuda::tc_smem_bytes(3));
+                                 bafe_cuda::tc_smem_bytes(3, false));
         if (e != cudaSuccess) {
             cudaGetLastError();
             return fail(14, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
@@ -152,6 +152,7 @@ extern "C" __attribute__((visibility("default"))) int bafe_cuda_gemm_3xtf32_stat
     s.a_col = a_col ? 1 : 0;
     s.b_col = b_col ? 1 : 0;
     s.tc_variant = 3;
+    s.tc_pair = false;
     bafe_cuda::TcLaunch L;
     std::string err;
     if (int rc = bafe_cuda::tc_prepare(s, A, B, a_lo, b_lo, out, {}, ds->sm_count, status, L, err))

@@ -35,8 +35,10 @@ static_assert(sizeof(TcArgsHost) == 704, "TcArgs layout");
 static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the launch block");
 
 int threads_of(int) { return 320; }
-int stages_of(int variant) { return variant == 3 ? 2 : 4; }
-int stage_bytes(int variant) { return (BM * BK * 4 + BN * BK * 4) * (variant == 3 ? 2 : 1); }
+int stages_of(int variant, bool pair) { return pair ? (variant == 3 ? 3 : 6) : (variant == 3 ? 2 : 4); }
+int stage_bytes(int variant, bool pair) {
+    return (BM * BK * 4 + (pair ? BN / 2 : BN) * BK * 4) * (variant == 3 ? 2 : 1);
+}
 
 }  // namespace
 
@@ -45,9 +47,9 @@ bool tc_kernel_enabled() {
     return !(e && *e && *e != '0');
 }
 
-int tc_smem_bytes(int variant) {
+int tc_smem_bytes(int variant, bool pair) {
     // alignment slack + stage ring + mbarriers + shared words
-    return 1024 + stages_of(variant) * stage_bytes(variant) + 256;
+    return 1024 + stages_of(variant, pair) * stage_bytes(variant, pair) + 256;
 }
 
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
@@ -86,7 +88,7 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     auto map_b = [&](CUtensorMap* m, const void* p) {
         if (s.b_col) {
             uint64_t dims[2] = {K, N}, strides[1] = {K * 4};
-            uint32_t box[2] = {32, (uint32_t)BN};
+            uint32_t box[2] = {32, (uint32_t)(s.tc_pair ? BN / 2 : BN)};
             return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 1, err);
         }
         uint64_t dims[2] = {N, K}, strides[1] = {N * 4};
@@ -108,7 +110,8 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     h.err = err_word;
     h.a_mn = s.a_col ? 1 : 0;
     h.b_mn = s.b_col ? 0 : 1;
-    h.num_m = (int)((s.M + BM - 1) / BM);
+    const int tile_m = s.tc_pair ? 2 * BM : BM;   // a CTA pair covers 256 rows
+    h.num_m = (int)((s.M + tile_m - 1) / tile_m);
     h.num_n = (int)((s.N + BN - 1) / BN);
     int64_t tiles = (int64_t)h.num_m * h.num_n;
     if (tiles > (1LL << 30)) {
@@ -120,9 +123,16 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     const char* to = getenv("BAFE_TC_TIMEOUT_MS");
     h.timeout_ns = (unsigned long long)(to ? atof(to) : 2000.0) * 1000000ull;
     memcpy(L.args, &h, sizeof(h));
-    L.grid = (unsigned)(tiles < sm_count ? tiles : sm_count);
+    if (s.tc_pair) {
+        const int64_t pairs = sm_count / 2;
+        L.grid = (unsigned)(2 * (tiles < pairs ? tiles : pairs));
+        L.cluster = 2;
+    } else {
+        L.grid = (unsigned)(tiles < sm_count ? tiles : sm_count);
+        L.cluster = 1;
+    }
     L.block = (unsigned)threads_of(s.tc_variant);
-    L.smem = (unsigned)tc_smem_bytes(s.tc_variant);
+    L.smem = (unsigned)tc_smem_bytes(s.tc_variant, s.tc_pair);
     return 0;
 }
 

@@ -8,10 +8,11 @@ namespace bafe_cuda {
 struct TcLaunch {
     alignas(64) unsigned char args[1024];
     unsigned grid = 0, block = 0, smem = 0;
+    unsigned cluster = 1;          // CTAs per cluster (2 for the CTA-pair kernel)
 };
 
 bool tc_kernel_enabled();
-int tc_smem_bytes(int variant);
+int tc_smem_bytes(int variant, bool pair = false);
 // a_lo / b_lo: 3xTF32 residual operands (same layouts as a / b), or null.
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,

@@ -314,9 +314,11 @@ class Ctx:
 def bench_gemm(c: Ctx) -> dict:
     import bafe_b200 as bafe
     torch, args = c.torch, c.args
+    from bafe_b200.parallel import broadcast_resident, row_panels
     S = args.gemm_size
     std = 1.0 / math.sqrt(S)
-    rows = S // c.world
+    r0, r1 = row_panels(S, c.world)[c.rank]
+    rows = r1 - r0
     A = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
     C = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
     B = torch.empty(S, S, device=c.dev)
@@ -327,7 +329,7 @@ def bench_gemm(c: Ctx) -> dict:
         c.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        c.dist.broadcast(B, src=0)
+        broadcast_resident(B, c.dist, src=0)
         e1.record()
         torch.cuda.synchronize()
         bcast_ms = c.max(e0.elapsed_time(e1))
@@ -386,8 +388,10 @@ def bench_gemm(c: Ctx) -> dict:
 def bench_ew(c: Ctx) -> dict:
     import bafe_b200 as bafe
     torch, args = c.torch, c.args
+    from bafe_b200.parallel import element_ranges
     n_total = args.ew_elements
-    n_local = n_total // c.world
+    e0_, e1_ = element_ranges(n_total, c.world)[c.rank]
+    n_local = e1_ - e0_
     X, Y, Z = (torch.rand(n_local, device=c.dev, generator=c.gen) * 2 - 1 for _ in range(3))
     O = torch.empty(n_local, device=c.dev)
     k = bafe.compile_graph(ew_graph(n_local))
