@@ -125,6 +125,20 @@ class Kernel:
     def input_bytes(self, i: int) -> int:
         return int(lib.bafe_cuda_plan_input_bytes(self.plan, i))
 
+    def row_split(self):
+        """(rows, per-input bytes per row, output bytes per row) when host
+        calls stream this plan in row panels (0 bytes: input read whole),
+        else None."""
+        rows = ctypes.c_int64()
+        out_rb = ctypes.c_int64()
+        in_rb = (ctypes.c_int64 * max(self.n_inputs, 1))()
+        rc = lib.bafe_cuda_plan_row_split(self.plan, ctypes.byref(rows), in_rb, self.n_inputs, ctypes.byref(out_rb))
+        if rc < 0:
+            raise RuntimeError("unknown plan")
+        if rc == 0:
+            return None
+        return int(rows.value), [int(in_rb[i]) for i in range(self.n_inputs)], int(out_rb.value)
+
     def call_host_ptrs(self, ptrs: Sequence[int]) -> None:
         """Call the ABI function (host pointers, synchronous) and raise on error."""
         lib.bafe_cuda_clear_error()

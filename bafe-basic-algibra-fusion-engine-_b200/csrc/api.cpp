@@ -24,6 +24,7 @@ Options& options() {
         if (const char* p = getenv("BAFE_GEMM_PRECISION")) o.gemm_precision = p;
         if (const char* d = getenv("BAFE_DEVICE")) o.device = atoi(d);
         if (const char* t = getenv("BAFE_TC_PAIR")) o.tc_pair = atoi(t) != 0;
+        if (const char* h = getenv("BAFE_HOST_PANELS")) o.host_panels = strcmp(h, "auto") == 0 ? -1 : atoi(h);
     }
     return o;
 }
@@ -262,6 +263,18 @@ BAFE_API int64_t bafe_cuda_plan_input_bytes(int plan, int i) {
     return p->in_bytes[i];
 }
 
+BAFE_API int bafe_cuda_plan_row_split(int plan, int64_t* rows, int64_t* in_row_bytes, int n_inputs,
+                                      int64_t* out_row_bytes) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) return -1;
+    if (rows) *rows = p->stream_ok ? p->stream_rows : 0;
+    if (out_row_bytes) *out_row_bytes = p->stream_ok ? p->out_rb : 0;
+    for (int k = 0; in_row_bytes && k < n_inputs && k < p->n_inputs; ++k)
+        in_row_bytes[k] = p->stream_ok ? p->in_rb[k] : 0;
+    return p->stream_ok ? 1 : 0;
+}
+
 BAFE_API int bafe_cuda_run_device(int plan, void* const* ptrs, int n_ptrs, void* stream) {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     Plan* p = plan_ptr(plan);
@@ -300,6 +313,14 @@ BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
         o.tc_pair = v == "1";
         return 0;
     }
+    if (k == "host_panels") {
+        if (v == "auto") { o.host_panels = -1; return 0; }
+        char* end = nullptr;
+        long n = strtol(value, &end, 10);
+        if (!end || *end || n < 0 || n > 4096) return -1;
+        o.host_panels = (int)n;
+        return 0;
+    }
     if (k == "device") {
         char* end = nullptr;
         long d = strtol(value, &end, 10);
@@ -318,6 +339,7 @@ BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
     if (k == "gemm_precision") v = o.gemm_precision;
     else if (k == "device") v = std::to_string(o.device);
     else if (k == "tc_pair") v = o.tc_pair ? "1" : "0";
+    else if (k == "host_panels") v = o.host_panels < 0 ? "auto" : std::to_string(o.host_panels);
     else return -1;
     if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());
     return 0;

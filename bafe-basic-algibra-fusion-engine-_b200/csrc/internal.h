@@ -76,6 +76,7 @@ struct Options {
     std::string gemm_precision = "auto";   // auto | 3xtf32 | tf32 | exact
     int device = -1;                        // -1: current device
     bool tc_pair = true;                    // tensor-core GEMM on CTA pairs (cta_group::2)
+    int host_panels = -1;                   // host calls: -1 auto, 0/1 off, n: n row panels
 };
 Options& options();
 
@@ -109,6 +110,13 @@ struct Step {
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
     bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
     std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
+    // Row streaming of host calls (analyse_row_streaming): the step runs
+    // once per row panel of the output (panel) or once per call; buffers
+    // with a nonzero byte count per row are offset to the panel's first row.
+    bool panel = false;
+    int64_t row_elems = 0;         // Ew: elements per output row
+    int64_t dst_rb = 0;
+    std::vector<int64_t> src_rb, aux_rb;
     // Transpose2d (output M x N), Gather, Reduce
     int64_t gdims[8] = {0}, gstride[8] = {0};
     int grank = 0;
@@ -129,6 +137,13 @@ struct Plan {
     int64_t out_bytes = 0;
     std::vector<int64_t> tmp_bytes;
     std::vector<Step> steps;
+    // Row streaming: host calls may copy the row-split inputs, run the
+    // panel steps and copy the output back panel by panel on three streams.
+    bool stream_ok = false;
+    int64_t stream_rows = 0;       // rows of the output (leading dimension)
+    int64_t stream_align = 1;      // panel boundaries are multiples of this
+    std::vector<int64_t> in_rb;    // bytes per output row of each input (0: whole)
+    int64_t out_rb = 0;
     std::string source;            // generated CUDA for every step's kernel
     std::string source_hash;       // key of the cubin
     std::string cubin;             // compiled image (kept for lazy per-device loads)
@@ -139,6 +154,9 @@ struct Plan {
 // Lower a parsed graph into steps + generated source.  Host-only: needs no
 // GPU.  Returns 0 or a nonzero code with a message in err.
 int lower_graph(const Graph& g, const Options& opt, Plan& plan, std::string& err);
+// Decides which steps and buffers split by output row (fills the row
+// streaming fields of the plan and its steps).
+void analyse_row_streaming(Plan& plan, const Shape& out_shape);
 
 // Embedded kernel headers (generated at build time from csrc/kernels/*.cuh).
 struct EmbeddedHeader { const char* name; const char* text; };

@@ -598,6 +598,12 @@ struct Lowerer {
         src << "    return " << store_convert(out_store, rv_dtype, rv) << ";\n  }\n};\n";
         for (auto& l : leaves) s.srcs.push_back(buf[l.node]);
         s.n_epi = (int)leaves.size();
+        s.src_esize = {dtype_size(buf_dtype[g.ch[0]]), dtype_size(buf_dtype[g.ch[1]])};
+        s.src_row = {false, false};
+        for (auto& l : leaves) {
+            s.src_esize.push_back(dtype_size(buf_dtype[l.node]));
+            s.src_row.push_back(l.access == ROW);
+        }
         if (s.kind == StepKind::GemmTc && s.tc_variant == 3) {
             // 3xTF32 residual operands lo = x - trunc_tf32(x), written once
             // per call by a streaming pre-pass into plan scratch.
@@ -957,6 +963,7 @@ struct Lowerer {
         std::ostringstream d;
         for (auto& s : P.steps) d << s.describe << "\n";
         P.describe = d.str();
+        analyse_row_streaming(P, N(G.root).shape);
         return 0;
     }
 };

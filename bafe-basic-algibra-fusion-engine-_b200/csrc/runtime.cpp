@@ -264,7 +264,10 @@ struct DeviceState {
     std::vector<void*> tmp;
     std::vector<void*> in_stage;
     void* out_stage = nullptr;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;      // host calls: kernels
+    cudaStream_t h2d = nullptr;         // host calls: input copies (row streaming)
+    cudaStream_t d2h = nullptr;         // host calls: output copies (row streaming)
+    std::vector<cudaEvent_t> events;    // row streaming: per-panel hand-offs
 };
 
 // One device word per GPU that kernels with bounded waits report a timeout
@@ -384,28 +387,24 @@ struct GatherArgsHost {
 };
 static_assert(sizeof(GatherArgsHost) == 144, "GatherArgs layout");
 
-}  // namespace
-
-int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
-    if (n_ptrs != p.n_inputs + 1) {
-        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
-        return 8;
-    }
-    int dev = 0;
-    cudaError_t ce = cudaGetDevice(&dev);
-    if (ce != cudaSuccess) {
-        cudaGetLastError();
-        set_error(4, std::string("no CUDA device available (") + cudaGetErrorString(ce) + ")");
-        return 4;
-    }
-    DeviceState* ds = nullptr;
-    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+int ensure_tmps(Plan& p, DeviceState* ds) {
     if (ds->tmp.size() != p.tmp_bytes.size()) {
         ds->tmp.assign(p.tmp_bytes.size(), nullptr);
         for (size_t t = 0; t < p.tmp_bytes.size(); ++t)
             if (int rc = alloc(&ds->tmp[t], p.tmp_bytes[t])) return rc;
     }
-    cudaStream_t stream = (cudaStream_t)stream_v;
+    return 0;
+}
+
+// Which steps one pass of run_steps launches: all of them over the whole
+// problem, only the once-per-call steps, or the per-panel steps over output
+// rows [r0, r0 + rows).
+struct Pass {
+    enum Kind { All, Once, Panel } kind = All;
+    int64_t r0 = 0, rows = 0;
+};
+
+int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t stream, const Pass& pass) {
     auto ptr_of = [&](const BufRef& b) -> void* {
         switch (b.kind) {
             case BufRef::In: return ptrs[b.idx];
@@ -413,9 +412,18 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
             default: return ptrs[p.n_inputs];
         }
     };
+    const bool cut = pass.kind == Pass::Panel;
+    // a buffer of a panel step, moved to the panel's first row
+    auto at_row = [&](void* base, int64_t row_bytes) -> void* {
+        return cut && row_bytes ? static_cast<void*>(static_cast<char*>(base) + pass.r0 * row_bytes) : base;
+    };
     for (size_t si = 0; si < p.steps.size(); ++si) {
         Step& s = p.steps[si];
-        void* dst = ptr_of(s.dst);
+        if (pass.kind == Pass::Once && s.panel) continue;
+        if (pass.kind == Pass::Panel && !s.panel) continue;
+        void* dst = at_row(ptr_of(s.dst), s.dst_rb);
+        const int64_t n_run = cut ? pass.rows * s.row_elems : s.n;
+        const int64_t m_run = cut ? pass.rows : s.M;
         switch (s.kind) {
             case StepKind::Zero: {
                 if (s.dst_bytes > 0) {
@@ -425,11 +433,11 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
                 break;
             }
             case StepKind::Ew: {
-                if (s.n == 0) break;
+                if (n_run == 0) break;
                 std::vector<uint64_t> args;
                 bool vec = ds->fn_vec[si] != nullptr;
                 for (size_t k = 0; k < s.srcs.size(); ++k) {
-                    void* q = ptr_of(s.srcs[k]);
+                    void* q = at_row(ptr_of(s.srcs[k]), s.src_rb.empty() ? 0 : s.src_rb[k]);
                     args.push_back((uint64_t)(uintptr_t)q);
                     uintptr_t need = s.src_esize[k] == 2 ? 8 : 16;
                     if ((uintptr_t)q % need) vec = false;
@@ -437,44 +445,54 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
                 }
                 if ((uintptr_t)dst % (s.dst_esize == 2 ? 8 : 16)) vec = false;
                 args.push_back((uint64_t)(uintptr_t)dst);
-                args.push_back((uint64_t)s.n);
+                args.push_back((uint64_t)n_run);
                 args.push_back((uint64_t)s.ncols);
                 void* params[] = {args.data()};
-                int64_t units = vec ? s.n / 4 : s.n;
+                int64_t units = vec ? n_run / 4 : n_run;
                 if (int rc = launch(vec ? ds->fn_vec[si] : ds->fn[si], grid_for(units, dev), 1, 1, 256, 1, 1, 0,
                                     stream, params))
                     return rc;
                 break;
             }
             case StepKind::GemmExact: {
-                if (s.M == 0 || s.N == 0 || s.batch == 0) break;
+                if (m_run == 0 || s.N == 0 || s.batch == 0) break;
                 GemmArgsHost g;
                 memset(&g, 0, sizeof(g));
-                g.a = ptr_of(s.srcs[0]);
+                g.a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
                 g.b = ptr_of(s.srcs[1]);
                 g.out = dst;
-                g.M = s.M; g.N = s.N; g.K = s.K; g.batch = s.batch;
+                g.M = m_run; g.N = s.N; g.K = s.K; g.batch = s.batch;
                 g.a_bstride = s.a_bstride; g.b_bstride = s.b_bstride; g.o_bstride = s.o_bstride;
                 g.a_col = s.a_col; g.b_col = s.b_col;
-                for (int k = 0; k < s.n_epi; ++k) g.ep[k] = ptr_of(s.srcs[2 + k]);
+                for (int k = 0; k < s.n_epi; ++k)
+                    g.ep[k] = at_row(ptr_of(s.srcs[2 + k]), s.src_rb.empty() ? 0 : s.src_rb[2 + k]);
                 void* params[] = {&g};
-                if (s.batch > 65535 || (s.M + 63) / 64 > 65535) { set_error(8, "GEMM grid too large"); return 8; }
-                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 63) / 64), (unsigned)((s.M + 63) / 64),
+                if (s.batch > 65535 || (m_run + 63) / 64 > 65535) { set_error(8, "GEMM grid too large"); return 8; }
+                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 63) / 64), (unsigned)((m_run + 63) / 64),
                                     (unsigned)s.batch, 256, 1, 1, 0, stream, params))
                     return rc;
                 break;
             }
             case StepKind::GemmTc: {
                 std::vector<const void*> ep;
-                for (int k = 0; k < s.n_epi; ++k) ep.push_back(ptr_of(s.srcs[2 + k]));
+                for (int k = 0; k < s.n_epi; ++k)
+                    ep.push_back(at_row(ptr_of(s.srcs[2 + k]), s.src_rb.empty() ? 0 : s.src_rb[2 + k]));
                 unsigned* err_word = device_error_word(dev);
                 if (!err_word) { set_error(6, "cannot allocate the device error word"); return 6; }
                 TcLaunch L;
                 std::string err;
-                const void* a_lo = s.aux.size() > 0 ? ptr_of(s.aux[0]) : nullptr;
+                const void* a_lo = s.aux.size() > 0 ? at_row(ptr_of(s.aux[0]), s.aux_rb.empty() ? 0 : s.aux_rb[0]) : nullptr;
                 const void* b_lo = s.aux.size() > 1 ? ptr_of(s.aux[1]) : nullptr;
-                if (int rc = tc_prepare(s, ptr_of(s.srcs[0]), ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev),
-                                        err_word, L, err)) {
+                const void* a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
+                int rc = 0;
+                if (cut) {
+                    Step t = s;
+                    t.M = m_run;
+                    rc = tc_prepare(t, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, L, err);
+                } else {
+                    rc = tc_prepare(s, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, L, err);
+                }
+                if (rc) {
                     set_error(rc, err);
                     return rc;
                 }
@@ -539,6 +557,26 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
     return 0;
 }
 
+}  // namespace
+
+int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
+    if (n_ptrs != p.n_inputs + 1) {
+        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
+        return 8;
+    }
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, std::string("no CUDA device available (") + cudaGetErrorString(ce) + ")");
+        return 4;
+    }
+    DeviceState* ds = nullptr;
+    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+    if (int rc = ensure_tmps(p, ds)) return rc;
+    return run_steps(p, ds, dev, ptrs, (cudaStream_t)stream_v, Pass());
+}
+
 // A kernel whose bounded wait expired wrote a nonzero code into the
 // device's error word: report it (the output is not valid) and reset it.
 // The caller has synchronised the work in question.
@@ -571,6 +609,129 @@ int synchronize_current_device() {
     }
     return check_device_error_word(dev);
 }
+
+namespace {
+
+// Number of row panels a host call of plan p is split into (1 = not split).
+int host_panel_count(const Plan& p) {
+    if (!p.stream_ok) return 1;
+    const int want = options().host_panels;
+    if (want == 0 || want == 1) return 1;
+    const int64_t R = p.stream_rows, align = p.stream_align;
+    const int64_t most = R / align;   // every panel but the last has >= align rows
+    if (most < 2) return 1;
+    int n = want;
+    if (want < 0) {
+        // Auto: split when the row-split traffic is large enough for the
+        // copy / compute overlap to pay for the extra launches.
+        int64_t per_row = p.out_rb;
+        for (int64_t b : p.in_rb) per_row += b;
+        if (R * per_row < (int64_t(64) << 20)) return 1;
+        n = 8;
+    }
+    return (int)(n < most ? n : most);
+}
+
+int sync_stream(cudaStream_t st) {
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(9, std::string("device error: ") + cudaGetErrorString(e));
+        return 9;
+    }
+    return 0;
+}
+
+int copy_async(void* dst, const void* src, int64_t bytes, cudaStream_t st, const char* what) {
+    if (bytes <= 0) return 0;
+    cudaError_t e = cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDefault, st);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(7, std::string(what) + ": " + cudaGetErrorString(e));
+        return 7;
+    }
+    return 0;
+}
+
+// Row-streamed host call.  h2d stream: whole inputs, then each panel's rows
+// of the split inputs; compute stream: the once-per-call steps after the
+// whole inputs, then each panel's steps after its rows arrived; d2h stream:
+// each panel's output rows after its steps.  All copies of one direction
+// are issued before the other's, so with pageable host memory (whose copies
+// the driver makes synchronous) the input copies still overlap the kernels.
+int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels) {
+    const int64_t R = p.stream_rows, align = p.stream_align;
+    int64_t rows_per = (R + panels - 1) / panels;
+    rows_per = (rows_per + align - 1) / align * align;
+    panels = (int)((R + rows_per - 1) / rows_per);
+    for (cudaStream_t* st : {&ds->h2d, &ds->d2h}) {
+        if (!*st && cudaStreamCreateWithFlags(st, cudaStreamNonBlocking) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(6, "cudaStreamCreate failed");
+            return 6;
+        }
+    }
+    const size_t n_events = 2 * (size_t)panels + 1;
+    while (ds->events.size() < n_events) {
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(6, "cudaEventCreate failed");
+            return 6;
+        }
+        ds->events.push_back(ev);
+    }
+    cudaEvent_t whole = ds->events[0];
+    auto in_done = [&](int i) { return ds->events[1 + 2 * i]; };
+    auto run_done = [&](int i) { return ds->events[2 + 2 * i]; };
+    std::vector<void*> dptrs(ds->in_stage);
+    dptrs.push_back(ds->out_stage);
+    int rc = 0;
+    auto fail = [&](int code) {
+        cudaStreamSynchronize(ds->h2d);
+        cudaStreamSynchronize(ds->stream);
+        cudaStreamSynchronize(ds->d2h);
+        cudaGetLastError();
+        return code;
+    };
+
+    // inputs every panel reads whole
+    for (int k = 0; k < p.n_inputs && !rc; ++k)
+        if (p.in_rb[k] == 0) rc = copy_async(ds->in_stage[k], ptrs[k], p.in_bytes[k], ds->h2d, "host-to-device copy");
+    if (rc) return fail(rc);
+    cudaEventRecord(whole, ds->h2d);
+    cudaStreamWaitEvent(ds->stream, whole, 0);
+    if ((rc = run_steps(p, ds, ds->device, dptrs.data(), ds->stream, Pass{Pass::Once, 0, 0}))) return fail(rc);
+
+    for (int i = 0; i < panels; ++i) {
+        const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
+        for (int k = 0; k < p.n_inputs && !rc; ++k) {
+            const int64_t b = p.in_rb[k];
+            if (b == 0) continue;
+            rc = copy_async(static_cast<char*>(ds->in_stage[k]) + r0 * b, static_cast<const char*>(ptrs[k]) + r0 * b,
+                            rows * b, ds->h2d, "host-to-device copy");
+        }
+        if (rc) return fail(rc);
+        cudaEventRecord(in_done(i), ds->h2d);
+        cudaStreamWaitEvent(ds->stream, in_done(i), 0);
+        if ((rc = run_steps(p, ds, ds->device, dptrs.data(), ds->stream, Pass{Pass::Panel, r0, rows})))
+            return fail(rc);
+        cudaEventRecord(run_done(i), ds->stream);
+    }
+    for (int i = 0; i < panels; ++i) {
+        const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
+        cudaStreamWaitEvent(ds->d2h, run_done(i), 0);
+        if ((rc = copy_async(static_cast<char*>(ptrs[p.n_inputs]) + r0 * p.out_rb,
+                             static_cast<char*>(ds->out_stage) + r0 * p.out_rb, rows * p.out_rb, ds->d2h,
+                             "device-to-host copy")))
+            return fail(rc);
+    }
+    for (cudaStream_t st : {ds->h2d, ds->stream, ds->d2h})
+        if ((rc = sync_stream(st))) return fail(rc);
+    return check_device_error_word(ds->device);
+}
+
+}  // namespace
 
 int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
     if (n_ptrs != p.n_inputs + 1) {
@@ -605,6 +766,9 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
             if (int rc = alloc(&ds->in_stage[k], p.in_bytes[k])) return rc;
         if (int rc = alloc(&ds->out_stage, p.out_bytes)) return rc;
     }
+    if (int rc = ensure_tmps(p, ds)) return rc;
+    const int panels = host_panel_count(p);
+    if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels);
     for (int k = 0; k < p.n_inputs; ++k) {
         if (p.in_bytes[k] == 0) continue;
         cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], ptrs[k], (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
@@ -640,6 +804,8 @@ void release_plan_device_state(Plan& p) {
         for (void* t : s->tmp) if (t) cudaFree(t);
         for (void* t : s->in_stage) if (t) cudaFree(t);
         if (s->out_stage) cudaFree(s->out_stage);
+        for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
+        for (cudaEvent_t ev : s->events) cudaEventDestroy(ev);
         if (s->stream) cudaStreamDestroy(s->stream);
         if (s->module && d.ok) d.moduleUnload(s->module);
         delete s;

@@ -156,6 +156,15 @@ int bafe_cuda_plan_describe(int plan, char *buf, size_t buf_size);
 int64_t bafe_cuda_plan_output_bytes(int plan);
 int64_t bafe_cuda_plan_input_bytes(int plan, int i);
 
+/* Row split of a plan for streamed host calls: returns 1 and fills *rows
+ * (output rows), in_row_bytes[0..n_inputs) (bytes per output row of each
+ * input; 0 = the input is read whole) and *out_row_bytes when host calls
+ * can run the plan in row panels, 0 when they run it in one piece, -1 for
+ * an unknown plan.  Extension: the reference runs every kernel in one
+ * piece. */
+int bafe_cuda_plan_row_split(int plan, int64_t *rows, int64_t *in_row_bytes, int n_inputs,
+                             int64_t *out_row_bytes);
+
 /* Run a plan on device-resident buffers: ptrs[0..n_inputs-1] are the
  * inputs, ptrs[n_inputs] the output, all device pointers on the current
  * device; `stream` is a cudaStream_t (NULL = the legacy default stream).
@@ -181,12 +190,23 @@ int bafe_cuda_synchronize(void);
 int bafe_cuda_last_error(char *buf, size_t buf_size);
 void bafe_cuda_clear_error(void);
 
-/* Backend options (strings, process-wide, read when a plan is built):
+/* Backend options (strings, process-wide):
  *   "gemm_precision": "auto" (default) | "3xtf32" | "tf32" | "exact"
- *   "device":         CUDA device ordinal used by new plans (default:
- *                     the current device)
- * Environment variables BAFE_GEMM_PRECISION and BAFE_DEVICE set the
- * initial values.  Returns 0, or -1 for an unknown key or value. */
+ *                     (read when a plan is built)
+ *   "tc_pair":        "1" (default): tensor-core GEMMs run on CTA pairs
+ *                     (256x256 tiles over two SMs); "0": one CTA per tile
+ *                     (read when a plan is built)
+ *   "host_panels":    "auto" (default) | "0" | n: host-pointer calls of a
+ *                     row-separable plan copy, compute and copy back in n
+ *                     row panels on three streams, overlapping the copies
+ *                     with the kernels; auto = 8 panels when the row-split
+ *                     bytes exceed 64 MiB; 0 or 1 = one piece (read at
+ *                     each call)
+ *   "device":         CUDA device ordinal used by host-pointer calls
+ *                     (default: the current device)
+ * Environment variables BAFE_GEMM_PRECISION, BAFE_TC_PAIR,
+ * BAFE_HOST_PANELS and BAFE_DEVICE set the initial values.  Returns 0, or
+ * -1 for an unknown key or value. */
 int bafe_cuda_set_option(const char *key, const char *value);
 int bafe_cuda_get_option(const char *key, char *buf, size_t buf_size);
 

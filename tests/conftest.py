@@ -46,6 +46,7 @@ def _clear_plans():
     import bafe_b200
     bafe_b200.jit_clear()
     bafe_b200.set_option("gemm_precision", "auto")
+    bafe_b200.set_option("host_panels", "auto")
     yield
 
 
