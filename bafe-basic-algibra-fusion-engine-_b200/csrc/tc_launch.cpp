@@ -119,7 +119,12 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
         return 12;
     }
     h.num_tiles = (int)tiles;
-    h.group_m = 16;
+    // Tiles are walked in groups of group_m M-tiles (all N-tiles of a group
+    // before the next).  One wave of concurrent tiles then reads about
+    // group_m A panels and waves/group_m B panels; their sum is smallest for
+    // a square footprint: 8 x 9.25 for 74 CTA pairs, 16 x 9.25 for 148 CTAs
+    // (whose B panels are twice as wide as their A panels).
+    h.group_m = s.tc_pair ? 8 : 16;
     const char* to = getenv("BAFE_TC_TIMEOUT_MS");
     h.timeout_ns = (unsigned long long)(to ? atof(to) : 2000.0) * 1000000ull;
     memcpy(L.args, &h, sizeof(h));

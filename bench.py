@@ -70,11 +70,13 @@ def parse():
 
 
 def peaks():
+    """(hbm GB/s, bf16 burst TFLOP/s, bf16 sustained TFLOP/s, source)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
-    return 6650.0, 1590.0, "fallback"
+        burst = d.get("bf16_tflops", 1590.0)
+        return d.get("hbm_gbs", 6650.0), burst, d.get("bf16_tflops_sustained", burst), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
 
 
 # ------------------------------------------------------------- clocks --
@@ -296,7 +298,7 @@ class Ctx:
             import torch.distributed as dist_mod
             dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
             self.dist = dist_mod
-        self.hbm_peak, self.bf16_peak, self.peak_src = peaks()
+        self.hbm_peak, self.bf16_peak, self.bf16_sustained, self.peak_src = peaks()
         self.gen = torch.Generator(device=self.dev).manual_seed(1234 + self.rank)
 
     def barrier(self):
@@ -350,8 +352,12 @@ def bench_gemm(c: Ctx) -> dict:
     kern_ms = statistics.mean(per)
     achieved = 2.0 * rows * S * S / (kern_ms * 1e-3) / 1e12
     tc3 = "3xtf32" in plan
-    tf32_peak = c.bf16_peak / 2.0
-    peak = tf32_peak / 3.0 if tc3 else tf32_peak
+    # The timed region is a long back-to-back loop of GEMMs (the power cap
+    # holds the clock down), so the sustained bf16 figure is the basis; the
+    # burst-based fraction is reported beside it.
+    div = 2.0 * (3.0 if tc3 else 1.0)
+    peak = c.bf16_sustained / div
+    peak_burst = c.bf16_peak / div
     res = {
         "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C))",
         "value": round(flops_total / (ms_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
@@ -363,8 +369,11 @@ def bench_gemm(c: Ctx) -> dict:
                    "plan": plan, "precision_option": args.precision},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(f"gemm_{S}"),
-                     "peak_basis": f"{c.peak_src} bf16 {c.bf16_peak} TFLOP/s / 2 (tf32 rate)"
-                                   + (" / 3 (three products)" if tc3 else "")},
+                     "peak_basis": f"{c.peak_src} sustained bf16 {c.bf16_sustained} TFLOP/s / 2 (tf32 rate)"
+                                   + (" / 3 (three products)" if tc3 else ""),
+                     "frac_of_burst": round(achieved / peak_burst, 4),
+                     "achieved_over": "CUDA events around each step of the plan (tf32 residual pre-passes + GEMM)"
+                                      if tc3 else "CUDA events around each step of the plan"},
         "gpu_launches": launches, "clocks": clocks, "b_broadcast_ms": round(bcast_ms, 3),
         "compile_s": round(t_compile, 2),
     }
