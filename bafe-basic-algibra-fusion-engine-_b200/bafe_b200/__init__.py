@@ -306,11 +306,20 @@ def _layout_of(a: np.ndarray) -> str:
 
 
 class JittedFunction:
-    """A traced function compiled by the B200 backend (mirrors __init__.py:310-545)."""
+    """A traced function compiled by the B200 backend (mirrors __init__.py:310-545).
 
-    def __init__(self, fn: Callable):
+    With autotune=True each call past the warm-up is timed on the DEVICE
+    (CUDA events around the plan's kernels, copies excluded), logged with
+    the graph's features and the plan's roofline prediction, and the
+    learned model is refitted every refit_threshold records, after which
+    the compiled plans are dropped so the next call re-plans
+    (__init__.py:386-430 times by wall clock around the host call)."""
+
+    def __init__(self, fn: Callable, autotune: bool = False):
         self._fn = fn
         self._compiled: dict = {}
+        self._autotune = bool(autotune)
+        self._call_count: dict = {}
         functools.update_wrapper(self, fn)
 
     def kernel_for(self, *args: np.ndarray) -> Kernel:
@@ -336,7 +345,31 @@ class JittedFunction:
             keep.append(a)
             ptrs.append(a.ctypes.data)
         out = np.zeros(k.out_shape, dtype=k.out_dtype)
-        k.call_host_ptrs(ptrs + [out.ctypes.data])
+        call = ptrs + [out.ctypes.data]
+        if not self._autotune:
+            k.call_host_ptrs(call)
+            return out
+        key = tuple((a.shape, str(a.dtype), _layout_of(a)) for a in args)
+        cfg = lib.bafe_cuda_autotune_get_config()
+        n = self._call_count.get(key, 0) + 1
+        self._call_count[key] = n
+        if n <= cfg.warmup_calls:
+            k.call_host_ptrs(call)
+            return out
+        iters = cfg.timing_iters if cfg.timing_iters > 0 else 1
+        total = 0.0
+        for _ in range(iters):
+            k.call_host_ptrs(call)
+            total += lib.bafe_cuda_plan_last_device_ms(k.plan)
+        features = (ctypes.c_double * _binding.BAFE_NUM_FEATURES)()
+        lib.bafe_cuda_profiling_extract_features(ctypes.byref(k.graph), features)
+        lib.bafe_cuda_profiling_add(graph_hash(k.graph).encode(), features, lib.bafe_cuda_plan_predict_ms(k.plan),
+                                    total / iters, k.plan)
+        log = lib.bafe_cuda_profiling_get_log().contents
+        if cfg.refit_threshold > 0 and log.n > 0 and log.n % cfg.refit_threshold == 0:
+            lib.bafe_cuda_profiling_refit()
+            self._compiled.clear()
+            lib.bafe_cuda_jit_invalidate_memory_cache()
         return out
 
     def _compile(self, args: Sequence[np.ndarray]) -> Kernel:
@@ -361,13 +394,75 @@ class JittedFunction:
         return compile_graph(builder)
 
 
-def jit(fn: Callable = None, **_ignored):
-    """Decorator (bafe.jit).  Search/autotune options of the reference
-    configure its optimizer, which this backend does not run; they are
-    accepted and ignored."""
+def jit(fn: Callable = None, *, autotune: bool = False, **_ignored):
+    """Decorator (bafe.jit).  autotune=True: device-timed profiling loop (see
+    JittedFunction).  The reference's search options configure its
+    optimizer, which this backend does not run; they are accepted and
+    ignored."""
     if fn is not None:
-        return JittedFunction(fn)
-    return lambda f: JittedFunction(f)
+        return JittedFunction(fn, autotune=autotune)
+    return lambda f: JittedFunction(f, autotune=autotune)
+
+
+# ------------------------------------------------ cost model / autotune --
+# Same names and return shapes as the reference's Python API
+# (__init__.py:646-717), on the backend's device-timed profiling state.
+
+def configure_autotune(refit_threshold: int = 20, invalidation_drift: float = 0.25, warmup_calls: int = 2,
+                       timing_iters: int = 5) -> None:
+    cfg = lib.bafe_cuda_autotune_config_default()
+    cfg.enabled = True
+    cfg.refit_threshold = int(refit_threshold)
+    cfg.invalidation_drift = float(invalidation_drift)
+    cfg.warmup_calls = int(warmup_calls)
+    cfg.timing_iters = int(timing_iters)
+    lib.bafe_cuda_autotune_configure(ctypes.byref(cfg))
+
+
+def autotune_stats() -> dict:
+    s = lib.bafe_cuda_autotune_get_stats()
+    return {"total_calls": s.total_calls, "total_compiles": s.total_compiles, "total_refits": s.total_refits,
+            "total_invalidations": s.total_invalidations, "last_refit_r_squared": s.last_refit_r_squared,
+            "log_size": s.log_size}
+
+
+def autotune_refit() -> int:
+    return int(lib.bafe_cuda_profiling_refit())
+
+
+def autotune_model() -> dict:
+    m = lib.bafe_cuda_profiling_get_model().contents
+    return {"weights": [m.weights[i] for i in range(_binding.BAFE_NUM_FEATURES)], "bias": m.bias,
+            "r_squared": m.r_squared, "n_samples": m.n_samples, "valid": bool(m.valid)}
+
+
+def autotune_dump_log(path: str) -> int:
+    return int(lib.bafe_cuda_profiling_dump_jsonl(path.encode("utf-8")))
+
+
+def autotune_reset() -> None:
+    lib.bafe_cuda_profiling_reset()
+
+
+def extract_features(graph: BafeGraph) -> List[float]:
+    f = (ctypes.c_double * _binding.BAFE_NUM_FEATURES)()
+    lib.bafe_cuda_profiling_extract_features(ctypes.byref(graph), f)
+    return list(f)
+
+
+def calibrate(device: int = 0, what: int = 3) -> None:
+    """Measure the B200 figures of the hardware model (bafe_cuda_calibrate)."""
+    check(lib.bafe_cuda_calibrate(int(device), int(what)), "calibrate")
+
+
+def hardware_model(device: int = -1) -> dict:
+    """BAFE's bafe_hardware_model filled with this GPU's figures; key
+    'measured' tells whether bafe_cuda_calibrate measured them."""
+    h = _binding.BafeHardwareModel()
+    rc = lib.bafe_cuda_hardware_model(int(device), ctypes.byref(h))
+    d = {name: getattr(h, name) for name, _ in h._fields_}
+    d["measured"] = rc == 1
+    return d
 
 
 __all__ = [
@@ -375,4 +470,6 @@ __all__ = [
     "transpose", "reduce_sum", "reduce_max", "reshape", "broadcast_to", "GraphBuilder", "compile_graph",
     "Kernel", "set_option", "get_option", "jit_stats", "jit_clear", "jit_invalidate_memory_cache",
     "set_cache_dir", "cache_dir", "graph_hash", "launch_count", "last_error", "synchronize",
+    "configure_autotune", "autotune_stats", "autotune_refit", "autotune_model", "autotune_dump_log",
+    "autotune_reset", "extract_features", "calibrate", "hardware_model",
 ]

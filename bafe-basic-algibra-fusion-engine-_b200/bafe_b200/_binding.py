@@ -62,6 +62,47 @@ class BafeJitStats(Structure):
     _fields_ = [("hits", c_int), ("misses", c_int), ("compiles", c_int), ("compile_failures", c_int)]
 
 
+# cost.h:27-44 and profiling.h:37-75, 137-143 (layouts of the reference).
+BAFE_NUM_FEATURES = 8
+BAFE_PROFILING_LOG_SIZE = 4096
+
+
+class BafeHardwareModel(Structure):
+    _fields_ = [
+        ("peak_gflops", c_double), ("clock_ghz", c_double), ("simd_width", c_int),
+        ("l1_cache_size", c_int), ("l2_cache_size", c_int), ("l3_cache_size", c_int),
+        ("l1_bandwidth_gbs", c_double), ("l2_bandwidth_gbs", c_double), ("l3_bandwidth_gbs", c_double),
+        ("dram_bandwidth_gbs", c_double), ("f32_flop_rate", c_double), ("f64_flop_rate", c_double),
+        ("f16_flop_rate", c_double), ("bf16_flop_rate", c_double), ("i32_flop_rate", c_double),
+        ("i64_flop_rate", c_double),
+    ]
+
+
+class BafeProfilingRecord(Structure):
+    _fields_ = [("graph_hash", c_char * 65), ("features", c_double * BAFE_NUM_FEATURES),
+                ("predicted_cost", c_double), ("observed_ms", c_double), ("kernel_id", c_int)]
+
+
+class BafeProfilingLog(Structure):
+    _fields_ = [("records", BafeProfilingRecord * BAFE_PROFILING_LOG_SIZE), ("n", c_int), ("head", c_int),
+                ("wrapped", c_bool)]
+
+
+class BafeLearnedCostModel(Structure):
+    _fields_ = [("weights", c_double * BAFE_NUM_FEATURES), ("bias", c_double), ("r_squared", c_double),
+                ("n_samples", c_int), ("valid", c_bool)]
+
+
+class BafeAutotuneStats(Structure):
+    _fields_ = [("total_calls", c_int), ("total_compiles", c_int), ("total_refits", c_int),
+                ("total_invalidations", c_int), ("last_refit_r_squared", c_double), ("log_size", c_int)]
+
+
+class BafeAutotuneConfig(Structure):
+    _fields_ = [("enabled", c_bool), ("refit_threshold", c_int), ("invalidation_drift", c_double),
+                ("warmup_calls", c_int), ("timing_iters", c_int)]
+
+
 PACKAGE_ROOT = Path(__file__).resolve().parent.parent
 
 
@@ -106,6 +147,26 @@ def _load() -> ctypes.CDLL:
         "bafe_cuda_abi_size": ([c_int], c_int64),
         "bafe_cuda_gemm_3xtf32_static_scratch": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
                                                   c_int, c_void_p], c_int),
+        "bafe_cuda_calibrate": ([c_int, c_int], c_int),
+        "bafe_cuda_hardware_model": ([c_int, POINTER(BafeHardwareModel)], c_int),
+        "bafe_cuda_plan_predict_ms": ([c_int], c_double),
+        "bafe_cuda_plan_last_device_ms": ([c_int], c_double),
+        "bafe_cuda_time_device": ([c_int, POINTER(c_void_p), c_int, c_void_p, c_int, POINTER(c_double)], c_int),
+        "bafe_cuda_profiling_init": ([], None),
+        "bafe_cuda_profiling_reset": ([], None),
+        "bafe_cuda_profiling_extract_features": ([G, POINTER(c_double)], None),
+        "bafe_cuda_profiling_add": ([c_char_p, POINTER(c_double), c_double, c_double, c_int], None),
+        "bafe_cuda_profiling_get_log": ([], POINTER(BafeProfilingLog)),
+        "bafe_cuda_profiling_dump_jsonl": ([c_char_p], c_int),
+        "bafe_cuda_profiling_refit": ([], c_int),
+        "bafe_cuda_profiling_get_model": ([], POINTER(BafeLearnedCostModel)),
+        "bafe_cuda_profiling_predict_log": ([POINTER(c_double)], c_double),
+        "bafe_cuda_profiling_predict_ms": ([POINTER(c_double)], c_double),
+        "bafe_cuda_autotune_config_default": ([], BafeAutotuneConfig),
+        "bafe_cuda_autotune_configure": ([POINTER(BafeAutotuneConfig)], None),
+        "bafe_cuda_autotune_get_config": ([], BafeAutotuneConfig),
+        "bafe_cuda_autotune_get_stats": ([], BafeAutotuneStats),
+        "bafe_cuda_autotune_dispatch": ([c_void_p, POINTER(c_void_p), c_int, G, c_char_p, c_double], c_double),
     }
     for name, (args, res) in proto.items():
         fn = getattr(lib, name)
@@ -125,6 +186,13 @@ EXPORTED_SYMBOLS = (
     "bafe_cuda_plan_input_bytes", "bafe_cuda_plan_row_split", "bafe_cuda_run_device", "bafe_cuda_run_host", "bafe_cuda_synchronize", "bafe_cuda_last_error",
     "bafe_cuda_clear_error", "bafe_cuda_set_option", "bafe_cuda_get_option", "bafe_cuda_launch_count",
     "bafe_cuda_abi_size", "bafe_cuda_gemm_3xtf32_static_scratch",
+    "bafe_cuda_calibrate", "bafe_cuda_hardware_model", "bafe_cuda_plan_predict_ms", "bafe_cuda_plan_last_device_ms",
+    "bafe_cuda_time_device", "bafe_cuda_profiling_init", "bafe_cuda_profiling_reset",
+    "bafe_cuda_profiling_extract_features", "bafe_cuda_profiling_add", "bafe_cuda_profiling_get_log",
+    "bafe_cuda_profiling_dump_jsonl", "bafe_cuda_profiling_refit", "bafe_cuda_profiling_get_model",
+    "bafe_cuda_profiling_predict_log", "bafe_cuda_profiling_predict_ms", "bafe_cuda_autotune_config_default",
+    "bafe_cuda_autotune_configure", "bafe_cuda_autotune_get_config", "bafe_cuda_autotune_get_stats",
+    "bafe_cuda_autotune_dispatch",
 )
 
 

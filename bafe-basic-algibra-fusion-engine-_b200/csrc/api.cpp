@@ -109,6 +109,18 @@ void write_err(char* buf, size_t n, const std::string& msg) {
 }
 
 }  // namespace
+
+std::recursive_mutex& api_mutex() { return g_mu; }
+Plan* find_plan(int id) { return plan_ptr(id); }
+int plan_id_of(bafe_kernel_fn fn) {
+    if (!fn) return -1;
+    init_slots();
+    for (int i = 0; i < kSlots; ++i)
+        if (reinterpret_cast<bafe_kernel_fn>(kTrampolines[i]) == fn) return g_slot_plan[i];
+    return -1;
+}
+void drop_memory_cache() { drop_all_plans(); }
+
 }  // namespace bafe_cuda
 
 using namespace bafe_cuda;

@@ -11,6 +11,7 @@
 #include "bafe_cuda.h"
 
 #include <cstdint>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -149,6 +150,7 @@ struct Plan {
     std::string cubin;             // compiled image (kept for lazy per-device loads)
     std::string describe;
     std::vector<DeviceState*> dev; // indexed by device ordinal
+    double last_device_ms = -1.0;  // kernel time of the last host call (CUDA events)
 };
 
 // Lower a parsed graph into steps + generated source.  Host-only: needs no
@@ -178,6 +180,16 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs);
 // Synchronises the current device and reports a kernel-raised error word.
 int synchronize_current_device();
 void release_plan_device_state(Plan& p);
+
+// Plan registry (api.cpp), for the autotuning entry points.
+std::recursive_mutex& api_mutex();
+Plan* find_plan(int id);
+int plan_id_of(bafe_kernel_fn fn);
+void drop_memory_cache();
+
+// Device timing of a plan on device buffers: mean ms of `iters` runs after
+// one untimed run (autotune.cpp).
+int time_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream, int iters, double& ms);
 
 // Error slot shared by every entry point.
 void set_error(int code, const std::string& msg);

@@ -268,7 +268,36 @@ struct DeviceState {
     cudaStream_t h2d = nullptr;         // host calls: input copies (row streaming)
     cudaStream_t d2h = nullptr;         // host calls: output copies (row streaming)
     std::vector<cudaEvent_t> events;    // row streaming: per-panel hand-offs
+    std::vector<cudaEvent_t> tev;       // host calls: timing events around the kernels
 };
+
+// Timing events (pairs: before / after kernels) of a host call.
+static int ensure_timing_events(DeviceState* ds, size_t n) {
+    while (ds->tev.size() < n) {
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreate(&ev) != cudaSuccess) {
+            cudaGetLastError();
+            set_error(6, "cudaEventCreate failed");
+            return 6;
+        }
+        ds->tev.push_back(ev);
+    }
+    return 0;
+}
+
+// Sum of the kernel intervals recorded in tev[0..2*pairs) (synchronised).
+static double timed_ms(DeviceState* ds, size_t pairs) {
+    double total = 0.0;
+    for (size_t i = 0; i < pairs; ++i) {
+        float ms = 0.0f;
+        if (cudaEventElapsedTime(&ms, ds->tev[2 * i], ds->tev[2 * i + 1]) != cudaSuccess) {
+            cudaGetLastError();
+            return -1.0;
+        }
+        total += ms;
+    }
+    return total;
+}
 
 // One device word per GPU that kernels with bounded waits report a timeout
 // into (0 = ok).  Allocated on first use of the device.
@@ -681,6 +710,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
         }
         ds->events.push_back(ev);
     }
+    if (int rc = ensure_timing_events(ds, 2 * (size_t)panels + 2)) return rc;
     cudaEvent_t whole = ds->events[0];
     auto in_done = [&](int i) { return ds->events[1 + 2 * i]; };
     auto run_done = [&](int i) { return ds->events[2 + 2 * i]; };
@@ -701,7 +731,9 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
     if (rc) return fail(rc);
     cudaEventRecord(whole, ds->h2d);
     cudaStreamWaitEvent(ds->stream, whole, 0);
+    cudaEventRecord(ds->tev[0], ds->stream);
     if ((rc = run_steps(p, ds, ds->device, dptrs.data(), ds->stream, Pass{Pass::Once, 0, 0}))) return fail(rc);
+    cudaEventRecord(ds->tev[1], ds->stream);
 
     for (int i = 0; i < panels; ++i) {
         const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
@@ -714,8 +746,10 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
         if (rc) return fail(rc);
         cudaEventRecord(in_done(i), ds->h2d);
         cudaStreamWaitEvent(ds->stream, in_done(i), 0);
+        cudaEventRecord(ds->tev[2 + 2 * i], ds->stream);
         if ((rc = run_steps(p, ds, ds->device, dptrs.data(), ds->stream, Pass{Pass::Panel, r0, rows})))
             return fail(rc);
+        cudaEventRecord(ds->tev[3 + 2 * i], ds->stream);
         cudaEventRecord(run_done(i), ds->stream);
     }
     for (int i = 0; i < panels; ++i) {
@@ -728,6 +762,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
     }
     for (cudaStream_t st : {ds->h2d, ds->stream, ds->d2h})
         if ((rc = sync_stream(st))) return fail(rc);
+    p.last_device_ms = timed_ms(ds, (size_t)panels + 1);
     return check_device_error_word(ds->device);
 }
 
@@ -776,10 +811,13 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
     }
     std::vector<void*> dptrs(ds->in_stage);
     dptrs.push_back(ds->out_stage);
+    if (int rc = ensure_timing_events(ds, 2)) return rc;
+    cudaEventRecord(ds->tev[0], ds->stream);
     if (int rc = run_plan_device(p, dptrs.data(), (int)dptrs.size(), ds->stream)) {
         cudaStreamSynchronize(ds->stream);
         return rc;
     }
+    cudaEventRecord(ds->tev[1], ds->stream);
     if (p.out_bytes) {
         cudaError_t e = cudaMemcpyAsync(ptrs[p.n_inputs], ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
         if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e)); return 7; }
@@ -790,7 +828,46 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
         set_error(9, std::string("device error: ") + cudaGetErrorString(e));
         return 9;
     }
+    p.last_device_ms = timed_ms(ds, 1);
     return check_device_error_word(ds->device);
+}
+
+int time_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v, int iters, double& ms) {
+    ms = -1.0;
+    if (iters < 1) iters = 1;
+    cudaStream_t st = (cudaStream_t)stream_v;
+    if (int rc = run_plan_device(p, ptrs, n_ptrs, st)) return rc;   // untimed: loads, allocates
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess) {
+        cudaGetLastError();
+        if (e0) cudaEventDestroy(e0);
+        set_error(6, "cudaEventCreate failed");
+        return 6;
+    }
+    int rc = 0;
+    cudaEventRecord(e0, st);
+    for (int i = 0; i < iters && !rc; ++i) rc = run_plan_device(p, ptrs, n_ptrs, st);
+    cudaEventRecord(e1, st);
+    cudaError_t e = cudaEventSynchronize(e1);
+    float total = 0.0f;
+    if (!rc && e != cudaSuccess) {
+        cudaGetLastError();
+        set_error(9, std::string("device error: ") + cudaGetErrorString(e));
+        rc = 9;
+    }
+    if (!rc && cudaEventElapsedTime(&total, e0, e1) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(9, "cudaEventElapsedTime failed");
+        rc = 9;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc) return rc;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if ((rc = check_device_error_word(dev))) return rc;
+    ms = total / iters;
+    return 0;
 }
 
 void release_plan_device_state(Plan& p) {
@@ -806,6 +883,7 @@ void release_plan_device_state(Plan& p) {
         if (s->out_stage) cudaFree(s->out_stage);
         for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
         for (cudaEvent_t ev : s->events) cudaEventDestroy(ev);
+        for (cudaEvent_t ev : s->tev) cudaEventDestroy(ev);
         if (s->stream) cudaStreamDestroy(s->stream);
         if (s->module && d.ok) d.moduleUnload(s->module);
         delete s;

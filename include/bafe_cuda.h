@@ -94,6 +94,69 @@ typedef void (*bafe_kernel_fn)(void);
 typedef struct { int hits; int misses; int compiles; int compile_failures; } bafe_jit_stats;
 #endif /* BAFE_JIT_H */
 
+#ifndef BAFE_COST_H
+/* cost.h:27-44 */
+typedef struct {
+    double peak_gflops;
+    double clock_ghz;
+    int    simd_width;
+    int    l1_cache_size;
+    int    l2_cache_size;
+    int    l3_cache_size;
+    double l1_bandwidth_gbs;
+    double l2_bandwidth_gbs;
+    double l3_bandwidth_gbs;
+    double dram_bandwidth_gbs;
+    double f32_flop_rate;
+    double f64_flop_rate;
+    double f16_flop_rate;
+    double bf16_flop_rate;
+    double i32_flop_rate;
+    double i64_flop_rate;
+} bafe_hardware_model;
+#endif /* BAFE_COST_H */
+
+#ifndef BAFE_PROFILING_H
+/* profiling.h:37-75, 137-143 */
+#define BAFE_NUM_FEATURES 8
+#define BAFE_PROFILING_LOG_SIZE 4096
+typedef struct {
+    char   graph_hash[65];
+    double features[BAFE_NUM_FEATURES];
+    double predicted_cost;
+    double observed_ms;
+    int    kernel_id;
+} bafe_profiling_record;
+typedef struct {
+    bafe_profiling_record records[BAFE_PROFILING_LOG_SIZE];
+    int  n;
+    int  head;
+    bool wrapped;
+} bafe_profiling_log;
+typedef struct {
+    double weights[BAFE_NUM_FEATURES];
+    double bias;
+    double r_squared;
+    int    n_samples;
+    bool   valid;
+} bafe_learned_cost_model;
+typedef struct {
+    int    total_calls;
+    int    total_compiles;
+    int    total_refits;
+    int    total_invalidations;
+    double last_refit_r_squared;
+    int    log_size;
+} bafe_autotune_stats;
+typedef struct {
+    bool   enabled;
+    int    refit_threshold;
+    double invalidation_drift;
+    int    warmup_calls;
+    int    timing_iters;
+} bafe_autotune_config;
+#endif /* BAFE_PROFILING_H */
+
 /* ------------------------------------------------------------------------
  * Drop-in replacements for bafe/include/bafe/jit.h
  * ---------------------------------------------------------------------- */
@@ -213,6 +276,77 @@ int bafe_cuda_get_option(const char *key, char *buf, size_t buf_size);
 /* Number of kernel launches the library has enqueued since load (all
  * plans, all devices).  Used to report launch counts. */
 int64_t bafe_cuda_launch_count(void);
+
+/* ------------------------------------------------------------------------
+ * Roofline cost model and device-timed autotuning on the B200.
+ * ---------------------------------------------------------------------- */
+
+/* Measures the figures bafe_cuda_hardware_model reports, on `device`:
+ * what & 1: streaming bandwidth from HBM and from L2, launch latency;
+ * what & 2: f32 GEMM rates (3xTF32 and TF32 tensor cores at 4096^3, the
+ * exact CUDA-core kernel at 2048^3); what & 4: the exact kernel's rates for
+ * f64, i32, i64, f16, bf16 (1024^3).  Compiles and runs backend plans
+ * (cached like any plan).  Returns 0, or nonzero with a message.  New: the
+ * reference's hardware models are fixed CPU figures (cost.c:25-67). */
+int bafe_cuda_calibrate(int device, int what);
+
+/* Fills BAFE's hardware model (cost.h:27-44) with the B200's figures, for
+ * bafe_cost_model_from_hardware (cost.c:73): peak_gflops = the f32 GEMM
+ * rate at the current gemm_precision; dram / l2 bandwidth = streaming
+ * rates; l1 = all SMs' shared memory; no L3 (l3 = l2); dtype rates relative
+ * to f32.  device < 0: the current device.  Returns 1 when the figures were
+ * measured by bafe_cuda_calibrate, 0 when nominal, -1 for a NULL out.
+ * Replaces bafe_hardware_model_default/_server (cost.c:25-67). */
+int bafe_cuda_hardware_model(int device, bafe_hardware_model *out);
+
+/* Roofline time of a plan on the current device: per step
+ * max(flops / rate, bytes / bandwidth) + launch latency, with the
+ * (calibrated) hardware model.  -1 for an unknown plan.  New. */
+double bafe_cuda_plan_predict_ms(int plan);
+
+/* Device time (CUDA events around the kernels, copies excluded) of the
+ * last host-pointer call of a plan; -1 before the first call.  New: the
+ * reference times calls by wall clock (__init__.py:386-430). */
+double bafe_cuda_plan_last_device_ms(int plan);
+
+/* Runs a plan once untimed, then `iters` times between CUDA events on
+ * `stream`, on device buffers; *ms = mean device time per run.
+ * Synchronous.  Returns 0 or an error code.  New. */
+int bafe_cuda_time_device(int plan, void *const *ptrs, int n_ptrs, void *stream, int iters, double *ms);
+
+/* Profiling log and learned model: restate bafe/include/bafe/profiling.h
+ * (profiling.c) with the same record layout, features, JSONL format and
+ * least-squares refit, so records and models are interchangeable.
+ * bafe_cuda_profiling_extract_features replaces profiling.c:83-131
+ * (identical feature values for the same graph). */
+void bafe_cuda_profiling_init(void);                                        /* profiling.h:82 */
+void bafe_cuda_profiling_reset(void);                                       /* profiling.h:85 */
+void bafe_cuda_profiling_extract_features(const bafe_graph *g, double *features);   /* profiling.h:93 */
+void bafe_cuda_profiling_add(const char *graph_hash, const double *features,
+                             double predicted_cost, double observed_ms, int kernel_id);   /* profiling.h:101 */
+const bafe_profiling_log *bafe_cuda_profiling_get_log(void);                /* profiling.h:108 */
+int bafe_cuda_profiling_dump_jsonl(const char *path);                       /* profiling.h:111 */
+int bafe_cuda_profiling_refit(void);                                        /* profiling.h:121 */
+const bafe_learned_cost_model *bafe_cuda_profiling_get_model(void);         /* profiling.h:124 */
+double bafe_cuda_profiling_predict_log(const double *features);             /* profiling.h:128 */
+double bafe_cuda_profiling_predict_ms(const double *features);              /* profiling.h:131 */
+bafe_autotune_config bafe_cuda_autotune_config_default(void);               /* profiling.h:145 */
+void bafe_cuda_autotune_configure(const bafe_autotune_config *cfg);         /* profiling.h:147 */
+bafe_autotune_config bafe_cuda_autotune_get_config(void);                   /* profiling.h:149 */
+bafe_autotune_stats bafe_cuda_autotune_get_stats(void);                     /* profiling.h:152 */
+
+/* Replaces bafe_autotune_dispatch (profiling.h:168-173, a placeholder in
+ * profiling.c:364-410 that neither runs nor times the kernel).  `fn` must
+ * be a function returned by bafe_cuda_jit_get_or_compile, `args` its n+1
+ * host pointers.  The first warmup_calls dispatches only run it; later ones
+ * run it timing_iters times, log (features of `graph`, predicted_cost --
+ * or the plan's roofline time when <= 0 --, mean DEVICE ms) and refit after
+ * refit_threshold new records; when the refitted model misses the measured
+ * time by more than invalidation_drift, the in-memory plan cache is dropped
+ * (as bafe_jit_invalidate_memory_cache; held function pointers go stale).
+ * Returns the observed device ms, 0 for a warm-up call, -1 on error. */
+double bafe_cuda_autotune_dispatch(bafe_kernel_fn fn, void **args, int n_args, const bafe_graph *graph,
+                                   const char *graph_hash, double predicted_cost);
 
 /* out = A . B (fp32, 3xTF32 tensor cores, M x N row-major out) without any
  * device allocation.  No counterpart in the reference.

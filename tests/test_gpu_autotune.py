@@ -1,0 +1,158 @@
+"""Device-timed cost model and autotuning on the B200.
+
+Calibration measures the hardware model on the device; host calls record
+the DEVICE time of their kernels (CUDA events, copies excluded); the plan
+roofline, fed the calibrated figures, predicts those times; the autotune
+dispatch and @jit(autotune=True) log device times, refit and drop stale
+plans the way BAFE's autotune loop does (bafe/tests/test_autotune.py)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import bafe_b200 as bafe
+from bafe_b200 import _binding
+from bafe_b200._binding import BAFE_NUM_FEATURES, lib
+from bafe_b200.graph import GraphBuilder
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _reset_profiling():
+    lib.bafe_cuda_profiling_reset()
+    yield
+    lib.bafe_cuda_profiling_reset()
+    bafe.configure_autotune()
+
+
+@pytest.fixture(scope="module")
+def calibrated(cuda):
+    bafe.calibrate(0, 7)
+    return bafe.hardware_model(0)
+
+
+def _ew(n):
+    g = GraphBuilder()
+    x, y, z = (g.add_input(c, (n,), 0, 0) for c in "XYZ")
+    g.set_output(g.add("relu", [g.add("add", [g.add("mul", [x, y]), z])]))
+    return g
+
+
+def _mm(M, K, N):
+    g = GraphBuilder()
+    a = g.add_input("A", (M, K), 0, 0)
+    b = g.add_input("B", (K, N), 0, 0)
+    g.set_output(g.add("relu", [g.add("matmul", [a, b])]))
+    return g
+
+
+def test_calibration_measures_the_device(calibrated):
+    h = calibrated
+    assert h["measured"]
+    assert 4000 < h["dram_bandwidth_gbs"] < 9000
+    assert h["l2_bandwidth_gbs"] > h["dram_bandwidth_gbs"]
+    assert 100e3 < h["peak_gflops"] < 400e3              # 3xTF32 f32 GEMM, GFLOP/s
+    assert h["l2_cache_size"] > 100 << 20 and h["l3_cache_size"] == h["l2_cache_size"]
+    assert all(0 < h[k] < 1 for k in ("f64_flop_rate", "i32_flop_rate", "i64_flop_rate"))
+
+
+def test_host_calls_record_device_time_and_roofline_predicts_it(calibrated):
+    n = 1 << 26
+    k = bafe.compile_graph(_ew(n))
+    rng = np.random.default_rng(1)
+    X, Y, Z = (rng.uniform(-1, 1, n).astype(np.float32) for _ in range(3))
+    out = k(X, Y, Z)
+    np.testing.assert_array_equal(out, np.maximum(X * Y + Z, 0))
+    dev_ms = lib.bafe_cuda_plan_last_device_ms(k.plan)
+    pred = lib.bafe_cuda_plan_predict_ms(k.plan)
+    assert dev_ms > 0 and 0.5 < dev_ms / pred < 2.0, (dev_ms, pred)
+
+    bafe.set_option("gemm_precision", "3xtf32")
+    gm = bafe.compile_graph(_mm(2048, 2048, 2048))
+    A = rng.standard_normal((2048, 2048), dtype=np.float32)
+    gm(A, A)
+    dev_ms = lib.bafe_cuda_plan_last_device_ms(gm.plan)
+    pred = lib.bafe_cuda_plan_predict_ms(gm.plan)
+    assert dev_ms > 0 and 0.4 < dev_ms / pred < 2.5, (dev_ms, pred)
+
+
+def test_time_device_on_resident_buffers(cuda):
+    torch = cuda
+    n = 1 << 24
+    k = bafe.compile_graph(_ew(n))
+    xs = [torch.rand(n, device="cuda") for _ in range(3)]
+    out = torch.empty(n, device="cuda")
+    ptrs = (ctypes.c_void_p * 4)(*[t.data_ptr() for t in xs + [out]])
+    ms = ctypes.c_double()
+    assert lib.bafe_cuda_time_device(k.plan, ptrs, 4, None, 20, ctypes.byref(ms)) == 0
+    assert 0 < ms.value < 1.0                           # 256 MiB of traffic: ~0.04 ms
+    assert torch.equal(out, torch.relu(xs[0] * xs[1] + xs[2]))
+
+
+def test_dispatch_logs_device_times_and_refits(cuda):
+    bafe.configure_autotune(refit_threshold=5, warmup_calls=1, timing_iters=2, invalidation_drift=1e9)
+    n = 1 << 22
+    g = _ew(n)
+    k = bafe.compile_graph(g)
+    rng = np.random.default_rng(2)
+    X, Y, Z = (rng.uniform(-1, 1, n).astype(np.float32) for _ in range(3))
+    out = np.zeros(n, np.float32)
+    args = (ctypes.c_void_p * 4)(X.ctypes.data, Y.ctypes.data, Z.ctypes.data, out.ctypes.data)
+    fn = ctypes.c_void_p(k.fn_ptr)
+    assert lib.bafe_cuda_autotune_dispatch(fn, args, 4, ctypes.byref(g.graph), None, 0.0) == 0.0   # warm-up
+    np.testing.assert_array_equal(out, np.maximum(X * Y + Z, 0))
+    times = [lib.bafe_cuda_autotune_dispatch(fn, args, 4, ctypes.byref(g.graph), None, 0.0) for _ in range(6)]
+    assert all(t > 0 for t in times)
+    st = bafe.autotune_stats()
+    assert st["log_size"] == 6 and st["total_refits"] == 1 and st["total_calls"] == 7
+    rec = lib.bafe_cuda_profiling_get_log().contents.records[0]
+    assert rec.predicted_cost > 0 and rec.observed_ms == times[0]
+
+
+def test_dispatch_drops_plans_when_the_model_drifts(cuda):
+    bafe.configure_autotune(refit_threshold=5, warmup_calls=0, timing_iters=1, invalidation_drift=0.0)
+    g = _ew(1 << 20)
+    k = bafe.compile_graph(g)
+    X = np.ones(1 << 20, np.float32)
+    out = np.zeros_like(X)
+    args = (ctypes.c_void_p * 4)(X.ctypes.data, X.ctypes.data, X.ctypes.data, out.ctypes.data)
+    fn = ctypes.c_void_p(k.fn_ptr)
+    for _ in range(5):
+        assert lib.bafe_cuda_autotune_dispatch(fn, args, 4, ctypes.byref(g.graph), None, 0.0) > 0
+    assert bafe.autotune_stats()["total_invalidations"] == 1
+    assert lib.bafe_cuda_autotune_dispatch(fn, args, 4, ctypes.byref(g.graph), None, 0.0) == -1.0   # stale
+
+
+def test_jit_autotune_logs_refits_and_stays_correct(cuda):
+    bafe.configure_autotune(refit_threshold=8, warmup_calls=1, timing_iters=2)
+
+    @bafe.jit(autotune=True)
+    def f(A, B):
+        return bafe.matmul(A, B)
+
+    rng = np.random.default_rng(3)
+    for i in range(30):
+        n = (256, 1024, 2048)[i % 3]
+        A = rng.standard_normal((n, 64), dtype=np.float32)
+        B = rng.standard_normal((64, n), dtype=np.float32)
+        out = f(A, B)
+        ref = A.astype(np.float64) @ B.astype(np.float64)
+        assert np.abs(out - ref).max() <= 1e-4 * np.sqrt(64 / 64) * 10
+    st = bafe.autotune_stats()
+    assert st["log_size"] == 27 and st["total_refits"] >= 3
+    m = bafe.autotune_model()
+    assert m["valid"] and m["r_squared"] > 0.3
+    log = lib.bafe_cuda_profiling_get_log().contents
+    assert all(log.records[i].observed_ms > 0 for i in range(log.n))
+
+
+def test_jit_without_autotune_does_not_log(cuda):
+    @bafe.jit
+    def f(A, B):
+        return bafe.matmul(A, B)
+
+    A = np.ones((16, 16), np.float32)
+    for _ in range(5):
+        f(A, A)
+    assert bafe.autotune_stats()["log_size"] == 0
