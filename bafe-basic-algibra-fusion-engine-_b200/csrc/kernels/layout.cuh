@@ -39,6 +39,52 @@ __device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restri
     }
 }
 
+// The same transpose for 4-byte element types with 16-byte global accesses
+// (M % 4 == 0 and N % 4 == 0, 16-byte aligned buffers): a CTA of 256
+// threads moves a 64 x 64 tile.  Each thread first issues its four 16-byte
+// loads (four rows of x, 64 B in flight), then scatters the 16 elements into
+// the tile stored transposed -- S[c][r] for x's row r, column c -- and after
+// the barrier reads four consecutive S[c][..] as one 16-byte vector, which
+// is four consecutive elements of out's row c, stored with one 16-byte
+// store.  The 16-byte chunks of each S row are XOR-swizzled with (c / 4) so
+// that the scattering stores spread over the banks (2-way at most) while
+// every vector read stays one aligned chunk.
+template <class T>
+__device__ __forceinline__ void transpose2d_w4(const T* __restrict__ x, T* __restrict__ out, i64 M, i64 N) {
+    static_assert(sizeof(T) == 4, "4-byte element types only");
+    __shared__ __align__(16) u32 S[64 * 64];
+    const i64 j0 = (i64)blockIdx.x * 64;   // x row block == out column block
+    const i64 i0 = (i64)blockIdx.y * 64;   // x column block == out row block
+    const int t = threadIdx.x;
+    const int q = t & 15, r0 = t >> 4;
+    uint4 v[4];
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+        const i64 xr = j0 + r0 + 16 * pass, xc = i0 + 4 * q;
+        if (xr < N && xc < M) v[pass] = __ldcs(reinterpret_cast<const uint4*>(x + xr * M + xc));
+        else v[pass] = make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+        const int r = r0 + 16 * pass;
+        const u32 e[4] = {v[pass].x, v[pass].y, v[pass].z, v[pass].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int c = 4 * q + k;               // (c / 4) & 15 == q
+            S[c * 64 + 4 * ((r >> 2) ^ q) + (r & 3)] = e[k];
+        }
+    }
+    __syncthreads();
+    const int p = t & 15, c0 = t >> 4;
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+        const int c = c0 + 16 * pass;
+        const i64 oi = i0 + c, oj = j0 + 4 * p;
+        const uint4 w = *reinterpret_cast<const uint4*>(&S[c * 64 + 4 * (p ^ ((c >> 2) & 15))]);
+        if (oi < M && oj < N) __stcs(reinterpret_cast<uint4*>(out + oi * N + oj), w);
+    }
+}
+
 // Strided gather over a rank-R output: out[o] = x[sum_d coord_d(o) * stride[d]]
 // where coord_d is o's row-major coordinate.  Used for rank-N transposes
 // (stride = input stride of the permuted axis) and for broadcast_to

@@ -38,6 +38,9 @@ extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) che
 extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
     bafe::transpose2d<float>(x, out, M, N);
 }
+extern "C" __global__ void __launch_bounds__(256) check_transpose_w4(const float* x, float* out, i64 M, i64 N) {
+    bafe::transpose2d_w4<float>(x, out, M, N);
+}
 extern "C" __global__ void __launch_bounds__(256) check_gather(const float* x, float* out, const bafe::GatherArgs g) {
     bafe::gather_nd<float>(x, out, g);
 }

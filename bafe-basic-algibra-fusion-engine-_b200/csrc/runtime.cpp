@@ -552,6 +552,13 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 const void* x = ptr_of(s.srcs[0]);
                 int64_t M = s.M, Nn = s.N;
                 void* params[] = {&x, &dst, &M, &Nn};
+                if (ds->fn_vec[si] && s.M % 4 == 0 && s.N % 4 == 0 && ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
+                    if ((s.M + 63) / 64 > 65535) { set_error(8, "transpose grid too large"); return 8; }
+                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((s.M + 63) / 64), 1,
+                                        256, 1, 1, 0, stream, params))
+                        return rc;
+                    break;
+                }
                 if ((s.M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
                 if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((s.M + 31) / 32), 1, 32, 8, 1,
                                     0, stream, params))

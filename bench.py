@@ -8,10 +8,13 @@ Headline workload (one "step" = one call of the plan):
         rows are split into contiguous row panels, one per rank; B is
         broadcast once from rank 0 over NCCL (outside the timed region, as
         the runtime keeps B resident; its time is reported separately).
-Secondary (same JSON line, key "ew"):
+Secondary (same JSON line, keys "ew" and "transpose"):
   ew:   relu(add(mul(X,Y),Z)) over 2^28 fp32 elements (1 GiB per vector),
         range-split across ranks with no collective.  Metric GB/s
         (16 bytes per element).
+  transpose: materialisation of transpose(X), X 16384 x 16384 fp32; ranks
+        own output row blocks (input column panels), no collective.
+        Metric GB/s (8 bytes per element).
 
 value:   device-resident inputs, CUDA events around every step on the
          launching stream, max over ranks; inputs are larger than L2
@@ -50,6 +53,7 @@ import numpy as np  # noqa: E402
 
 GEMM_M = GEMM_N = GEMM_K = 16384
 EW_N = 1 << 28
+TR_N = 16384
 STD = 1.0 / math.sqrt(GEMM_K)
 
 
@@ -62,10 +66,11 @@ def parse():
     p.add_argument("--precision", default=os.environ.get("BAFE_GEMM_PRECISION", "auto"))
     p.add_argument("--e2e-steps", type=int, default=3, help="0 skips the host-pointer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--only", choices=["gemm", "ew"], default=None,
+    p.add_argument("--only", choices=["gemm", "ew", "transpose"], default=None,
                    help="run one workload (profiling); prints its own line")
     p.add_argument("--gemm-size", type=int, default=GEMM_M, help="M=N=K (profiling smaller cases)")
     p.add_argument("--ew-elements", type=int, default=EW_N)
+    p.add_argument("--transpose-size", type=int, default=TR_N, help="transpose of an S x S fp32 matrix")
     return p.parse_args()
 
 
@@ -150,6 +155,14 @@ def ew_graph(n: int):
     g = bafe.GraphBuilder()
     ids = [g.add_input(nm, (n,), 0, 0) for nm in "XYZ"]
     g.set_output(g.add("relu", [g.add("add", [g.add("mul", [ids[0], ids[1]]), ids[2]])]))
+    return g
+
+
+def transpose_graph(rows: int, cols: int):
+    import bafe_b200 as bafe
+    g = bafe.GraphBuilder()
+    x = g.add_input("X", (rows, cols), 0, 0)
+    g.set_output(g.add("transpose", [x], perm=[1, 0]))
     return g
 
 
@@ -296,6 +309,10 @@ class Ctx:
         if self.world > 1:
             import datetime
             import torch.distributed as dist_mod
+            # rank 0's stdout carries exactly one JSON line: keep NCCL's
+            # version banner (NCCL_DEBUG=VERSION) off it
+            if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+                os.environ["NCCL_DEBUG"] = "WARN"
             dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)
             self.dist = dist_mod
         self.hbm_peak, self.bf16_peak, self.bf16_sustained, self.peak_src = peaks()
@@ -438,19 +455,104 @@ def bench_ew(c: Ctx) -> dict:
     return res
 
 
+def cpu_baseline_transpose(x: np.ndarray):
+    """The reference's generated transpose kernel (codegen.c:360-369) on a
+    column panel: X[:, c0:c1] stored contiguously, transposed to rows."""
+    from oracle import refbafe
+    rows, cols = x.shape
+    if refbafe.available():
+        import tempfile
+        from bafe_b200.graph import GraphBuilder
+        ref = refbafe.Reference(cache_dir=tempfile.mkdtemp(prefix="bafe_ref_"))
+        g = GraphBuilder()
+        xi = g.add_input("X", (rows, cols), 0, 0)
+        g.set_output(g.add("transpose", [xi], perm=[1, 0]))
+        opt = ref.optimize(g.graph)
+        fn = ref.compile(opt)
+        nodes = refbafe.graph_nodes(opt)
+        out = np.zeros((cols, rows), np.float32)
+        ref.call_kernel(fn, [x], out, stack_bytes=refbafe.stack_bytes_for(nodes))   # warm
+        t0 = time.perf_counter()
+        reps = 3
+        for _ in range(reps):
+            ref.call_kernel(fn, [x], out, stack_bytes=refbafe.stack_bytes_for(nodes))
+        dt = (time.perf_counter() - t0) / reps
+        kind = "reference"
+    else:
+        from oracle import oracle
+        t0 = time.perf_counter()
+        oracle.transpose2d(x, cols, rows)
+        dt = time.perf_counter() - t0
+        kind = "port"
+    return {"value": 8.0 * x.size / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{rows}x{cols} column panel ({dt * 1e3:.1f} ms per call)"}
+
+
+def bench_transpose(c: Ctx) -> dict:
+    """Transpose materialisation of an S x S fp32 matrix.  Rank r owns output
+    rows [r0, r1) = input columns r0:r1, held as its own contiguous S x
+    (r1 - r0) panel; no collective."""
+    import bafe_b200 as bafe
+    torch, args = c.torch, c.args
+    from bafe_b200.parallel import row_panels
+    S = args.transpose_size
+    r0, r1 = row_panels(S, c.world, align=32)[c.rank]
+    cols = r1 - r0
+    X = torch.rand(S, cols, device=c.dev, generator=c.gen)
+    O = torch.empty(cols, S, device=c.dev)
+    k = bafe.compile_graph(transpose_graph(S, cols))
+    steps = max(args.steps, 100)
+    c.barrier()
+    with Clocks(c.local) as ck:
+        per, total, launches = time_steps(torch, k, [X], O, steps, args.warmup)
+    c.barrier()
+    total = c.max(total)
+    ms = total / steps
+    achieved = 8.0 * S * cols / (statistics.mean(per) * 1e-3) / 1e9
+    if not torch.equal(O[:, :64], X[:64, :].t()):
+        raise RuntimeError("transpose output check failed")
+    res = {
+        "metric": f"GB/s (transpose materialisation {S}x{S} fp32)",
+        "value": round(8.0 * S * S / (ms * 1e-3) / 1e9, 1), "unit": "GB/s", "ms_per_step": round(ms, 4),
+        "steps": steps,
+        "config": {"workload": f"transpose(X) perm (1,0), X {S}x{S} fp32, materialised row-major",
+                   "parallelism": f"output row blocks x{c.world} (input column panels), no collective",
+                   "l2": "input and output larger than L2; no flush" if S * cols * 4 > (126 << 20)
+                         else "inputs smaller than L2",
+                   "plan": k.describe().strip()},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": c.hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / c.hbm_peak, 4),
+                     "traffic": traffic_from_profiles(f"transpose_{S}"), "peak_basis": f"{c.peak_src} hbm_gbs"},
+        "gpu_launches": int(c.sum(launches)), "clocks": ck.summary(),
+    }
+    if args.e2e_steps > 0:
+        hX = X.cpu().pin_memory()
+        hO = torch.empty(cols, S).pin_memory()
+        c.barrier()
+        e2e_ms = c.max(time_e2e(torch, k, [hX], hO, args.e2e_steps))
+        res["e2e"] = {"value": round(8.0 * S * S / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                      "h2d_bytes_per_step": 4.0 * S * S, "d2h_bytes_per_step": 4.0 * S * S,
+                      "ms_per_step": round(e2e_ms, 2)}
+        if c.rank == 0 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline_transpose(np.ascontiguousarray(hX[:, :min(cols, 256)].numpy()))
+    return res
+
+
 def run_ours(args):
     import bafe_b200 as bafe
     c = Ctx(args)
     bafe.set_option("gemm_precision", args.precision)
     common = {"n_gpus": c.world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
               "scaling": "strong", "vs_baseline": None, "data": "synthetic, generated on device"}
-    if args.only == "ew":
-        line = dict(bench_ew(c), **{k: v for k, v in common.items() if k != "steps"})
+    if args.only in ("ew", "transpose"):
+        fn = bench_ew if args.only == "ew" else bench_transpose
+        line = dict(fn(c), **{k: v for k, v in common.items() if k != "steps"})
         line["scaling"] = "strong"
     else:
         line = dict(common, **bench_gemm(c))
         if args.only is None:
             line["ew"] = bench_ew(c)
+            line["transpose"] = bench_transpose(c)
     if c.rank == 0:
         print(json.dumps(line), flush=True)
     if c.dist is not None:

@@ -1,0 +1,51 @@
+"""Transpose materialisation on the device, bit for bit.
+
+4-byte element types with row lengths divisible by 4 take the vectorised
+64 x 64 tile kernel; everything else the 32 x 32 scalar kernel.  Both must
+return what the oracle returns (codegen.c:363-369: x.T; f16 graphs pass
+through the emitter's own f16 <-> f32 conversions, which rescale f16
+subnormals), on whole and ragged tile edges."""
+import numpy as np
+import pytest
+
+import bafe_b200 as bafe
+from bafe_b200.graph import GraphBuilder
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+DT = {np.float32: 0, np.float64: 1, np.int32: 2, np.float16: 4}
+
+
+def _transpose(x):
+    g = GraphBuilder()
+    xi = g.add_input("X", x.shape, DT[x.dtype.type], 0)
+    g.set_output(g.add("transpose", [xi], perm=[1, 0]))
+    k = bafe.compile_graph(g)
+    want = oracle.evaluate(g.to_list(), {xi: x}, g.output).reshape(x.shape[::-1])
+    return k(x), k.describe(), want
+
+
+@pytest.mark.parametrize("shape", [(4, 8), (64, 64), (68, 132), (196, 260), (1000, 4), (4100, 4096), (37, 53),
+                                   (1, 1000), (130, 3)])
+@pytest.mark.parametrize("dtype", [np.float32, np.int32, np.float64, np.float16])
+def test_transpose_is_exact(cuda, shape, dtype):
+    rng = np.random.default_rng(hash((shape, dtype.__name__)) % (1 << 32))
+    if np.issubdtype(dtype, np.integer):
+        x = rng.integers(-2**31, 2**31 - 1, size=shape, dtype=dtype)
+    else:
+        x = rng.standard_normal(shape).astype(dtype)
+    out, plan, want = _transpose(x)
+    assert "transpose2d" in plan
+    assert out.shape == shape[::-1]
+    assert out.tobytes() == want.tobytes()
+    if dtype != np.float16:
+        assert out.tobytes() == np.ascontiguousarray(x.T).tobytes()
+
+
+def test_transpose_of_special_values_is_a_bit_copy(cuda):
+    x = np.array([[np.nan, -0.0, np.inf, -np.inf], [1e-45, -1e-45, 3.0, -3.0],
+                  [0.0, 1.0, 2.0, 3.0], [4.0, 5.0, 6.0, 7.0]], np.float32)
+    x.view(np.uint32)[0, 0] = 0x7FC12345              # NaN payload survives
+    out, _, _ = _transpose(x)
+    assert out.view(np.uint32).tobytes() == np.ascontiguousarray(x.T).view(np.uint32).tobytes()
