@@ -373,6 +373,14 @@ class JittedFunction:
         return out
 
     def _compile(self, args: Sequence[np.ndarray]) -> Kernel:
+        return compile_graph(self._trace_graph(args))
+
+    @property
+    def n_args(self) -> int:
+        return self._fn.__code__.co_argcount
+
+    def _trace_graph(self, args: Sequence) -> GraphBuilder:
+        """Trace the function on arguments of these shapes / dtypes / layouts."""
         global _TRACE
         _TRACE = GraphBuilder()
         try:
@@ -391,7 +399,57 @@ class JittedFunction:
             builder = _TRACE
         finally:
             _TRACE = None
-        return compile_graph(builder)
+        return builder
+
+
+class FusedFunction(JittedFunction):
+    """h = fuse(f, g): h(*f_args, *g_args[1:]) == g(f(*f_args), *g_args[1:]),
+    compiled as ONE plan (__init__.py:758-916, fuse.c:12-125).  The graphs
+    are concatenated with f's output feeding g's first input, so on the
+    device the intermediate is a plan temporary -- or, when it is
+    elementwise-consumed, never stored at all (the lowering merges the
+    chain into one region or into the GEMM's epilogue) -- and it never
+    crosses PCIe.  Chains: fuse(fuse(f, g), h)."""
+
+    def __init__(self, func_a, func_b):
+        self._func_a = func_a
+        self._func_b = func_b
+        self._compiled = {}
+        self._autotune = False
+        self._call_count = {}
+        self._fn = func_a._fn
+        # name / doc of f only: copying f's __dict__ (update_wrapper's default)
+        # would overwrite _func_a / _func_b when f is itself fused, which is
+        # what breaks 3-way chains in the reference (its test_fuse.py xfails
+        # fuse(fuse(f, g), h))
+        functools.update_wrapper(self, func_a._fn, updated=())
+
+    @property
+    def n_args(self) -> int:
+        return self._func_a.n_args + self._func_b.n_args - 1
+
+    def _trace_graph(self, args: Sequence) -> GraphBuilder:
+        na = self._func_a.n_args
+        if len(args) != self.n_args:
+            raise TypeError(f"fused function expects {self.n_args} args ({na} for f + "
+                            f"{self._func_b.n_args - 1} for g, since g's first input is f's output), got {len(args)}")
+        ga = self._func_a._trace_graph(args[:na])
+        out = ga.output
+        # g is traced on a row-major stand-in of f's output, as the reference
+        # does (a zero array, __init__.py:853-855); concat then rewires g's
+        # uses of it to f's output node.  Zero strides: nothing is allocated.
+        shape = ga.shape(out)
+        stand_in = np.lib.stride_tricks.as_strided(np.zeros(1, _BAFE_TO_NP[ga.dtype(out)]), shape=shape,
+                                                   strides=(0,) * len(shape))
+        gb = self._func_b._trace_graph((stand_in,) + tuple(args[na:]))
+        return GraphBuilder.concat(ga, gb)
+
+
+def fuse(func_a, func_b):
+    """bafe.fuse (__init__.py:918-938)."""
+    if not isinstance(func_a, JittedFunction) or not isinstance(func_b, JittedFunction):
+        raise TypeError("fuse() requires @bafe.jit-decorated or fused functions")
+    return FusedFunction(func_a, func_b)
 
 
 def jit(fn: Callable = None, *, autotune: bool = False, **_ignored):
@@ -471,5 +529,5 @@ __all__ = [
     "Kernel", "set_option", "get_option", "jit_stats", "jit_clear", "jit_invalidate_memory_cache",
     "set_cache_dir", "cache_dir", "graph_hash", "launch_count", "last_error", "synchronize",
     "configure_autotune", "autotune_stats", "autotune_refit", "autotune_model", "autotune_dump_log",
-    "autotune_reset", "extract_features", "calibrate", "hardware_model",
+    "autotune_reset", "extract_features", "calibrate", "hardware_model", "fuse", "FusedFunction",
 ]

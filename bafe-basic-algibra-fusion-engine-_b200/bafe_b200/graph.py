@@ -234,6 +234,47 @@ class GraphBuilder:
         g.outputs[g.n_outputs] = nid
         g.n_outputs += 1
 
+    # -- cross-call fusion ------------------------------------------------------
+    @classmethod
+    def concat(cls, a: "GraphBuilder", b: "GraphBuilder") -> "GraphBuilder":
+        """fuse.c:12-104: a's nodes, then b's nodes with children shifted by
+        a's node count, except that uses of b's FIRST input read a's output;
+        inputs = a's inputs + b's inputs[1:]; output = b's output.  b's first
+        input node stays in the node list, unreferenced."""
+        ga, gb = a.graph, b.graph
+        if ga.n_outputs == 0:
+            raise ValueError("graph_a has no outputs")
+        if gb.n_inputs == 0:
+            raise ValueError("graph_b has no inputs")
+        if ga.n_nodes + gb.n_nodes > BAFE_MAX_NODES:
+            raise ValueError("fused graph too large")
+        out = cls()
+        g = out.graph
+        off = ga.n_nodes
+        a_out = ga.outputs[0]
+        b_first = gb.inputs[0]
+        b_inputs = {gb.inputs[k] for k in range(gb.n_inputs)}
+        for i in range(ga.n_nodes):
+            g.nodes[i] = ga.nodes[i]
+            g.nodes[i].id = i
+        for j in range(gb.n_nodes):
+            g.nodes[off + j] = gb.nodes[j]
+            d = g.nodes[off + j]
+            d.id = off + j
+            for c in range(d.n_children):
+                ch = d.children[c]
+                d.children[c] = a_out if (ch == b_first and ch in b_inputs) else ch + off
+        g.n_nodes = ga.n_nodes + gb.n_nodes
+        for i in range(ga.n_inputs):
+            g.inputs[g.n_inputs] = ga.inputs[i]
+            g.n_inputs += 1
+        for i in range(1, gb.n_inputs):
+            g.inputs[g.n_inputs] = gb.inputs[i] + off
+            g.n_inputs += 1
+        g.outputs[0] = gb.outputs[0] + off
+        g.n_outputs = 1
+        return out
+
     # -- export for the oracle -------------------------------------------------
     def to_list(self) -> list:
         """Plain-Python view of the nodes (for the CPU oracle)."""
