@@ -60,6 +60,8 @@ struct TcArgs {
     int num_m, num_n, num_tiles;
     int group_m;                   // rasterisation group along M
     unsigned long long timeout_ns; // per-wait deadline
+    int batch;                     // independent products (tiles: batch x num_m x num_n)
+    int a_batched, b_batched;      // operand has a batch dimension (3-D tensor map)
 };
 
 template <int VARIANT> struct TcCfg;
@@ -124,6 +126,12 @@ __device__ __forceinline__ void tma_load_2d(u32 dst, const TmaDesc* map, u32 bar
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar), "r"(x), "r"(y) : "memory");
+}
+// The same with a third (batch) coordinate.
+__device__ __forceinline__ void tma_load_3d(u32 dst, const TmaDesc* map, u32 bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar), "r"(x), "r"(y), "r"(z) : "memory");
 }
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -238,6 +246,11 @@ __device__ __forceinline__ void tma_load_2d_pair(u32 dst, const TmaDesc* map, u3
         "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
         ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar & 0xFEFFFFFFu), "r"(x), "r"(y) : "memory");
 }
+__device__ __forceinline__ void tma_load_3d_pair(u32 dst, const TmaDesc* map, u32 bar, int x, int y, int z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+        ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar & 0xFEFFFFFFu), "r"(x), "r"(y), "r"(z) : "memory");
+}
 __device__ __forceinline__ void tc_mma_tf32_pair(u32 tmem_d, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -255,7 +268,10 @@ __device__ __forceinline__ void tc_commit_pair(u32 bar) {
         ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int& nb) {
+__device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int& nb, int& bi) {
+    const int per_batch = g.num_m * g.num_n;
+    bi = t / per_batch;
+    t -= bi * per_batch;
     const int per_group = g.group_m * g.num_n;
     const int group = t / per_group;
     const int first_m = group * g.group_m;
@@ -332,9 +348,17 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
-                int mb, nb;
-                tile_coords(g, t, mb, nb);
+                int mb, nb, bi;
+                tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * BM, n0 = nb * BN;
+                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (g.a_batched) tma_load_3d(dst, m, bar, x, y, bi);
+                    else tma_load_2d(dst, m, bar, x, y);
+                };
+                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (g.b_batched) tma_load_3d(dst, m, bar, x, y, bi);
+                    else tma_load_2d(dst, m, bar, x, y);
+                };
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
@@ -350,15 +374,15 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                         const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
                         if (g.a_mn) {
                             for (int j = 0; j < BM / 32; ++j)
-                                tma_load_2d(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                                load_a(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
                         } else {
-                            tma_load_2d(ad, ma, FULL(s), k0, m0);
+                            load_a(ad, ma, FULL(s), k0, m0);
                         }
                         if (g.b_mn) {
                             for (int j = 0; j < BN / 32; ++j)
-                                tma_load_2d(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                                load_b(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
                         } else {
-                            tma_load_2d(bd, mbp, FULL(s), k0, n0);
+                            load_b(bd, mbp, FULL(s), k0, n0);
                         }
                     }
                     if (++s == STAGES) { s = 0; phase ^= 1u; }
@@ -457,8 +481,8 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                 mbar_arrive(TEMPTY(buf));
             }
             if (!ok) break;
-            int mb, nb;
-            tile_coords(g, t, mb, nb);
+            int mb, nb, bi;
+            tile_coords(g, t, mb, nb, bi);
             const i64 i = (i64)mb * BM + row_in_tile;
             const i64 n0 = (i64)nb * BN + half * 128;
             if (i < g.M) {
@@ -468,8 +492,8 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                     if (j < g.N) {
                         Vec4<typename Spec::Out> o;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, 0, i, j + e);
-                        st4(out + i * g.N + j, o);
+                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, bi, i, j + e);
+                        st4(out + bi * g.o_bstride + i * g.N + j, o);
                     }
                 }
             }
@@ -562,9 +586,17 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
             bool ok = true;
             for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
-                int mb, nb;
-                tile_coords(g, t, mb, nb);
+                int mb, nb, bi;
+                tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
+                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (g.a_batched) tma_load_3d_pair(dst, m, bar, x, y, bi);
+                    else tma_load_2d_pair(dst, m, bar, x, y);
+                };
+                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (g.b_batched) tma_load_3d_pair(dst, m, bar, x, y, bi);
+                    else tma_load_2d_pair(dst, m, bar, x, y);
+                };
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
@@ -582,15 +614,15 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
                         if (g.a_mn) {
                             for (int j = 0; j < BM / 32; ++j)
-                                tma_load_2d_pair(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                                load_a(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
                         } else {
-                            tma_load_2d_pair(ad, ma, FULL(s), k0, m0);
+                            load_a(ad, ma, FULL(s), k0, m0);
                         }
                         if (g.b_mn) {
                             for (int j = 0; j < (BN / 2) / 32; ++j)
-                                tma_load_2d_pair(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                                load_b(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
                         } else {
-                            tma_load_2d_pair(bd, mbp, FULL(s), k0, n0);
+                            load_b(bd, mbp, FULL(s), k0, n0);
                         }
                     }
                     if (++s == STAGES) { s = 0; phase ^= 1u; }
@@ -694,8 +726,8 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 else mbar_arrive_cluster(TEMPTY(buf), 0u);
             }
             if (!ok) break;
-            int mb, nb;
-            tile_coords(g, t, mb, nb);
+            int mb, nb, bi;
+            tile_coords(g, t, mb, nb, bi);
             const i64 i = (i64)mb * 2 * BM + (i64)cta * BM + row_in_tile;
             const i64 n0 = (i64)nb * BN + half * 128;
             if (i < g.M) {
@@ -705,8 +737,8 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     if (j < g.N) {
                         Vec4<typename Spec::Out> o;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, 0, i, j + e);
-                        st4(out + i * g.N + j, o);
+                        for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(acc[v + e], g, bi, i, j + e);
+                        st4(out + bi * g.o_bstride + i * g.N + j, o);
                     }
                 }
             }

@@ -632,11 +632,11 @@ struct Lowerer {
         return 0;
     }
 
-    // The tensor-core kernel reads A and B through TMA: row strides must be
-    // multiples of 16 bytes and the problem must not be batched.
+    // The tensor-core kernel reads A and B through TMA: row strides (and
+    // with them the per-batch strides) must be multiples of 16 bytes.
     bool tc_shape_ok(const Step& s) const {
         if (!tc_available()) return false;
-        if (s.batch != 1) return false;
+        if (s.batch < 1 || s.batch > (1 << 20)) return false;
         if (s.M < 1 || s.N < 1 || s.K < 1) return false;
         const int64_t a_ld = s.a_col ? s.M : s.K;
         const int64_t b_ld = s.b_col ? s.K : s.N;

@@ -29,6 +29,8 @@ struct alignas(64) TcArgsHost {
     int32_t num_m, num_n, num_tiles;
     int32_t group_m;
     unsigned long long timeout_ns;
+    int32_t batch;
+    int32_t a_batched, b_batched;
 };
 static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
 static_assert(sizeof(TcArgsHost) == 704, "TcArgs layout");
@@ -71,29 +73,33 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     TcArgsHost h;
     memset(&h, 0, sizeof(h));
     const uint64_t M = (uint64_t)s.M, N = (uint64_t)s.N, K = (uint64_t)s.K;
+    const uint64_t batch = (uint64_t)(s.batch > 1 ? s.batch : 1);
+    // An operand with its own matrix per batch item gets a 3-D map (the
+    // batch index is the third coordinate); one shared by all items, 2-D.
+    const bool a3 = batch > 1 && s.a_bstride != 0, b3 = batch > 1 && s.b_bstride != 0;
     // A: row-major = K-major (box 32 k x 128 rows, 128B swizzle); col-major =
     // M-major (stored [K][M]; boxes of 32 m x 32 k, 128B swizzle, 32B atoms).
     auto map_a = [&](CUtensorMap* m, const void* p) {
         if (s.a_col) {
-            uint64_t dims[2] = {M, K}, strides[1] = {M * 4};
-            uint32_t box[2] = {32, 32};
-            return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 2, err);
+            uint64_t dims[3] = {M, K, batch}, strides[2] = {M * 4, M * K * 4};
+            uint32_t box[3] = {32, 32, 1};
+            return tc_encode_tensor_map(m, 1, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 2, err);
         }
-        uint64_t dims[2] = {K, M}, strides[1] = {K * 4};
-        uint32_t box[2] = {32, (uint32_t)BM};
-        return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 1, err);
+        uint64_t dims[3] = {K, M, batch}, strides[2] = {K * 4, M * K * 4};
+        uint32_t box[3] = {32, (uint32_t)BM, 1};
+        return tc_encode_tensor_map(m, 1, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
     };
     // B: col-major = K-major (stored [N][K]; box 32 k x 256 cols);
     // row-major = N-major (stored [K][N]; boxes of 32 n x 32 k, 32B atoms).
     auto map_b = [&](CUtensorMap* m, const void* p) {
         if (s.b_col) {
-            uint64_t dims[2] = {K, N}, strides[1] = {K * 4};
-            uint32_t box[2] = {32, (uint32_t)(s.tc_pair ? BN / 2 : BN)};
-            return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 1, err);
+            uint64_t dims[3] = {K, N, batch}, strides[2] = {K * 4, K * N * 4};
+            uint32_t box[3] = {32, (uint32_t)(s.tc_pair ? BN / 2 : BN), 1};
+            return tc_encode_tensor_map(m, 1, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
         }
-        uint64_t dims[2] = {N, K}, strides[1] = {N * 4};
-        uint32_t box[2] = {32, 32};
-        return tc_encode_tensor_map(m, 1, 2, const_cast<void*>(p), dims, strides, box, 2, err);
+        uint64_t dims[3] = {N, K, batch}, strides[2] = {N * 4, K * N * 4};
+        uint32_t box[3] = {32, 32, 1};
+        return tc_encode_tensor_map(m, 1, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 2, err);
     };
     if (int rc = map_a(&h.tmap_a, a)) return rc;
     if (int rc = map_b(&h.tmap_b, b)) return rc;
@@ -113,7 +119,10 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     const int tile_m = s.tc_pair ? 2 * BM : BM;   // a CTA pair covers 256 rows
     h.num_m = (int)((s.M + tile_m - 1) / tile_m);
     h.num_n = (int)((s.N + BN - 1) / BN);
-    int64_t tiles = (int64_t)h.num_m * h.num_n;
+    h.batch = (int32_t)batch;
+    h.a_batched = a3 ? 1 : 0;
+    h.b_batched = b3 ? 1 : 0;
+    int64_t tiles = (int64_t)h.num_m * h.num_n * (int64_t)batch;
     if (tiles > (1LL << 30)) {
         err = "tensor-core GEMM: too many tiles";
         return 12;

@@ -163,3 +163,48 @@ def test_host_pointer_path_tensor_cores(cuda):
     ref = np.maximum(A.astype(np.float64) @ B.astype(np.float64) + C, 0)
     assert "a=row b=col" in f.kernel_for(A, B, C).describe()
     assert np.max(np.abs(out - ref)) <= 1e-4 * math.sqrt(384 / 64)
+
+
+# ---------------------------------------------------------------- batched --
+# Rank-3 products (the emitter's batched loop, codegen.c:215-236): each batch
+# item is its own GEMM; an operand without a batch dimension is shared.  The
+# tensor-core kernels take the batch index as the third TMA coordinate.
+
+@pytest.mark.parametrize("batch,M,N,K,a_col,b_col,b_shared", [
+    (3, 256, 320, 192, 0, 0, False),
+    (4, 300, 260, 520, 1, 1, False),
+    (5, 512, 256, 256, 0, 1, True),
+    (2, 128, 1024, 2048, 1, 0, True),
+])
+@pytest.mark.parametrize("prec", ["3xtf32", "tf32"])
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_batched_gemm_on_tensor_cores(cuda, batch, M, N, K, a_col, b_col, b_shared, prec, pair):
+    torch = cuda
+    gen = torch.Generator(device="cuda").manual_seed(batch * 131 + M)
+    A = torch.randn(batch, M, K, device="cuda", generator=gen)
+    B = torch.randn(K, N, device="cuda", generator=gen) if b_shared else \
+        torch.randn(batch, K, N, device="cuda", generator=gen)
+    C = torch.randn(batch, M, N, device="cuda", generator=gen)
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", (batch, M, K), 0, 1 if a_col else 0)
+    b = g.add_input("B", tuple(B.shape), 0, 1 if b_col else 0)
+    c = g.add_input("C", (batch, M, N), 0, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
+    bafe.set_option("gemm_precision", prec)
+    bafe.set_option("tc_pair", pair)
+    try:
+        k = bafe.compile_graph(g)
+        assert ("gemm.tc.3xtf32" if prec == "3xtf32" else "gemm.tc.tf32") in k.describe()
+        assert f"batch={batch}" in k.describe()
+        a_store = A.transpose(1, 2).contiguous() if a_col else A
+        b_store = B.transpose(-1, -2).contiguous() if b_col else B
+        out = torch.full((batch, M, N), float("nan"), device="cuda")
+        k.run_torch([a_store, b_store, C], out)
+        bafe.synchronize()
+    finally:
+        bafe.set_option("tc_pair", "1")
+    ref = torch.relu(torch.matmul(A.double(), B.double()) + C.double())
+    err = float((out.double() - ref).abs().max())
+    tol = (1e-4 if prec == "3xtf32" else TF32_TOL) * math.sqrt(K / 64)
+    print(f"batched {prec} pair={pair} {batch}x{M}x{N}x{K}: max err {err:.3e} (bound {tol:.3e})")
+    assert err <= tol
