@@ -110,6 +110,7 @@ struct Step {
     bool direct = false;           // fused-form summation order (one chunk)
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
     bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
+    int tc_elem = 0;               // GemmTc operands: 0 = f32 (tf32 MMAs), 1 = bf16 (kind::f16)
     std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
     // Row streaming of host calls (analyse_row_streaming): the step runs
     // once per row panel of the output (panel) or once per call; buffers

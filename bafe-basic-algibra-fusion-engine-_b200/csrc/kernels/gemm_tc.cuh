@@ -153,6 +153,14 @@ __device__ __forceinline__ void tc_mma_tf32(u32 tmem_d, u64 adesc, u64 bdesc, u3
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
           "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
 }
+__device__ __forceinline__ void tc_mma_f16kind(u32 tmem_d, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
+          "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
+}
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets row
 // (lane base + t), columns [col, col+32).  tmem_ld32_nowait issues the load
 // only; tmem_wait_ld waits for every load issued before it.
@@ -195,10 +203,10 @@ __device__ __forceinline__ u64 smem_desc(u32 addr, u32 lbo, u32 sbo, u32 layout)
     return d;
 }
 
-// Instruction descriptor: D f32, A/B tf32, majors, N, M (128, or 256 for
-// a CTA pair).
-__device__ __forceinline__ u32 instr_desc(int a_mn, int b_mn, int n, int m = BM) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((u32)a_mn << 15) | ((u32)b_mn << 16) |
+// Instruction descriptor: D f32, A/B format (kind::tf32: 2 = TF32;
+// kind::f16: 0 = F16, 1 = BF16), majors, N, M (128, or 256 for a CTA pair).
+__device__ __forceinline__ u32 instr_desc(int a_mn, int b_mn, int n, int m = BM, u32 fmt = 2u) {
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((u32)a_mn << 15) | ((u32)b_mn << 16) |
            ((u32)(n >> 3) << 17) | ((u32)(m >> 4) << 24);
 }
 
@@ -259,6 +267,14 @@ __device__ __forceinline__ void tc_mma_tf32_pair(u32 tmem_d, u64 adesc, u64 bdes
         ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
           "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
 }
+__device__ __forceinline__ void tc_mma_f16kind_pair(u32 tmem_d, u64 adesc, u64 bdesc, u32 idesc, u32 accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate),
+          "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u) : "memory");
+}
 // Completion of the pair's prior MMAs signalled on the barrier at offset
 // `bar` in both CTAs of the pair (tcgen05.commit, not a load).
 __device__ __forceinline__ void tc_commit_pair(u32 bar) {
@@ -284,14 +300,43 @@ __device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int
 
 }  // namespace tc
 
-template <class Spec, int VARIANT>
+// Operand element types.  A k-block is one 128-byte swizzle row of K: 32
+// tf32 or 64 bf16 elements; an MMA consumes 32 bytes of K (8 tf32 under
+// kind::tf32, 16 bf16 under kind::f16), four MMAs per k-block, so stage
+// sizes and K-major descriptors are the same in bytes.  MN-major tiles
+// differ: tf32 needs the 128B swizzle with 32-byte atoms (32 elements per
+// row, 4-row K groups), bf16 uses the plain 128B swizzle (64 elements per
+// row, 8-row K groups).
+struct ElemTf32 {
+    static constexpr int BYTES = 4, BKE = 32;       // elements per k-block
+    static constexpr u32 FMT = 2u;                   // instruction-descriptor a/b format
+    static constexpr int MN_ATOM = 32;               // MN elements per swizzle row
+    static constexpr u32 MN_LT = 1u, MN_SBO = 512u, MN_KK = 1024u;   // layout, K-group stride, per-MMA advance
+    static constexpr int KB_CHUNK = 0;               // promotion chunk: the config's
+    __device__ static __forceinline__ void mma(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_tf32(d, a, b, idesc, acc); }
+    __device__ static __forceinline__ void mma_pair(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_tf32_pair(d, a, b, idesc, acc); }
+};
+struct ElemBf16 {
+    static constexpr int BYTES = 2, BKE = 64;
+    static constexpr u32 FMT = 1u;
+    static constexpr int MN_ATOM = 64;
+    static constexpr u32 MN_LT = 2u, MN_SBO = 1024u, MN_KK = 2048u;
+    static constexpr int KB_CHUNK = 2;               // products are exact: promote every 128 k
+    __device__ static __forceinline__ void mma(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_f16kind(d, a, b, idesc, acc); }
+    __device__ static __forceinline__ void mma_pair(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_f16kind_pair(d, a, b, idesc, acc); }
+};
+
+template <class Spec, int VARIANT, class E = ElemTf32>
 __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     using namespace tc;
     typedef TcCfg<VARIANT> Cfg;
     constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES;
     constexpr bool SPLIT = VARIANT == 3;
-    constexpr int KB_PER_CHUNK = Cfg::KB_PER_CHUNK;
-    constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB
+    static_assert(!SPLIT || E::BYTES == 4, "the 3-product split is for fp32 operands");
+    constexpr int KB_PER_CHUNK = E::KB_CHUNK ? E::KB_CHUNK : Cfg::KB_PER_CHUNK;
+    constexpr int BKE = E::BKE;                      // elements per k-block
+    constexpr u32 MN_BOX = BKE * 128u;              // one MN-major box: a k-block of 128-byte rows
+    constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB (128 rows x 128 B)
     constexpr u32 B_BYTES = BN * BK * 4;            // 32 KB
     constexpr u32 STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
     constexpr u32 TMEM_COLS = 2 * BN;
@@ -336,7 +381,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     __syncthreads();
     tc_fence_after();
     const u32 tmem = sh->tmem_base;
-    const int k_blocks = (int)((g.K + BK - 1) / BK);
+    const int k_blocks = (int)((g.K + BKE - 1) / BKE);
     const int n_chunks = (k_blocks + KB_PER_CHUNK - 1) / KB_PER_CHUNK;
 
     if (warp == 0) {
@@ -365,7 +410,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                     const u32 b_dst = a_dst + A_BYTES;
                     mbar_expect_tx(FULL(s), STAGE_BYTES);
                     armed[s] = phase;
-                    const int k0 = kb * BK;
+                    const int k0 = kb * BKE;
 #pragma unroll
                     for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
                         const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
@@ -373,14 +418,14 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                         const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
                         const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
                         if (g.a_mn) {
-                            for (int j = 0; j < BM / 32; ++j)
-                                load_a(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                            for (int j = 0; j < BM / E::MN_ATOM; ++j)
+                                load_a(ad + j * MN_BOX, ma, FULL(s), m0 + E::MN_ATOM * j, k0);
                         } else {
                             load_a(ad, ma, FULL(s), k0, m0);
                         }
                         if (g.b_mn) {
-                            for (int j = 0; j < BN / 32; ++j)
-                                load_b(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                            for (int j = 0; j < BN / E::MN_ATOM; ++j)
+                                load_b(bd + j * MN_BOX, mbp, FULL(s), n0 + E::MN_ATOM * j, k0);
                         } else {
                             load_b(bd, mbp, FULL(s), k0, n0);
                         }
@@ -398,10 +443,10 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     } else if (warp == 1) {
         // ------------------------------------------------- MMA issuer --
         if (lane == 0) {
-            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN);
-            const u32 a_lbo = g.a_mn ? 32u * BK * 4u : 16u, b_lbo = g.b_mn ? 32u * BK * 4u : 16u;
-            const u32 a_sbo = g.a_mn ? 512u : 1024u, b_sbo = g.b_mn ? 512u : 1024u;
-            const u32 a_lt = g.a_mn ? 1u : 2u, b_lt = g.b_mn ? 1u : 2u;
+            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN, BM, E::FMT);
+            const u32 a_lbo = g.a_mn ? MN_BOX : 16u, b_lbo = g.b_mn ? MN_BOX : 16u;
+            const u32 a_sbo = g.a_mn ? E::MN_SBO : 1024u, b_sbo = g.b_mn ? E::MN_SBO : 1024u;
+            const u32 a_lt = g.a_mn ? E::MN_LT : 2u, b_lt = g.b_mn ? E::MN_LT : 2u;
             int s = 0;
             u32 phase = 0;
             u32 chunk = 0;                              // chunks issued by this CTA
@@ -422,20 +467,20 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                         const u32 a_lo = a_hi + A_BYTES + B_BYTES;
                         const u32 b_lo = a_lo + A_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < BK / 8; ++kk) {
-                            // K-major: 8 tf32 = 32 B further along the row;
-                            // MN-major: the next 8 k-rows (1024 B).
-                            const u32 ao = g.a_mn ? kk * 1024u : kk * 32u;
-                            const u32 bo = g.b_mn ? kk * 1024u : kk * 32u;
+                        for (int kk = 0; kk < 4; ++kk) {
+                            // K-major: 32 B further along the row; MN-major:
+                            // the next 8 (tf32) / 16 (bf16) k-rows.
+                            const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
+                            const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
                             const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
                             const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
                             const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
-                            tc_mma_tf32(d, ah, bh, idesc, acc);
+                            E::mma(d, ah, bh, idesc, acc);
                             if (SPLIT) {
                                 const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
                                 const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
-                                tc_mma_tf32(d, ah, bl, idesc, 1u);
-                                tc_mma_tf32(d, al, bh, idesc, 1u);
+                                E::mma(d, ah, bl, idesc, 1u);
+                                E::mma(d, al, bh, idesc, 1u);
                             }
                         }
                         tc_commit(EMPTY(s));           // stage free once these MMAs finish
@@ -520,13 +565,16 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
 // committed to the barriers of both CTAs; the accumulate warps of both
 // CTAs release a TMEM chunk buffer by arriving on the leader's barrier.
 // Roles, chunked register accumulation, bounded waits as in gemm_tc.
-template <class Spec, int VARIANT>
+template <class Spec, int VARIANT, class E = ElemTf32>
 __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     using namespace tc;
     typedef TcPairCfg<VARIANT> Cfg;
     constexpr int BN = 256, STAGES = Cfg::STAGES;
     constexpr bool SPLIT = VARIANT == 3;
-    constexpr int KB_PER_CHUNK = Cfg::KB_PER_CHUNK;
+    static_assert(!SPLIT || E::BYTES == 4, "the 3-product split is for fp32 operands");
+    constexpr int KB_PER_CHUNK = E::KB_CHUNK ? E::KB_CHUNK : Cfg::KB_PER_CHUNK;
+    constexpr int BKE = E::BKE;
+    constexpr u32 MN_BOX = BKE * 128u;
     constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB: this CTA's 128 rows
     constexpr u32 B_BYTES = (BN / 2) * BK * 4;      // 16 KB: this CTA's half of B
     constexpr u32 STAGE_BYTES = (A_BYTES + B_BYTES) * (SPLIT ? 2 : 1);
@@ -574,7 +622,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     cluster_sync();                                  // both CTAs' barriers exist
     tc_fence_after();
     const u32 tmem = sh->tmem_base;
-    const int k_blocks = (int)((g.K + BK - 1) / BK);
+    const int k_blocks = (int)((g.K + BKE - 1) / BKE);
     const int n_chunks = (k_blocks + KB_PER_CHUNK - 1) / KB_PER_CHUNK;
 
     if (warp == 0) {
@@ -605,7 +653,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         mbar_expect_tx(FULL(s), 2 * STAGE_BYTES);   // both CTAs' bytes
                         armed[s] = phase;
                     }
-                    const int k0 = kb * BK;
+                    const int k0 = kb * BKE;
 #pragma unroll
                     for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
                         const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
@@ -613,14 +661,14 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
                         const u32 bd = b_dst + part * (A_BYTES + B_BYTES);
                         if (g.a_mn) {
-                            for (int j = 0; j < BM / 32; ++j)
-                                load_a(ad + j * (32 * BK * 4), ma, FULL(s), m0 + 32 * j, k0);
+                            for (int j = 0; j < BM / E::MN_ATOM; ++j)
+                                load_a(ad + j * MN_BOX, ma, FULL(s), m0 + E::MN_ATOM * j, k0);
                         } else {
                             load_a(ad, ma, FULL(s), k0, m0);
                         }
                         if (g.b_mn) {
-                            for (int j = 0; j < (BN / 2) / 32; ++j)
-                                load_b(bd + j * (32 * BK * 4), mbp, FULL(s), n0 + 32 * j, k0);
+                            for (int j = 0; j < (BN / 2) / E::MN_ATOM; ++j)
+                                load_b(bd + j * MN_BOX, mbp, FULL(s), n0 + E::MN_ATOM * j, k0);
                         } else {
                             load_b(bd, mbp, FULL(s), k0, n0);
                         }
@@ -641,10 +689,10 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     } else if (warp == 1) {
         // --------------------------------------- MMA issuer (leader CTA) --
         if (lane == 0 && cta == 0) {
-            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN, 2 * BM);
-            const u32 a_lbo = g.a_mn ? 32u * BK * 4u : 16u, b_lbo = g.b_mn ? 32u * BK * 4u : 16u;
-            const u32 a_sbo = g.a_mn ? 512u : 1024u, b_sbo = g.b_mn ? 512u : 1024u;
-            const u32 a_lt = g.a_mn ? 1u : 2u, b_lt = g.b_mn ? 1u : 2u;
+            const u32 idesc = instr_desc(g.a_mn, g.b_mn, BN, 2 * BM, E::FMT);
+            const u32 a_lbo = g.a_mn ? MN_BOX : 16u, b_lbo = g.b_mn ? MN_BOX : 16u;
+            const u32 a_sbo = g.a_mn ? E::MN_SBO : 1024u, b_sbo = g.b_mn ? E::MN_SBO : 1024u;
+            const u32 a_lt = g.a_mn ? E::MN_LT : 2u, b_lt = g.b_mn ? E::MN_LT : 2u;
             int s = 0;
             u32 phase = 0;
             u32 chunk = 0;
@@ -665,18 +713,18 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         const u32 a_lo = a_hi + A_BYTES + B_BYTES;
                         const u32 b_lo = a_lo + A_BYTES;
 #pragma unroll
-                        for (int kk = 0; kk < BK / 8; ++kk) {
-                            const u32 ao = g.a_mn ? kk * 1024u : kk * 32u;
-                            const u32 bo = g.b_mn ? kk * 1024u : kk * 32u;
+                        for (int kk = 0; kk < 4; ++kk) {
+                            const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
+                            const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
                             const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
                             const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
                             const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
-                            tc_mma_tf32_pair(d, ah, bh, idesc, acc);
+                            E::mma_pair(d, ah, bh, idesc, acc);
                             if (SPLIT) {
                                 const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
                                 const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
-                                tc_mma_tf32_pair(d, ah, bl, idesc, 1u);
-                                tc_mma_tf32_pair(d, al, bh, idesc, 1u);
+                                E::mma_pair(d, ah, bl, idesc, 1u);
+                                E::mma_pair(d, al, bh, idesc, 1u);
                             }
                         }
                         tc_commit_pair(EMPTY(s));      // both CTAs' stage s is free

@@ -35,6 +35,20 @@ extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) che
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_tc1_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpec, 1>(g);
 }
+// bf16 operands (kind::f16), bf16 output through the emitter's conversion.
+struct CheckSpecBf16 {
+    typedef float TA; typedef float TB; typedef float T; typedef float P; typedef float S;
+    typedef u16 Out;
+    template <class G> static __device__ __forceinline__ Out apply(T acc, const G& g, i64 b, i64 i, i64 j) {
+        return bafe::f32_to_bf16(bafe::relu(acc));
+    }
+};
+extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_bf16_pair(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_pair<CheckSpecBf16, 1, bafe::ElemBf16>(g);
+}
+extern "C" __global__ void __launch_bounds__(bafe::TcCfg<1>::THREADS, 1) check_gemm_bf16(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc<CheckSpecBf16, 1, bafe::ElemBf16>(g);
+}
 extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
     bafe::transpose2d<float>(x, out, M, N);
 }

@@ -531,15 +531,22 @@ struct Lowerer {
         if (R) for (auto& l : R->leaves) leaves.push_back(l);
         if (leaves.size() > 8) { err = "GEMM epilogue reads more than 8 operands"; return 2; }
 
-        // Tensor-core path choice.
+        // Tensor-core path choice.  f32 operands: tf32 MMAs (3xTF32 split by
+        // default).  bf16 operands: kind::f16 MMAs -- the emitter converts
+        // bf16 to f32 exactly (codegen.c:85-127) and bf16 x bf16 products are
+        // exact in f32, so only the accumulation differs.  f16 operands stay
+        // on the exact kernel: the emitter's f16 -> f32 conversion rescales
+        // subnormals, which the tensor core would read as IEEE values.
         const std::string& prec = opt.gemm_precision;
-        bool tc_ok = T == BAFE_DTYPE_F32 && TA == BAFE_DTYPE_F32 && TB == BAFE_DTYPE_F32 &&
-                     a.dtype == BAFE_DTYPE_F32 && b.dtype == BAFE_DTYPE_F32 && tc_shape_ok(s);
-        if (tc_ok && prec != "exact") {
+        const bool f32_ops = T == BAFE_DTYPE_F32 && TA == BAFE_DTYPE_F32 && TB == BAFE_DTYPE_F32 &&
+                             a.dtype == BAFE_DTYPE_F32 && b.dtype == BAFE_DTYPE_F32;
+        const bool bf16_ops = T == BAFE_DTYPE_F32 && a.dtype == BAFE_DTYPE_BF16 && b.dtype == BAFE_DTYPE_BF16;
+        if ((f32_ops || bf16_ops) && tc_shape_ok(s, f32_ops ? 4 : 2) && prec != "exact") {
             bool big = (double)M * (double)Nn * (double)K >= 16777216.0;   // 256^3
             if (prec == "tf32" || prec == "3xtf32" || big) {
                 s.kind = StepKind::GemmTc;
-                s.tc_variant = prec == "tf32" ? 1 : 3;
+                s.tc_variant = (bf16_ops || prec == "tf32") ? 1 : 3;
+                s.tc_elem = bf16_ops ? 1 : 0;
                 s.tc_pair = opt.tc_pair;
             }
         }
@@ -617,14 +624,16 @@ struct Lowerer {
         } else {
             const char* cfg = s.tc_pair ? "TcPairCfg" : "TcCfg";
             const char* fn = s.tc_pair ? "gemm_tc_pair" : "gemm_tc";
+            const char* elem = s.tc_elem == 1 ? "bafe::ElemBf16" : "bafe::ElemTf32";
             src << "extern \"C\" __global__ void __launch_bounds__(bafe::" << cfg << "<" << s.tc_variant
                 << ">::THREADS, 1) " << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::" << fn << "<"
-                << S_ << ", " << s.tc_variant << ">(g); }\n";
+                << S_ << ", " << s.tc_variant << ", " << elem << ">(g); }\n";
         }
         char geo[256];
         snprintf(geo, sizeof(geo), " batch=%lld m=%lld n=%lld k=%lld a=%s b=%s", (long long)batch, (long long)M,
                  (long long)Nn, (long long)K, s.a_col ? "col" : "row", s.b_col ? "col" : "row");
-        std::string kindname = s.kind == StepKind::GemmTc ? std::string(s.tc_variant == 1 ? "gemm.tc.tf32" : "gemm.tc.3xtf32") +
+        std::string kindname = s.kind == StepKind::GemmTc ? std::string(s.tc_elem == 1 ? "gemm.tc.bf16"
+                                                                        : s.tc_variant == 1 ? "gemm.tc.tf32" : "gemm.tc.3xtf32") +
                                                                 (s.tc_pair ? ".pair" : "")
                                                           : (s.direct ? "gemm.exact.direct" : "gemm.exact.chunk32");
         s.describe = kindname + geo + " epi=" + epi_desc + " -> " + bufname(s.dst);
@@ -634,13 +643,13 @@ struct Lowerer {
 
     // The tensor-core kernel reads A and B through TMA: row strides (and
     // with them the per-batch strides) must be multiples of 16 bytes.
-    bool tc_shape_ok(const Step& s) const {
+    bool tc_shape_ok(const Step& s, int esize) const {
         if (!tc_available()) return false;
         if (s.batch < 1 || s.batch > (1 << 20)) return false;
         if (s.M < 1 || s.N < 1 || s.K < 1) return false;
         const int64_t a_ld = s.a_col ? s.M : s.K;
         const int64_t b_ld = s.b_col ? s.K : s.N;
-        if ((a_ld * 4) % 16 || (b_ld * 4) % 16) return false;
+        if ((a_ld * esize) % 16 || (b_ld * esize) % 16) return false;
         if (s.N % 4) return false;   // vectorised epilogue
         return true;
     }

@@ -236,7 +236,7 @@ int sm_count(int dev) {
 }  // namespace
 
 // Driver calls used by the tensor-core launcher (tc_launch.cpp).
-int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
+int tc_encode_tensor_map(void* map, int elem, int rank, void* gaddr, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err) {
     Driver& d = driver();
     if (!d.ok) { err = d.why; return 4; }
@@ -245,7 +245,9 @@ int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, con
     for (int i = 0; i < rank; ++i) { gd[i] = dims[i]; bx[i] = box[i]; es[i] = 1; }
     for (int i = 0; i < rank - 1; ++i) gs[i] = strides_bytes[i];
     CUresult r = d.tensorMapEncodeTiled(
-        reinterpret_cast<CUtensorMap*>(map), dtype_is_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8,
+        reinterpret_cast<CUtensorMap*>(map),
+        elem == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                  : (elem == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8),
         (cuuint32_t)rank, gaddr, gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
         swizzle == 2 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
                      : (swizzle == 1 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE),

@@ -74,6 +74,14 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     memset(&h, 0, sizeof(h));
     const uint64_t M = (uint64_t)s.M, N = (uint64_t)s.N, K = (uint64_t)s.K;
     const uint64_t batch = (uint64_t)(s.batch > 1 ? s.batch : 1);
+    // Element size and the k-block width in elements (one 128-byte row):
+    // f32 32, bf16 64.  K-major boxes: k-block x rows; MN-major boxes:
+    // 128 B of MN (32 f32 with 32-byte atoms, 64 bf16 plain 128B swizzle)
+    // x k-block rows.
+    const bool bf16 = s.tc_elem == 1;
+    const uint64_t es = bf16 ? 2 : 4;
+    const uint32_t bke = bf16 ? 64 : 32, mn_atom = bf16 ? 64 : 32;
+    const int elem = bf16 ? 2 : 1, mn_swz = bf16 ? 1 : 2;
     // An operand with its own matrix per batch item gets a 3-D map (the
     // batch index is the third coordinate); one shared by all items, 2-D.
     const bool a3 = batch > 1 && s.a_bstride != 0, b3 = batch > 1 && s.b_bstride != 0;
@@ -81,25 +89,25 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     // M-major (stored [K][M]; boxes of 32 m x 32 k, 128B swizzle, 32B atoms).
     auto map_a = [&](CUtensorMap* m, const void* p) {
         if (s.a_col) {
-            uint64_t dims[3] = {M, K, batch}, strides[2] = {M * 4, M * K * 4};
-            uint32_t box[3] = {32, 32, 1};
-            return tc_encode_tensor_map(m, 1, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 2, err);
+            uint64_t dims[3] = {M, K, batch}, strides[2] = {M * es, M * K * es};
+            uint32_t box[3] = {mn_atom, bke, 1};
+            return tc_encode_tensor_map(m, elem, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, mn_swz, err);
         }
-        uint64_t dims[3] = {K, M, batch}, strides[2] = {K * 4, M * K * 4};
-        uint32_t box[3] = {32, (uint32_t)BM, 1};
-        return tc_encode_tensor_map(m, 1, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
+        uint64_t dims[3] = {K, M, batch}, strides[2] = {K * es, M * K * es};
+        uint32_t box[3] = {bke, (uint32_t)BM, 1};
+        return tc_encode_tensor_map(m, elem, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
     };
     // B: col-major = K-major (stored [N][K]; box 32 k x 256 cols);
     // row-major = N-major (stored [K][N]; boxes of 32 n x 32 k, 32B atoms).
     auto map_b = [&](CUtensorMap* m, const void* p) {
         if (s.b_col) {
-            uint64_t dims[3] = {K, N, batch}, strides[2] = {K * 4, K * N * 4};
-            uint32_t box[3] = {32, (uint32_t)(s.tc_pair ? BN / 2 : BN), 1};
-            return tc_encode_tensor_map(m, 1, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
+            uint64_t dims[3] = {K, N, batch}, strides[2] = {K * es, K * N * es};
+            uint32_t box[3] = {bke, (uint32_t)(s.tc_pair ? BN / 2 : BN), 1};
+            return tc_encode_tensor_map(m, elem, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
         }
-        uint64_t dims[3] = {N, K, batch}, strides[2] = {N * 4, K * N * 4};
-        uint32_t box[3] = {32, 32, 1};
-        return tc_encode_tensor_map(m, 1, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 2, err);
+        uint64_t dims[3] = {N, K, batch}, strides[2] = {N * es, K * N * es};
+        uint32_t box[3] = {mn_atom, bke, 1};
+        return tc_encode_tensor_map(m, elem, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, mn_swz, err);
     };
     if (int rc = map_a(&h.tmap_a, a)) return rc;
     if (int rc = map_b(&h.tmap_b, b)) return rc;

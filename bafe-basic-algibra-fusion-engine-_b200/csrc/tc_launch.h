@@ -17,8 +17,8 @@ int tc_smem_bytes(int variant, bool pair = false);
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,
                std::string& err);
-// swizzle: 0 none, 1 = 128B, 2 = 128B with 32-byte atoms
-int tc_encode_tensor_map(void* map, int dtype_is_f32, int rank, void* gaddr, const uint64_t* dims,
+// elem: 0 = u8, 1 = f32, 2 = bf16; swizzle: 0 none, 1 = 128B, 2 = 128B with 32-byte atoms
+int tc_encode_tensor_map(void* map, int elem, int rank, void* gaddr, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err);
 
 }  // namespace bafe_cuda
