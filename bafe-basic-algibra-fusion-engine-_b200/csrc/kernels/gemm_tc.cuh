@@ -61,7 +61,7 @@ struct TcArgs {
     int group_m;                   // rasterisation group along M
     unsigned long long timeout_ns; // per-wait deadline
     int batch;                     // independent products (tiles: batch x num_m x num_n)
-    int a_batched, b_batched;      // operand has a batch dimension (3-D tensor map)
+    int a_batched, b_batched;      // operand has its own matrix per batch item
 };
 
 template <int VARIANT> struct TcCfg;
@@ -396,14 +396,12 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                 int mb, nb, bi;
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * BM, n0 = nb * BN;
-                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
-                    if (g.a_batched) tma_load_3d(dst, m, bar, x, y, bi);
-                    else tma_load_2d(dst, m, bar, x, y);
-                };
-                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
-                    if (g.b_batched) tma_load_3d(dst, m, bar, x, y, bi);
-                    else tma_load_2d(dst, m, bar, x, y);
-                };
+                // Every operand map is 3-D (batch extent 1 when the operand
+                // is shared): the batch coordinate is fixed per tile, so the
+                // k-loop issues one load form without a branch.
+                const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
+                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d(dst, m, bar, x, y, za); };
+                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d(dst, m, bar, x, y, zb); };
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
@@ -637,14 +635,9 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 int mb, nb, bi;
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
-                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
-                    if (g.a_batched) tma_load_3d_pair(dst, m, bar, x, y, bi);
-                    else tma_load_2d_pair(dst, m, bar, x, y);
-                };
-                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
-                    if (g.b_batched) tma_load_3d_pair(dst, m, bar, x, y, bi);
-                    else tma_load_2d_pair(dst, m, bar, x, y);
-                };
+                const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
+                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d_pair(dst, m, bar, x, y, za); };
+                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d_pair(dst, m, bar, x, y, zb); };
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;

@@ -82,32 +82,34 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     const uint64_t es = bf16 ? 2 : 4;
     const uint32_t bke = bf16 ? 64 : 32, mn_atom = bf16 ? 64 : 32;
     const int elem = bf16 ? 2 : 1, mn_swz = bf16 ? 1 : 2;
-    // An operand with its own matrix per batch item gets a 3-D map (the
-    // batch index is the third coordinate); one shared by all items, 2-D.
+    // Every map is 3-D: an operand with its own matrix per batch item has
+    // the batch as third dimension, one shared by all items (or an
+    // unbatched product) extent 1 there, read at batch coordinate 0.
     const bool a3 = batch > 1 && s.a_bstride != 0, b3 = batch > 1 && s.b_bstride != 0;
+    const uint64_t a_batch = a3 ? batch : 1, b_batch = b3 ? batch : 1;
     // A: row-major = K-major (box 32 k x 128 rows, 128B swizzle); col-major =
     // M-major (stored [K][M]; boxes of 32 m x 32 k, 128B swizzle, 32B atoms).
     auto map_a = [&](CUtensorMap* m, const void* p) {
         if (s.a_col) {
-            uint64_t dims[3] = {M, K, batch}, strides[2] = {M * es, M * K * es};
+            uint64_t dims[3] = {M, K, a_batch}, strides[2] = {M * es, M * K * es};
             uint32_t box[3] = {mn_atom, bke, 1};
-            return tc_encode_tensor_map(m, elem, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, mn_swz, err);
+            return tc_encode_tensor_map(m, elem, 3, const_cast<void*>(p), dims, strides, box, mn_swz, err);
         }
-        uint64_t dims[3] = {K, M, batch}, strides[2] = {K * es, M * K * es};
+        uint64_t dims[3] = {K, M, a_batch}, strides[2] = {K * es, M * K * es};
         uint32_t box[3] = {bke, (uint32_t)BM, 1};
-        return tc_encode_tensor_map(m, elem, a3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
+        return tc_encode_tensor_map(m, elem, 3, const_cast<void*>(p), dims, strides, box, 1, err);
     };
     // B: col-major = K-major (stored [N][K]; box 32 k x 256 cols);
     // row-major = N-major (stored [K][N]; boxes of 32 n x 32 k, 32B atoms).
     auto map_b = [&](CUtensorMap* m, const void* p) {
         if (s.b_col) {
-            uint64_t dims[3] = {K, N, batch}, strides[2] = {K * es, K * N * es};
+            uint64_t dims[3] = {K, N, b_batch}, strides[2] = {K * es, K * N * es};
             uint32_t box[3] = {bke, (uint32_t)(s.tc_pair ? BN / 2 : BN), 1};
-            return tc_encode_tensor_map(m, elem, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, 1, err);
+            return tc_encode_tensor_map(m, elem, 3, const_cast<void*>(p), dims, strides, box, 1, err);
         }
-        uint64_t dims[3] = {N, K, batch}, strides[2] = {N * es, K * N * es};
+        uint64_t dims[3] = {N, K, b_batch}, strides[2] = {N * es, K * N * es};
         uint32_t box[3] = {mn_atom, bke, 1};
-        return tc_encode_tensor_map(m, elem, b3 ? 3 : 2, const_cast<void*>(p), dims, strides, box, mn_swz, err);
+        return tc_encode_tensor_map(m, elem, 3, const_cast<void*>(p), dims, strides, box, mn_swz, err);
     };
     if (int rc = map_a(&h.tmap_a, a)) return rc;
     if (int rc = map_b(&h.tmap_b, b)) return rc;

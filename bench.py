@@ -8,7 +8,9 @@ Headline workload (one "step" = one call of the plan):
         rows are split into contiguous row panels, one per rank; B is
         broadcast once from rank 0 over NCCL (outside the timed region, as
         the runtime keeps B resident; its time is reported separately).
-Secondary (same JSON line, keys "ew" and "transpose"):
+Secondary (same JSON line, keys "gemm_bf16", "ew" and "transpose"):
+  gemm_bf16: the same fused GEMM with bf16 A, B, C and output (kind::f16
+        tensor cores, f32 accumulation).
   ew:   relu(add(mul(X,Y),Z)) over 2^28 fp32 elements (1 GiB per vector),
         range-split across ranks with no collective.  Metric GB/s
         (16 bytes per element).
@@ -411,6 +413,49 @@ def bench_gemm(c: Ctx) -> dict:
     return res
 
 
+def bench_gemm_bf16(c: Ctx) -> dict:
+    """The same fused GEMM with bf16 A, B, C and output (kind::f16 tensor
+    cores, f32 accumulation): device-resident, row panels per rank."""
+    import bafe_b200 as bafe
+    torch, args = c.torch, c.args
+    from bafe_b200.parallel import broadcast_resident, row_panels
+    S = args.gemm_size
+    r0, r1 = row_panels(S, c.world)[c.rank]
+    rows = r1 - r0
+    std = 1.0 / math.sqrt(S)
+    A = (torch.randn(rows, S, device=c.dev, generator=c.gen) * std).to(torch.bfloat16).view(torch.int16)
+    C = (torch.randn(rows, S, device=c.dev, generator=c.gen) * std).to(torch.bfloat16).view(torch.int16)
+    B = (torch.randn(S, S, device=c.dev, generator=c.gen) * std).to(torch.bfloat16).view(torch.int16)
+    if c.dist is not None:
+        broadcast_resident(B, c.dist, src=0)
+    out = torch.empty(rows, S, dtype=torch.int16, device=c.dev)
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", (rows, S), 5, 0)
+    b = g.add_input("B", (S, S), 5, 2)
+    cc = g.add_input("C", (rows, S), 5, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), cc])]))
+    k = bafe.compile_graph(g)
+    c.barrier()
+    with Clocks(c.local) as ck:
+        per, total, launches = time_steps(torch, k, [A, B, C], out, args.steps, args.warmup)
+    c.barrier()
+    total = c.max(total)
+    ms = total / args.steps
+    achieved = 2.0 * rows * S * S / (statistics.mean(per) * 1e-3) / 1e12
+    return {
+        "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C), bf16 operands and output)",
+        "value": round(2.0 * S ** 3 / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "dtype": "bf16 (f32 accumulate)",
+        "config": {"workload": f"relu(matmul(A,B)+C) M=N=K={S} bf16, A row-major, B BLOCKED tag",
+                   "parallelism": f"M-row panels x{c.world}, B broadcast once", "plan": k.describe().strip(),
+                   "l2": "inputs larger than L2; no flush" if S >= 8192 else "inputs smaller than L2"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": c.bf16_sustained, "unit": "TFLOP/s",
+                     "frac": round(achieved / c.bf16_sustained, 4), "frac_of_burst": round(achieved / c.bf16_peak, 4),
+                     "traffic": None, "peak_basis": f"{c.peak_src} sustained bf16 (cuBLAS)"},
+        "gpu_launches": int(c.sum(launches)), "clocks": ck.summary(),
+    }
+
+
 def bench_ew(c: Ctx) -> dict:
     import bafe_b200 as bafe
     torch, args = c.torch, c.args
@@ -551,6 +596,7 @@ def run_ours(args):
     else:
         line = dict(common, **bench_gemm(c))
         if args.only is None:
+            line["gemm_bf16"] = bench_gemm_bf16(c)
             line["ew"] = bench_ew(c)
             line["transpose"] = bench_transpose(c)
     if c.rank == 0:
