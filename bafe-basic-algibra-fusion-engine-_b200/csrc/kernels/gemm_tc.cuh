@@ -321,7 +321,10 @@ struct ElemBf16 {
     static constexpr u32 FMT = 1u;
     static constexpr int MN_ATOM = 64;
     static constexpr u32 MN_LT = 2u, MN_SBO = 1024u, MN_KK = 2048u;
-    static constexpr int KB_CHUNK = 2;               // products are exact: promote every 128 k
+    // Products are exact; promoting every 512 k keeps the accumulator's
+    // truncation far below a bf16 ulp and gives the drain ~4 k cycles of
+    // MMAs to hide behind (a 64-k block is ~540 cycles on a CTA pair).
+    static constexpr int KB_CHUNK = 8;
     __device__ static __forceinline__ void mma(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_f16kind(d, a, b, idesc, acc); }
     __device__ static __forceinline__ void mma_pair(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_f16kind_pair(d, a, b, idesc, acc); }
 };
