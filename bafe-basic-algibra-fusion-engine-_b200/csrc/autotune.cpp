@@ -388,7 +388,7 @@ double step_seconds(const Step& s, const Rates& r, int gemm_dtype) {
                 else if (k == 1) b += (double)s.K * s.N * s.src_esize[k] * (s.b_bstride ? s.batch : 1);
                 else b += (double)(s.src_row[k] ? s.N : s.M * s.N) * s.src_esize[k];
             }
-            if (s.kind == StepKind::GemmTc && s.tc_variant == 3) b += (double)(s.M * s.K + s.K * s.N) * 4.0;
+            if (s.kind == StepKind::GemmTc && s.tc_variant == 3 && !s.tc_convert) b += (double)(s.M * s.K + s.K * s.N) * 4.0;
             const double rate = s.kind == StepKind::GemmTc ? (s.tc_variant == 3 ? r.tc3 : r.tc1)
                                                            : r.exact[gemm_dtype >= 0 && gemm_dtype < 6 ? gemm_dtype : 0];
             return std::max(flops / rate, stream_time(r, b));

@@ -78,6 +78,7 @@ struct Options {
     int device = -1;                        // -1: current device
     bool tc_pair = true;                    // tensor-core GEMM on CTA pairs (cta_group::2)
     int host_panels = -1;                   // host calls: -1 auto, 0/1 off, n: n row panels
+    bool tc_convert = false;                // 3xTF32: make the tf32 residuals inside the kernel
 };
 Options& options();
 
@@ -111,6 +112,7 @@ struct Step {
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
     bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
     int tc_elem = 0;               // GemmTc operands: 0 = f32 (tf32 MMAs), 1 = bf16 (kind::f16)
+    bool tc_convert = false;       // GemmTc 3xTF32: residuals made in shared memory (no aux buffers)
     std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
     // Row streaming of host calls (analyse_row_streaming): the step runs
     // once per row panel of the output (panel) or once per call; buffers

@@ -16,6 +16,9 @@
 //                 round-to-nearest, then releases the TMEM buffer to the
 //                 MMA warp.  After the last chunk it applies the generated
 //                 epilogue (Spec::apply: relu(acc + C), ...) and stores.
+//                 For 3xTF32 with CONVERT the same threads also write the
+//                 tf32 residuals of every stage, one chunk ahead of the
+//                 drain they wait for (see below).
 //
 // Why chunks: the tensor core's fp32 accumulator truncates at every
 // accumulation step, which biases long sums (measured: the 3xTF32 error
@@ -25,9 +28,15 @@
 //
 // kind::tf32 reads the top 19 bits of each fp32 operand (the low 13
 // mantissa bits are ignored), so for 3xTF32 the raw operand is its own
-// "hi" part; a streaming pre-pass (bafe::tf32_residual) writes
-// lo = x - trunc_tf32(x), and each k-step issues
+// "hi" part and only lo = x - trunc_tf32(x) is computed; each k-step issues
 //     A.B += A.B + A.B_lo + A_lo.B        (three MMAs, all on the tensor core)
+// By default a streaming pre-pass (bafe::tf32_residual) writes lo to
+// memory and TMA loads both halves.  With CONVERT the producer loads only
+// the raw operands and the accumulate threads write lo into the stage's
+// second half in shared memory (elementwise, so the swizzle needs no index
+// mapping), releasing each stage to the MMA issuer on LO(s): no pre-pass,
+// no scratch, half the operand bytes from L2 and HBM -- but 64 KB more
+// shared-memory traffic per k-block and CTA, which costs throughput on B200.
 //
 // Operand layouts (BAFE layout tags): A row-major = K-major, A col-major =
 // M-major; B col-major = K-major, B row-major = N-major.  K-major tiles are
@@ -216,6 +225,51 @@ struct Shared {
     u32 tmem_base;
 };
 
+// try_wait with cluster-scope acquire: the phase completes with arrivals
+// released by the peer CTA of a pair (their shared-memory writes included).
+__device__ __forceinline__ bool mbar_try_cluster(u32 bar, u32 parity) {
+    u32 ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint4 lds128(u32 addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+__device__ __forceinline__ void sts128(u32 addr, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+// Writes the tf32 residual of PER x NT 16-byte chunks (chunk i of thread ct
+// at (ct + i * NT) * 16 bytes) from `hi` to the same offsets at `lo`, four
+// chunks per round (four shared-memory loads in flight; the callers hold
+// 128 accumulators, so a wider round spills).
+template <int PER, int NT>
+__device__ __forceinline__ void convert_stage(u32 hi, u32 lo, int ct) {
+    constexpr int R = 4;
+    static_assert(PER % R == 0, "rounds of four chunks");
+#pragma unroll
+    for (int r = 0; r < PER; r += R) {
+        uint4 v[R];
+#pragma unroll
+        for (int j = 0; j < R; ++j) v[j] = lds128(hi + 16u * (u32)(ct + (r + j) * NT));
+#pragma unroll
+        for (int j = 0; j < R; ++j) {
+            v[j].x = __float_as_uint(tf32_lo(__uint_as_float(v[j].x)));
+            v[j].y = __float_as_uint(tf32_lo(__uint_as_float(v[j].y)));
+            v[j].z = __float_as_uint(tf32_lo(__uint_as_float(v[j].z)));
+            v[j].w = __float_as_uint(tf32_lo(__uint_as_float(v[j].w)));
+        }
+#pragma unroll
+        for (int j = 0; j < R; ++j) sts128(lo + 16u * (u32)(ct + (r + j) * NT), v[j]);
+    }
+}
+
 // Bounded wait on an mbarrier phase; returns false (and raises the abort
 // flag / error word) on timeout or when another role has aborted.
 __device__ __forceinline__ bool wait(u32 bar, u32 parity, volatile Shared* sh, const TcArgs& g, u32 code) {
@@ -223,6 +277,21 @@ __device__ __forceinline__ bool wait(u32 bar, u32 parity, volatile Shared* sh, c
     const u64 t0 = now_ns();
     while (true) {
         if (mbar_try(bar, parity)) return true;
+        if (sh->abort) return false;
+        if (now_ns() - t0 > g.timeout_ns) {
+            sh->abort = 1u;
+            atomicCAS(g.err, 0u, code);
+            return false;
+        }
+    }
+}
+
+// The same wait with cluster-scope acquire (mbar_try_cluster).
+__device__ __forceinline__ bool wait_cluster(u32 bar, u32 parity, volatile Shared* sh, const TcArgs& g, u32 code) {
+    if (mbar_try_cluster(bar, parity)) return true;
+    const u64 t0 = now_ns();
+    while (true) {
+        if (mbar_try_cluster(bar, parity)) return true;
         if (sh->abort) return false;
         if (now_ns() - t0 > g.timeout_ns) {
             sh->abort = 1u;
@@ -329,14 +398,18 @@ struct ElemBf16 {
     __device__ static __forceinline__ void mma_pair(u32 d, u64 a, u64 b, u32 idesc, u32 acc) { tc::tc_mma_f16kind_pair(d, a, b, idesc, acc); }
 };
 
-template <class Spec, int VARIANT, class E = ElemTf32>
+template <class Spec, int VARIANT, class E = ElemTf32, bool CONVERT = false>
 __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     using namespace tc;
     typedef TcCfg<VARIANT> Cfg;
     constexpr int BN = Cfg::BN, STAGES = Cfg::STAGES;
     constexpr bool SPLIT = VARIANT == 3;
+    constexpr bool CONV = SPLIT && CONVERT;          // residuals made in shared memory
     static_assert(!SPLIT || E::BYTES == 4, "the 3-product split is for fp32 operands");
     constexpr int KB_PER_CHUNK = E::KB_CHUNK ? E::KB_CHUNK : Cfg::KB_PER_CHUNK;
+    // the conversion look-ahead (one chunk) must fit in the stage ring, or
+    // the converters wait on loads that wait on MMAs that wait on them
+    static_assert(!CONV || KB_PER_CHUNK <= STAGES, "conversion look-ahead exceeds the stages");
     constexpr int BKE = E::BKE;                      // elements per k-block
     constexpr u32 MN_BOX = BKE * 128u;              // one MN-major box: a k-block of 128-byte rows
     constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB (128 rows x 128 B)
@@ -357,7 +430,8 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
     auto TFULL = [&](int b) { return bars + 8u * (2 * STAGES + b); };
     auto TEMPTY = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
     const u32 DRAIN = bars + 8u * (2 * STAGES + 4);
-    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5));
+    auto LO = [&](int s) { return bars + 8u * (2 * STAGES + 5 + s); };   // residuals of stage s ready
+    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (3 * STAGES + 5));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -372,6 +446,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             mbar_init(TEMPTY(b), ACC_THREADS);
         }
         mbar_init(DRAIN, 1);
+        for (int s = 0; s < STAGES; ++s) mbar_init(LO(s), ACC_THREADS);
         sh->abort = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -409,11 +484,11 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
                     const u32 b_dst = a_dst + A_BYTES;
-                    mbar_expect_tx(FULL(s), STAGE_BYTES);
+                    mbar_expect_tx(FULL(s), CONV ? A_BYTES + B_BYTES : STAGE_BYTES);
                     armed[s] = phase;
                     const int k0 = kb * BKE;
 #pragma unroll
-                    for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
+                    for (int part = 0; part < (SPLIT && !CONV ? 2 : 1); ++part) {
                         const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
                         const TmaDesc* mbp = part ? &g.tmap_b_lo : &g.tmap_b;
                         const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
@@ -461,7 +536,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                     const u32 d = tmem + (u32)(buf * BN);
                     const int kb_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
                     for (int kb = c * KB_PER_CHUNK; kb < kb_end; ++kb) {
-                        if (!wait(FULL(s), phase, sh, g, 3u)) { ok = false; break; }
+                        if (!wait(CONV ? LO(s) : FULL(s), phase, sh, g, 3u)) { ok = false; break; }
                         tc_fence_after();
                         const u32 a_hi = base + s * STAGE_BYTES;
                         const u32 b_hi = a_hi + A_BYTES;
@@ -505,15 +580,46 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
         typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
         u32 chunk = 0;
         bool ok = true;
+        // 3xTF32 with converted residuals: these threads also write the tf32
+        // residuals of every stage (each its 1/256 share), one
+        // TMEM chunk ahead of the drain they wait for, and release it on the
+        // MMA issuer through LO(s).
+        // conv counts converted k-blocks from the current tile's first; the
+        // look-ahead may run into the next tiles but never past this CTA's
+        // last k-block, nor more than KB_PER_CHUNK <= STAGES k-blocks beyond
+        // the chunk being drained (so producer, converters and MMA issuer
+        // never wait on one another in a circle).
+        const int at = threadIdx.x - 64;
+        int conv = 0, cs = 0;
+        u32 cph = 0;
+        auto convert_until = [&](int target) -> bool {
+            if constexpr (CONV) {
+                while (conv < target) {
+                    if (!wait(FULL(cs), cph, sh, g, 5u)) return false;
+                    const u32 hi = base + cs * STAGE_BYTES;
+                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS>(hi, hi + A_BYTES + B_BYTES, at);
+                    fence_async_smem();                    // visible to the tensor core
+                        mbar_arrive(LO(cs));
+                    if (++cs == STAGES) { cs = 0; cph ^= 1u; }
+                    ++conv;
+                }
+            }
+            return true;
+        };
         for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+            // k-blocks this CTA still has after the current tile, capped
+            const long long after = (long long)(g.num_tiles - 1 - t) / (int)gridDim.x * k_blocks;
+            const int limit = k_blocks + (after < KB_PER_CHUNK ? (int)after : KB_PER_CHUNK);
             float acc[128];
 #pragma unroll
             for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
             for (int c = 0; c < n_chunks; ++c, ++chunk) {
                 const int buf = (int)(chunk & 1u);
                 const u32 use = (chunk >> 1) & 1u;
+                const int c_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
                 // warp-uniform: tcgen05.ld below needs all 32 lanes converged
-                const bool ready = wait(TFULL(buf), use, sh, g, 4u);
+                const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
                 if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
@@ -527,6 +633,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                 mbar_arrive(TEMPTY(buf));
             }
             if (!ok) break;
+            if (CONV) conv -= k_blocks;                // counted from the next tile's first k-block
             int mb, nb, bi;
             tile_coords(g, t, mb, nb, bi);
             const i64 i = (i64)mb * BM + row_in_tile;
@@ -566,14 +673,18 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
 // committed to the barriers of both CTAs; the accumulate warps of both
 // CTAs release a TMEM chunk buffer by arriving on the leader's barrier.
 // Roles, chunked register accumulation, bounded waits as in gemm_tc.
-template <class Spec, int VARIANT, class E = ElemTf32>
+template <class Spec, int VARIANT, class E = ElemTf32, bool CONVERT = false>
 __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     using namespace tc;
     typedef TcPairCfg<VARIANT> Cfg;
     constexpr int BN = 256, STAGES = Cfg::STAGES;
     constexpr bool SPLIT = VARIANT == 3;
+    constexpr bool CONV = SPLIT && CONVERT;          // residuals made in shared memory
     static_assert(!SPLIT || E::BYTES == 4, "the 3-product split is for fp32 operands");
     constexpr int KB_PER_CHUNK = E::KB_CHUNK ? E::KB_CHUNK : Cfg::KB_PER_CHUNK;
+    // the conversion look-ahead (one chunk) must fit in the stage ring, or
+    // the converters wait on loads that wait on MMAs that wait on them
+    static_assert(!CONV || KB_PER_CHUNK <= STAGES, "conversion look-ahead exceeds the stages");
     constexpr int BKE = E::BKE;
     constexpr u32 MN_BOX = BKE * 128u;
     constexpr u32 A_BYTES = BM * BK * 4;            // 16 KB: this CTA's 128 rows
@@ -592,7 +703,8 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     auto TFULL = [&](int b) { return bars + 8u * (2 * STAGES + b); };
     auto TEMPTY = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
     const u32 DRAIN = bars + 8u * (2 * STAGES + 4);
-    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 5));
+    auto LO = [&](int s) { return bars + 8u * (2 * STAGES + 5 + s); };   // residuals of stage s ready
+    volatile Shared* sh = reinterpret_cast<volatile Shared*>(smem + STAGES * STAGE_BYTES + 8 * (3 * STAGES + 5));
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -610,6 +722,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             mbar_init(TEMPTY(b), 2 * ACC_THREADS);
         }
         mbar_init(DRAIN, 1);
+        for (int s = 0; s < STAGES; ++s) mbar_init(LO(s), 2 * ACC_THREADS);   // both CTAs' converting threads
         sh->abort = 0u;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -639,19 +752,31 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
                 const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
-                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d_pair(dst, m, bar, x, y, za); };
-                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d_pair(dst, m, bar, x, y, zb); };
+                // With converted residuals each CTA's copies complete on its
+                // own FULL barrier (its converting threads wait there);
+                // otherwise on the leader's, which the MMA issuer waits on.
+                auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (CONV) tma_load_3d(dst, m, bar, x, y, za);
+                    else tma_load_3d_pair(dst, m, bar, x, y, za);
+                };
+                auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) {
+                    if (CONV) tma_load_3d(dst, m, bar, x, y, zb);
+                    else tma_load_3d_pair(dst, m, bar, x, y, zb);
+                };
                 for (int kb = 0; kb < k_blocks; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
                     const u32 b_dst = a_dst + A_BYTES;
-                    if (cta == 0) {
-                        mbar_expect_tx(FULL(s), 2 * STAGE_BYTES);   // both CTAs' bytes
+                    if (CONV) {
+                        mbar_expect_tx(FULL(s), A_BYTES + B_BYTES);   // this CTA's raw operands
+                        armed[s] = phase;
+                    } else if (cta == 0) {
+                        mbar_expect_tx(FULL(s), 2 * STAGE_BYTES);     // both CTAs' bytes
                         armed[s] = phase;
                     }
                     const int k0 = kb * BKE;
 #pragma unroll
-                    for (int part = 0; part < (SPLIT ? 2 : 1); ++part) {
+                    for (int part = 0; part < (SPLIT && !CONV ? 2 : 1); ++part) {
                         const TmaDesc* ma = part ? &g.tmap_a_lo : &g.tmap_a;
                         const TmaDesc* mbp = part ? &g.tmap_b_lo : &g.tmap_b;
                         const u32 ad = a_dst + part * (A_BYTES + B_BYTES);
@@ -672,11 +797,11 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     if (++s == STAGES) { s = 0; phase ^= 1u; }
                 }
             }
-            // Drain (bounded): the leader's FULL phases count both CTAs'
-            // copies; the peer waits until the MMAs released its last stages.
+            // Drain (bounded): wait for the copies on this CTA's armed FULL
+            // phases (the leader's count both CTAs' copies unless converting).
             for (int i = 0; i < STAGES; ++i) {
                 const u64 t0 = now_ns();
-                if (cta == 0) {
+                if (CONV || cta == 0) {
                     if (armed[i] == 0xFFFFFFFFu) continue;
                     while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < g.timeout_ns) {}
                 }
@@ -702,7 +827,8 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     const u32 d = tmem + (u32)(buf * BN);
                     const int kb_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
                     for (int kb = c * KB_PER_CHUNK; kb < kb_end; ++kb) {
-                        if (!wait(FULL(s), phase, sh, g, 3u)) { ok = false; break; }
+                        const bool ready = CONV ? wait_cluster(LO(s), phase, sh, g, 3u) : wait(FULL(s), phase, sh, g, 3u);
+                        if (!ready) { ok = false; break; }
                         tc_fence_after();
                         const u32 a_hi = base + s * STAGE_BYTES;
                         const u32 b_hi = a_hi + A_BYTES;
@@ -743,14 +869,46 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
         typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
         u32 chunk = 0;
         bool ok = true;
+        // 3xTF32 with converted residuals: these threads also write the tf32
+        // residuals of every stage of their CTA (each its 1/256 share), one
+        // TMEM chunk ahead of the drain they wait for, and release it on the
+        // leader's LO(s) (the MMA reads both CTAs' stages).
+        // conv counts converted k-blocks from the current tile's first; the
+        // look-ahead may run into the next tiles but never past this CTA's
+        // last k-block, nor more than KB_PER_CHUNK <= STAGES k-blocks beyond
+        // the chunk being drained (so producer, converters and MMA issuer
+        // never wait on one another in a circle).
+        const int at = threadIdx.x - 64;
+        int conv = 0, cs = 0;
+        u32 cph = 0;
+        auto convert_until = [&](int target) -> bool {
+            if constexpr (CONV) {
+                while (conv < target) {
+                    if (!wait(FULL(cs), cph, sh, g, 5u)) return false;
+                    const u32 hi = base + cs * STAGE_BYTES;
+                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS>(hi, hi + A_BYTES + B_BYTES, at);
+                    fence_async_smem();                    // visible to the tensor core
+                        if (cta == 0) mbar_arrive(LO(cs));
+                        else mbar_arrive_cluster(LO(cs), 0u);
+                    if (++cs == STAGES) { cs = 0; cph ^= 1u; }
+                    ++conv;
+                }
+            }
+            return true;
+        };
         for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+            // k-blocks this CTA still has after the current tile, capped
+            const long long after = (long long)(g.num_tiles - 1 - t) / num_pairs * k_blocks;
+            const int limit = k_blocks + (after < KB_PER_CHUNK ? (int)after : KB_PER_CHUNK);
             float acc[128];
 #pragma unroll
             for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
             for (int c = 0; c < n_chunks; ++c, ++chunk) {
                 const int buf = (int)(chunk & 1u);
                 const u32 use = (chunk >> 1) & 1u;
-                const bool ready = wait(TFULL(buf), use, sh, g, 4u);
+                const int c_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
+                const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
                 if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
@@ -770,6 +928,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 else mbar_arrive_cluster(TEMPTY(buf), 0u);
             }
             if (!ok) break;
+            if (CONV) conv -= k_blocks;                // counted from the next tile's first k-block
             int mb, nb, bi;
             tile_coords(g, t, mb, nb, bi);
             const i64 i = (i64)mb * 2 * BM + (i64)cta * BM + row_in_tile;

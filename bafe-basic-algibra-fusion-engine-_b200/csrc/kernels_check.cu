@@ -35,6 +35,12 @@ extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) che
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_tc1_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpec, 1>(g);
 }
+extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) check_gemm_tc3_pair_conv(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_pair<CheckSpec, 3, bafe::ElemTf32, true>(g);
+}
+extern "C" __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1) check_gemm_tc3_conv(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc<CheckSpec, 3, bafe::ElemTf32, true>(g);
+}
 // bf16 operands (kind::f16), bf16 output through the emitter's conversion.
 struct CheckSpecBf16 {
     typedef float TA; typedef float TB; typedef float T; typedef float P; typedef float S;

@@ -547,6 +547,10 @@ struct Lowerer {
                 s.kind = StepKind::GemmTc;
                 s.tc_variant = (bf16_ops || prec == "tf32") ? 1 : 3;
                 s.tc_elem = bf16_ops ? 1 : 0;
+                // 3xTF32 residuals: a pre-pass into plan scratch (default), or
+                // made in shared memory by the kernel (tc_convert: no scratch,
+                // half the operand traffic, more shared-memory traffic)
+                s.tc_convert = s.tc_variant == 3 && opt.tc_convert;
                 s.tc_pair = opt.tc_pair;
             }
         }
@@ -611,7 +615,7 @@ struct Lowerer {
             s.src_esize.push_back(dtype_size(buf_dtype[l.node]));
             s.src_row.push_back(l.access == ROW);
         }
-        if (s.kind == StepKind::GemmTc && s.tc_variant == 3) {
+        if (s.kind == StepKind::GemmTc && s.tc_variant == 3 && !s.tc_convert) {
             // 3xTF32 residual operands lo = x - trunc_tf32(x), written once
             // per call by a streaming pre-pass into plan scratch.
             s.aux.push_back(emit_residual(s.srcs[0], M * K * a_items, "A"));
@@ -627,7 +631,8 @@ struct Lowerer {
             const char* elem = s.tc_elem == 1 ? "bafe::ElemBf16" : "bafe::ElemTf32";
             src << "extern \"C\" __global__ void __launch_bounds__(bafe::" << cfg << "<" << s.tc_variant
                 << ">::THREADS, 1) " << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::" << fn << "<"
-                << S_ << ", " << s.tc_variant << ", " << elem << ">(g); }\n";
+                << S_ << ", " << s.tc_variant << ", " << elem << ", " << (s.tc_convert ? "true" : "false")
+                << ">(g); }\n";
         }
         char geo[256];
         snprintf(geo, sizeof(geo), " batch=%lld m=%lld n=%lld k=%lld a=%s b=%s", (long long)batch, (long long)M,

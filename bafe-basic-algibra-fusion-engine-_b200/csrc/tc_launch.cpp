@@ -58,7 +58,8 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,
                std::string& err) {
     const bool split = s.tc_variant == 3;
-    if (split && (!a_lo || !b_lo)) {
+    const bool lo_maps = split && !s.tc_convert;     // residuals read from memory
+    if (lo_maps && (!a_lo || !b_lo)) {
         err = "tensor-core GEMM: 3xTF32 needs the residual operands";
         return 12;
     }
@@ -113,7 +114,7 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     };
     if (int rc = map_a(&h.tmap_a, a)) return rc;
     if (int rc = map_b(&h.tmap_b, b)) return rc;
-    if (split) {
+    if (lo_maps) {
         if (int rc = map_a(&h.tmap_a_lo, a_lo)) return rc;
         if (int rc = map_b(&h.tmap_b_lo, b_lo)) return rc;
     }

@@ -259,6 +259,10 @@ void bafe_cuda_clear_error(void);
  *   "tc_pair":        "1" (default): tensor-core GEMMs run on CTA pairs
  *                     (256x256 tiles over two SMs); "0": one CTA per tile
  *                     (read when a plan is built)
+ *   "tc_convert":     "0" (default): 3xTF32 residuals come from a pre-pass
+ *                     into plan scratch; "1": the GEMM kernel makes them in
+ *                     shared memory (no scratch, half the operand traffic,
+ *                     lower throughput on B200) (read when a plan is built)
  *   "host_panels":    "auto" (default) | "0" | n: host-pointer calls of a
  *                     row-separable plan copy, compute and copy back in n
  *                     row panels on three streams, overlapping the copies
@@ -267,7 +271,7 @@ void bafe_cuda_clear_error(void);
  *                     each call)
  *   "device":         CUDA device ordinal used by host-pointer calls
  *                     (default: the current device)
- * Environment variables BAFE_GEMM_PRECISION, BAFE_TC_PAIR,
+ * Environment variables BAFE_GEMM_PRECISION, BAFE_TC_PAIR, BAFE_TC_CONVERT,
  * BAFE_HOST_PANELS and BAFE_DEVICE set the initial values.  Returns 0, or
  * -1 for an unknown key or value. */
 int bafe_cuda_set_option(const char *key, const char *value);

@@ -208,3 +208,26 @@ def test_batched_gemm_on_tensor_cores(cuda, batch, M, N, K, a_col, b_col, b_shar
     tol = (1e-4 if prec == "3xtf32" else TF32_TOL) * math.sqrt(K / 64)
     print(f"batched {prec} pair={pair} {batch}x{M}x{N}x{K}: max err {err:.3e} (bound {tol:.3e})")
     assert err <= tol
+
+
+# ------------------------------------------------- in-kernel residuals --
+# tc_convert=1: the kernel makes the tf32 residuals in shared memory (no
+# pre-pass, no scratch); same products, same bound.
+
+@pytest.mark.parametrize("shape,a_col,b_col", [((512, 512, 512), 0, 0), ((300, 260, 1000), 1, 1),
+                                               ((1024, 768, 4096), 0, 1), ((4096, 4096, 4096), 0, 0)])
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_3xtf32_in_kernel_residuals(cuda, shape, a_col, b_col, pair):
+    M, N, K = shape
+    bafe.set_option("tc_convert", "1")
+    bafe.set_option("tc_pair", pair)
+    try:
+        k, out, err = _run(cuda, M, N, K, a_col, b_col, "relu_add_c", "3xtf32", seed=11)
+    finally:
+        bafe.set_option("tc_convert", "0")
+        bafe.set_option("tc_pair", "1")
+    steps = k.describe().strip().splitlines()
+    assert len(steps) == 1 and steps[0].startswith("gemm.tc.3xtf32"), steps
+    bound = 1e-4 * math.sqrt(K / 64)
+    print(f"3xtf32 in-kernel residuals {shape} pair={pair}: max err {err:.3e} (bound {bound:.1e})")
+    assert err <= bound

@@ -139,3 +139,20 @@ def test_every_golden_graph_lowers_and_compiles(name):
                 return meta["nodes"][i]["dtype"]
         k = bafe.compile_graph(B)
         assert k.describe()
+
+
+def test_tc_convert_option_drops_the_residual_pre_pass():
+    g = GraphBuilder()
+    a = g.add_input("A", (512, 512), 0, 0)
+    b = g.add_input("B", (512, 512), 0, 0)
+    g.set_output(g.add("matmul", [a, b]))
+    bafe.set_option("gemm_precision", "3xtf32")
+    default = bafe.compile_graph(g).describe().strip().splitlines()
+    assert [l.split()[0] for l in default][:2] == ["ew", "ew"] and default[2].startswith("gemm.tc.3xtf32")
+    assert bafe.get_option("tc_convert") == "0"
+    bafe.set_option("tc_convert", "1")
+    try:
+        conv = bafe.compile_graph(g).describe().strip().splitlines()
+    finally:
+        bafe.set_option("tc_convert", "0")
+    assert len(conv) == 1 and conv[0].startswith("gemm.tc.3xtf32")
