@@ -43,9 +43,15 @@ def element_ranges(n: int, world: int, align: int = 4) -> List[Tuple[int, int]]:
 
 
 def broadcast_resident(tensor, dist, src: int = 0):
-    """Broadcast `tensor` from `src` in place (B of a sharded GEMM)."""
+    """Broadcast `tensor` from `src` in place (B of a sharded GEMM).  Raw
+    16-bit half buffers (int16 / uint16 holding bf16 or f16 bits) travel as
+    bytes: NCCL has no 16-bit integer type."""
     if dist is not None and dist.is_initialized() and dist.get_world_size() > 1:
-        dist.broadcast(tensor, src=src)
+        import torch
+        t = tensor
+        if t.dtype in (torch.int16, getattr(torch, "uint16", torch.int16)) and t.is_contiguous():
+            t = t.view(torch.uint8)
+        dist.broadcast(t, src=src)
     return tensor
 
 

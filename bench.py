@@ -311,8 +311,10 @@ class Ctx:
         if self.world > 1:
             import datetime
             import torch.distributed as dist_mod
-            # rank 0's stdout carries exactly one JSON line: keep NCCL's
-            # version banner (NCCL_DEBUG=VERSION) off it
+            # rank 0's stdout carries exactly one JSON line: NCCL prints its
+            # version banner (and warnings) to stdout at NCCL_DEBUG=VERSION or
+            # WARN, so its log goes to stderr unless a log file was chosen
+            os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
             if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
                 os.environ["NCCL_DEBUG"] = "WARN"
             dist_mod.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.dev)

@@ -127,3 +127,44 @@ def test_failed_rank_surfaces_as_error_on_the_other_rank():
     errs = [m for kind, m in res if kind == "error"]
     assert any(m.startswith("rank 1") for m in errs), res
     assert any(m.startswith("rank 0") for m in errs), res
+
+
+def _bcast_worker(rank, world, port, q):
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from bafe_b200.parallel import broadcast_resident
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        want = torch.arange(64, dtype=torch.int16).reshape(8, 8) * 311
+        t = want.clone() if rank == 0 else torch.zeros(8, 8, dtype=torch.int16)
+        broadcast_resident(t, dist)
+        q.put(("ok", bool(torch.equal(t, want))))
+    except Exception as e:
+        q.put(("error", f"rank {rank}: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_broadcast_of_raw_half_buffers():
+    """bf16 / f16 operands travel as raw 16-bit words; the broadcast moves
+    their bytes (NCCL has no 16-bit integer type)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bcast_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    assert out == [("ok", True), ("ok", True)], out
