@@ -148,6 +148,7 @@ def _load() -> ctypes.CDLL:
         "bafe_cuda_gemm_3xtf32_static_scratch": ([c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
                                                   c_int, c_void_p], c_int),
         "bafe_cuda_calibrate": ([c_int, c_int], c_int),
+        "bafe_cuda_selftest_wait_timeout": ([c_int, POINTER(ctypes.c_uint), POINTER(c_double)], c_int),
         "bafe_cuda_hardware_model": ([c_int, POINTER(BafeHardwareModel)], c_int),
         "bafe_cuda_plan_predict_ms": ([c_int], c_double),
         "bafe_cuda_plan_last_device_ms": ([c_int], c_double),
@@ -192,7 +193,7 @@ EXPORTED_SYMBOLS = (
     "bafe_cuda_profiling_dump_jsonl", "bafe_cuda_profiling_refit", "bafe_cuda_profiling_get_model",
     "bafe_cuda_profiling_predict_log", "bafe_cuda_profiling_predict_ms", "bafe_cuda_autotune_config_default",
     "bafe_cuda_autotune_configure", "bafe_cuda_autotune_get_config", "bafe_cuda_autotune_get_stats",
-    "bafe_cuda_autotune_dispatch",
+    "bafe_cuda_autotune_dispatch", "bafe_cuda_selftest_wait_timeout",
 )
 
 

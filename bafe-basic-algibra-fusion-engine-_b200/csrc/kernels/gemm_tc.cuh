@@ -286,6 +286,13 @@ __device__ __forceinline__ bool wait(u32 bar, u32 parity, volatile Shared* sh, c
     }
 }
 
+// Limit of the final drains (copies in flight, MMAs before TMEM is freed):
+// never below 200 ms, so that a short wait deadline cannot cut them off --
+// asynchronous work that is already issued finishes in microseconds.
+__device__ __forceinline__ u64 drain_ns(const TcArgs& g) {
+    return g.timeout_ns > 200000000ull ? g.timeout_ns : 200000000ull;
+}
+
 // The same wait with cluster-scope acquire (mbar_try_cluster).
 __device__ __forceinline__ bool wait_cluster(u32 bar, u32 parity, volatile Shared* sh, const TcArgs& g, u32 code) {
     if (mbar_try_cluster(bar, parity)) return true;
@@ -513,7 +520,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             for (int i = 0; i < STAGES; ++i) {
                 if (armed[i] == 0xFFFFFFFFu) continue;
                 const u64 t0 = now_ns();
-                while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < g.timeout_ns) {}
+                while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < drain_ns(g)) {}
             }
         }
     } else if (warp == 1) {
@@ -569,7 +576,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             // Drain outstanding MMAs before TMEM is released (bounded).
             tc_commit(DRAIN);
             const u64 t0 = now_ns();
-            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < g.timeout_ns) {}
+            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < drain_ns(g)) {}
         }
     } else {
         // ------------------------------------ accumulate + epilogue --
@@ -803,7 +810,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 const u64 t0 = now_ns();
                 if (CONV || cta == 0) {
                     if (armed[i] == 0xFFFFFFFFu) continue;
-                    while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < g.timeout_ns) {}
+                    while (!mbar_try(FULL(i), armed[i]) && now_ns() - t0 < drain_ns(g)) {}
                 }
             }
         }
@@ -858,7 +865,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             }
             tc_commit_pair(DRAIN);
             const u64 t0 = now_ns();
-            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < g.timeout_ns) {}
+            while (!mbar_try(DRAIN, 0u) && now_ns() - t0 < drain_ns(g)) {}
         }
     } else {
         // ------------------------- accumulate + epilogue (both CTAs) --

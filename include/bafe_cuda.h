@@ -352,6 +352,16 @@ bafe_autotune_stats bafe_cuda_autotune_get_stats(void);                     /* p
 double bafe_cuda_autotune_dispatch(bafe_kernel_fn fn, void **args, int n_args, const bafe_graph *graph,
                                    const char *graph_hash, double predicted_cost);
 
+/* Failure-detection self-test: launches, on the current device, a kernel
+ * whose bounded mbarrier wait -- the same wait every role of the
+ * tensor-core GEMMs uses -- runs out after timeout_us (1 .. 10^7), because
+ * nothing arrives at the barrier; no asynchronous copies or MMAs are issued.
+ * Returns 0 when the kernel reported its timeout code through the device
+ * error word (*code_out = the code, *elapsed_ms = host time of the call),
+ * else a nonzero code.  The context stays usable.  New: no counterpart in
+ * the reference (its kernels run on the host). */
+int bafe_cuda_selftest_wait_timeout(int timeout_us, unsigned *code_out, double *elapsed_ms);
+
 /* out = A . B (fp32, 3xTF32 tensor cores, M x N row-major out) without any
  * device allocation.  No counterpart in the reference.
  *
