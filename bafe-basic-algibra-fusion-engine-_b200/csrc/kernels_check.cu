@@ -18,6 +18,16 @@ struct CheckSpec {
         const float x0 = reinterpret_cast<const float*>(g.ep[0])[flat];
         return bafe::relu(bafe::add(acc, x0));
     }
+    template <class G> static __device__ __forceinline__ void apply4(const T* acc4, const G& g, i64 b, i64 i, i64 j, bafe::Vec4<Out>& o4) {
+        const i64 flat = b * g.o_bstride + i * g.N + j;
+        const bafe::Vec4<float> v0 = bafe::ld4(reinterpret_cast<const float*>(g.ep[0]) + flat);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o4.v[e] = bafe::relu(bafe::add(acc4[e], v0.v[e]));
+    }
+    template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0, int n) {
+        const char* p = reinterpret_cast<const char*>(g.ep[0]) + (b * g.o_bstride + i * g.N + j0) * 4;
+        for (int o = 0; o < n * 4; o += 128) asm volatile("prefetch.global.L2 [%0];" :: "l"(p + o));
+    }
 };
 
 extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
@@ -48,6 +58,11 @@ struct CheckSpecBf16 {
     template <class G> static __device__ __forceinline__ Out apply(T acc, const G& g, i64 b, i64 i, i64 j) {
         return bafe::f32_to_bf16(bafe::relu(acc));
     }
+    template <class G> static __device__ __forceinline__ void apply4(const T* acc4, const G&, i64, i64, i64, bafe::Vec4<Out>& o4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o4.v[e] = bafe::f32_to_bf16(bafe::relu(acc4[e]));
+    }
+    template <class G> static __device__ __forceinline__ void prefetch(const G&, i64, i64, i64, int) {}
 };
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_bf16_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpecBf16, 1, bafe::ElemBf16>(g);

@@ -570,43 +570,79 @@ struct Lowerer {
             << load_convert(a.dtype, std::string("reinterpret_cast<const ") + dtype_ctype(a.dtype) + "*>(p)[i]") << "; }\n"
             << "  static __device__ __forceinline__ TB loadB(const void* p, i64 i) { return "
             << load_convert(b.dtype, std::string("reinterpret_cast<const ") + dtype_ctype(b.dtype) + "*>(p)[i]") << "; }\n";
-        // apply(acc, ...) -> stored output element
-        src << "  template <class G> static __device__ __forceinline__ Out apply(T acc_in, const G& g, i64 b, i64 i, i64 j) {\n"
-            << "    const i64 flat = b * g.o_bstride + i * g.N + j;\n    (void)flat;\n";
-        // built-in epilogue first
-        std::string accexpr = "acc_in";
-        int leaf_base = 0;
-        if (g.op == Op::FusedMatmulRelu) {
-            src << "    const T acc0 = bafe::relu(acc_in);\n";
-            accexpr = "acc0";
-        } else if (g.op == Op::FusedMatmulBias || g.op == Op::FusedMatmulBiasRelu) {
-            const int tb = ct(g.ch[2]);
-            const int cm = common_type(T, tb);
-            src << "    const " << ctype(tb) << " bias = "
-                << load_convert(buf_dtype[g.ch[2]], std::string("reinterpret_cast<const ") + dtype_ctype(buf_dtype[g.ch[2]]) + "*>(g.ep[0])[j]")
-                << ";\n";
-            std::string sum = cast(T, cm, "bafe::add(" + cast(cm, T, "acc_in") + ", " + cast(cm, tb, "bias") + ")");
-            if (g.op == Op::FusedMatmulBiasRelu) sum = "bafe::relu(" + sum + ")";
-            src << "    const T acc0 = " << sum << ";\n";
-            accexpr = "acc0";
-            leaf_base = 1;
-        }
-        src << "    const T acc = " << accexpr << ";\n    (void)acc;\n";
-        std::string rv = "acc";
-        int rv_dtype = T;
-        if (R) {
-            for (size_t k = 0; k < R->leaves.size(); ++k) {
-                int node = R->leaves[k].node;
-                std::string p = std::string("reinterpret_cast<const ") + dtype_ctype(buf_dtype[node]) + "*>(g.ep[" +
-                                std::to_string(leaf_base + k) + "])";
-                std::string idx = R->leaves[k].access == ROW ? "j" : "flat";
-                src << "    const " << ctype(ct(node)) << " x" << k << " = "
-                    << load_convert(buf_dtype[node], p + "[" + idx + "]") << ";\n";
+        // apply(acc, g, b, i, j) -> the stored output element (i, j); and
+        // apply4(acc4, g, b, i, j, o4): the same for columns j .. j+3 (j a
+        // multiple of 4), each operand read as one 4-element vector (the
+        // tensor-core kernels use it when every operand is aligned for that).
+        // Both are the same statements; only the operand reads differ.
+        auto emit_apply = [&](bool vec) {
+            const std::string in = vec ? "      " : "    ";
+            if (vec)
+                src << "  template <class G> static __device__ __forceinline__ void apply4(const T* acc4, const G& g, i64 b, "
+                       "i64 i, i64 j, bafe::Vec4<Out>& o4) {\n";
+            else
+                src << "  template <class G> static __device__ __forceinline__ Out apply(T acc_in, const G& g, i64 b, i64 i, i64 j) {\n";
+            src << "    const i64 flat = b * g.o_bstride + i * g.N + j;\n    (void)flat;\n";
+            // operand k of the epilogue (ep[k]) read at idx: the expression of
+            // one element (inside apply4's loop: element e of its vector)
+            auto operand = [&](int k, int node, const std::string& idx) {
+                const std::string st = dtype_ctype(buf_dtype[node]);
+                const std::string p = "reinterpret_cast<const " + st + "*>(g.ep[" + std::to_string(k) + "])";
+                if (!vec) return p + "[" + idx + "]";
+                src << "    const bafe::Vec4<" << st << "> v" << k << " = bafe::ld4(" << p << " + " << idx << ");\n";
+                return "v" + std::to_string(k) + ".v[e]";
+            };
+            const bool bias = g.op == Op::FusedMatmulBias || g.op == Op::FusedMatmulBiasRelu;
+            const int leaf_base = bias ? 1 : 0;
+            std::string bias_rd;
+            if (bias) bias_rd = operand(0, g.ch[2], "j");
+            std::vector<std::string> leaf_rd;
+            if (R)
+                for (size_t k = 0; k < R->leaves.size(); ++k)
+                    leaf_rd.push_back(operand(leaf_base + (int)k, R->leaves[k].node, R->leaves[k].access == ROW ? "j" : "flat"));
+            if (vec) src << "#pragma unroll\n    for (int e = 0; e < 4; ++e) {\n" << in << "const T acc_in = acc4[e];\n";
+            // built-in epilogue first
+            std::string accexpr = "acc_in";
+            if (g.op == Op::FusedMatmulRelu) {
+                src << in << "const T acc0 = bafe::relu(acc_in);\n";
+                accexpr = "acc0";
+            } else if (bias) {
+                const int tb = ct(g.ch[2]);
+                const int cm = common_type(T, tb);
+                src << in << "const " << ctype(tb) << " bias = " << load_convert(buf_dtype[g.ch[2]], bias_rd) << ";\n";
+                std::string sum = cast(T, cm, "bafe::add(" + cast(cm, T, "acc_in") + ", " + cast(cm, tb, "bias") + ")");
+                if (g.op == Op::FusedMatmulBiasRelu) sum = "bafe::relu(" + sum + ")";
+                src << in << "const T acc0 = " << sum << ";\n";
+                accexpr = "acc0";
             }
-            rv = emit_region_body(*R, src, "    ");
-            rv_dtype = ct(R->root);
+            src << in << "const T acc = " << accexpr << ";\n" << in << "(void)acc;\n";
+            std::string rv = "acc";
+            int rv_dtype = T;
+            if (R) {
+                for (size_t k = 0; k < R->leaves.size(); ++k)
+                    src << in << "const " << ctype(ct(R->leaves[k].node)) << " x" << k << " = "
+                        << load_convert(buf_dtype[R->leaves[k].node], leaf_rd[k]) << ";\n";
+                rv = emit_region_body(*R, src, in);
+                rv_dtype = ct(R->root);
+            }
+            if (vec) src << in << "o4.v[e] = " << store_convert(out_store, rv_dtype, rv) << ";\n    }\n  }\n";
+            else src << "    return " << store_convert(out_store, rv_dtype, rv) << ";\n  }\n";
+        };
+        emit_apply(false);
+        emit_apply(true);
+        // prefetch(g, b, i, j0, n): pull the epilogue operands of output
+        // row i, columns [j0, j0 + n), into L2 ahead of apply() (the
+        // tensor-core kernels call it while their last chunk runs).
+        src << "  template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0, int n) {\n"
+            << "    (void)g; (void)b; (void)i; (void)j0; (void)n;\n";
+        for (size_t k = 0; k < leaves.size(); ++k) {
+            const int node = leaves[k].node;
+            const int es = dtype_size(buf_dtype[node]);
+            const std::string first = leaves[k].access == ROW ? "j0" : "(b * g.o_bstride + i * g.N + j0)";
+            src << "    { const char* p = reinterpret_cast<const char*>(g.ep[" << k << "]) + " << first << " * " << es
+                << "; for (int o = 0; o < n * " << es << "; o += 128) asm volatile(\"prefetch.global.L2 [%0];\" :: \"l\"(p + o)); }\n";
         }
-        src << "    return " << store_convert(out_store, rv_dtype, rv) << ";\n  }\n};\n";
+        src << "  }\n};\n";
         for (auto& l : leaves) s.srcs.push_back(buf[l.node]);
         s.n_epi = (int)leaves.size();
         s.src_esize = {dtype_size(buf_dtype[g.ch[0]]), dtype_size(buf_dtype[g.ch[1]])};

@@ -271,6 +271,16 @@ struct DeviceState {
     cudaStream_t d2h = nullptr;         // host calls: output copies (row streaming)
     std::vector<cudaEvent_t> events;    // row streaming: per-panel hand-offs
     std::vector<cudaEvent_t> tev;       // host calls: timing events around the kernels
+    // Prepared tensor-core launches (tensor maps + argument block) per step,
+    // reused while the buffers and panel rows are the same: encoding four
+    // tensor maps per call is host work that small GEMMs would wait for.
+    struct TcCached {
+        bool valid = false;
+        const void* key[14] = {};   // a, b, a_lo, b_lo, out, error word, 8 epilogue operands
+        int64_t rows = 0;
+        TcLaunch L;
+    };
+    std::vector<TcCached> tc_cache;
 };
 
 // Timing events (pairs: before / after kernels) of a host call.
@@ -510,23 +520,35 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                     ep.push_back(at_row(ptr_of(s.srcs[2 + k]), s.src_rb.empty() ? 0 : s.src_rb[2 + k]));
                 unsigned* err_word = device_error_word(dev);
                 if (!err_word) { set_error(6, "cannot allocate the device error word"); return 6; }
-                TcLaunch L;
                 std::string err;
                 const void* a_lo = s.aux.size() > 0 ? at_row(ptr_of(s.aux[0]), s.aux_rb.empty() ? 0 : s.aux_rb[0]) : nullptr;
                 const void* b_lo = s.aux.size() > 1 ? ptr_of(s.aux[1]) : nullptr;
                 const void* a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
-                int rc = 0;
-                if (cut) {
-                    Step t = s;
-                    t.M = m_run;
-                    rc = tc_prepare(t, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, L, err);
-                } else {
-                    rc = tc_prepare(s, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, L, err);
+                if (ds->tc_cache.size() != p.steps.size()) ds->tc_cache.assign(p.steps.size(), DeviceState::TcCached());
+                DeviceState::TcCached& cached = ds->tc_cache[si];
+                const void* key[14] = {a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, err_word};
+                for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
+                bool hit = cached.valid && cached.rows == m_run;
+                for (int k = 0; hit && k < 14; ++k) hit = cached.key[k] == key[k];
+                if (!hit) {
+                    int rc = 0;
+                    if (cut) {
+                        Step t = s;
+                        t.M = m_run;
+                        rc = tc_prepare(t, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, cached.L, err);
+                    } else {
+                        rc = tc_prepare(s, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, cached.L, err);
+                    }
+                    if (rc) {
+                        cached.valid = false;
+                        set_error(rc, err);
+                        return rc;
+                    }
+                    for (int k = 0; k < 14; ++k) cached.key[k] = key[k];
+                    cached.rows = m_run;
+                    cached.valid = true;
                 }
-                if (rc) {
-                    set_error(rc, err);
-                    return rc;
-                }
+                TcLaunch& L = cached.L;
                 void* params[] = {L.args};
                 CUlaunchConfig cfg;
                 memset(&cfg, 0, sizeof(cfg));

@@ -55,6 +55,12 @@ struct PlainSpec {
     typedef float Out;
     template <class G>
     static __device__ __forceinline__ float apply(float acc, const G&, i64, i64, i64) { return acc; }
+    template <class G>
+    static __device__ __forceinline__ void apply4(const float* acc4, const G&, i64, i64, i64, bafe::Vec4<float>& o4) {
+        for (int e = 0; e < 4; ++e) o4.v[e] = acc4[e];
+    }
+    template <class G>
+    static __device__ __forceinline__ void prefetch(const G&, i64, i64, i64, int) {}
 };
 
 __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1)

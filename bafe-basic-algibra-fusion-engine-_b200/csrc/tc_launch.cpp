@@ -20,6 +20,7 @@ struct alignas(64) TcArgsHost {
     CUtensorMap tmap_b;
     CUtensorMap tmap_a_lo;
     CUtensorMap tmap_b_lo;
+    CUtensorMap tmap_out;
     void* out;
     int64_t M, N, K;
     int64_t o_bstride;
@@ -31,9 +32,11 @@ struct alignas(64) TcArgsHost {
     unsigned long long timeout_ns;
     int32_t batch;
     int32_t a_batched, b_batched;
+    int32_t out_tma;
+    int32_t ep_vec;
 };
 static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
-static_assert(sizeof(TcArgsHost) == 704, "TcArgs layout");
+static_assert(sizeof(TcArgsHost) == 832, "TcArgs layout");
 static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the launch block");
 
 int threads_of(int) { return 320; }
@@ -50,8 +53,10 @@ bool tc_kernel_enabled() {
 }
 
 int tc_smem_bytes(int variant, bool pair) {
-    // alignment slack + stage ring + mbarriers + shared words
-    return 1024 + stages_of(variant, pair) * stage_bytes(variant, pair) + 256;
+    // alignment slack + stage ring + mbarriers and shared words (1 KB, so
+    // the epilogue staging stays 1024-aligned) + the epilogue staging of
+    // the 8 accumulate warps (4 KB each)
+    return 1024 + stages_of(variant, pair) * stage_bytes(variant, pair) + 1024 + 8 * 4096;
 }
 
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
@@ -117,6 +122,24 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     if (lo_maps) {
         if (int rc = map_a(&h.tmap_a_lo, a_lo)) return rc;
         if (int rc = map_b(&h.tmap_b_lo, b_lo)) return rc;
+    }
+    // Epilogue: stores through a TMA map of the output when its results are
+    // 2 or 4 bytes and its rows whole 16-byte units (box: 32 rows x 128
+    // bytes, the accumulate warps' staging sub-tile); 16-byte operand loads
+    // when every epilogue operand is aligned for them (columns come in
+    // groups of 4 from a multiple of 4, and N % 4 == 0).
+    const uint64_t oes = (uint64_t)s.dst_esize;
+    if ((oes == 4 || oes == 2) && (N * oes) % 16 == 0) {
+        uint64_t dims[3] = {N, M, batch}, strides[2] = {N * oes, M * N * oes};
+        uint32_t box[3] = {(uint32_t)(128 / oes), 32, 1};
+        if (int rc = tc_encode_tensor_map(&h.tmap_out, oes == 4 ? 1 : 2, 3, out, dims, strides, box, 1, err)) return rc;
+        h.out_tma = 1;
+    }
+    h.ep_vec = 1;
+    for (size_t k = 0; k < ep.size(); ++k) {
+        const int es = k + 2 < s.src_esize.size() ? s.src_esize[k + 2] : 8;
+        const uintptr_t need = es >= 4 ? 16 : (uintptr_t)(4 * es);
+        if ((uintptr_t)ep[k] % need) h.ep_vec = 0;
     }
     h.out = out;
     h.M = s.M;

@@ -8,7 +8,7 @@ Headline workload (one "step" = one call of the plan):
         rows are split into contiguous row panels, one per rank; B is
         broadcast once from rank 0 over NCCL (outside the timed region, as
         the runtime keeps B resident; its time is reported separately).
-Secondary (same JSON line, keys "gemm_bf16", "ew" and "transpose"):
+Secondary (same JSON line, keys "gemm_bf16", "ew", "transpose", "configs"):
   gemm_bf16: the same fused GEMM with bf16 A, B, C and output (kind::f16
         tensor cores, f32 accumulation).
   ew:   relu(add(mul(X,Y),Z)) over 2^28 fp32 elements (1 GiB per vector),
@@ -17,6 +17,10 @@ Secondary (same JSON line, keys "gemm_bf16", "ew" and "transpose"):
   transpose: materialisation of transpose(X), X 16384 x 16384 fp32; ranks
         own output row blocks (input column panels), no collective.
         Metric GB/s (8 bytes per element).
+  configs: the reference's other benchmark configurations on rank 0's GPU:
+        relu(matmul(A,B)+C) 64^3 and matmul 256^3 (B row- / col-major) in
+        microseconds per call (launch-latency bound), relu(add(matmul(A,B),
+        mul(C,D))) 4096^3 in TFLOP/s.
 
 value:   device-resident inputs, CUDA events around every step on the
          launching stream, max over ranks; inputs are larger than L2
@@ -585,6 +589,65 @@ def bench_transpose(c: Ctx) -> dict:
     return res
 
 
+def bench_configs(c: Ctx) -> dict:
+    """The other configurations of the reference's benchmark set, on one GPU
+    (rank 0; they are too small to shard): relu(matmul(A,B)+C) at 64^3,
+    matmul at 256^3 with B row- and column-major (launch-latency bound:
+    microseconds per call, no roofline claim), and relu(add(matmul(A,B),
+    mul(C,D))) at 4096^3 (tensor-core bound)."""
+    import bafe_b200 as bafe
+    torch = c.torch
+    g0 = torch.Generator(device=c.dev).manual_seed(5)
+    out = {}
+
+    def run(name, g, shapes, steps, flops=None):
+        import ctypes
+        from bafe_b200._binding import lib
+        k = bafe.compile_graph(g)
+        ins = [torch.randn(*sh, device=c.dev, generator=g0) for sh in shapes]
+        o = torch.empty(*k.out_shape, device=c.dev)
+        per, total, _ = time_steps(torch, k, ins, o, steps, 5)
+        # device time per call with the launches issued back to back from C
+        # (bafe_cuda_time_device), free of the Python call overhead that the
+        # per-step events above include for microsecond-sized calls
+        ptrs = (ctypes.c_void_p * (len(ins) + 1))(*[t.data_ptr() for t in ins + [o]])
+        dev_ms = ctypes.c_double()
+        lib.bafe_cuda_time_device(k.plan, ptrs, len(ins) + 1, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                  steps, ctypes.byref(dev_ms))
+        hins = [t.cpu().pin_memory() for t in ins]
+        hout = torch.empty(*k.out_shape).pin_memory()
+        e2e_ms = time_e2e(torch, k, hins, hout, 20)
+        ms = total / steps
+        r = {"plan": k.describe().strip(), "device_us_per_call": round(dev_ms.value * 1e3, 2),
+             "python_loop_us_per_call": round(ms * 1e3, 2), "e2e_us_per_call": round(e2e_ms * 1e3, 1)}
+        if flops:
+            achieved = flops / (statistics.mean(per) * 1e-3) / 1e12
+            basis = c.bf16_peak / 2.0 / (3.0 if "3xtf32" in r["plan"] else 1.0)
+            r.update({"value": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
+                      "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(basis, 1),
+                                   "unit": "TFLOP/s", "frac": round(achieved / basis, 4),
+                                   "peak_basis": f"{c.peak_src} burst bf16 / 2 (tf32 rate)"
+                                                 + (" / 3 (three products)" if "3xtf32" in r["plan"] else "")}})
+        out[name] = r
+
+    g = bafe.GraphBuilder()
+    a, b, cc = (g.add_input(n, (64, 64), 0, 0) for n in "ABC")
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), cc])]))
+    run("cfg1 relu(matmul(A,B)+C) 64^3", g, [(64, 64)] * 3, 200)
+    for col in (0, 1):
+        g = bafe.GraphBuilder()
+        a = g.add_input("A", (256, 256), 0, 0)
+        b = g.add_input("B", (256, 256), 0, col)
+        g.set_output(g.add("matmul", [a, b]))
+        run(f"cfg2 matmul 256^3 B {'col' if col else 'row'}-major", g, [(256, 256)] * 2, 200)
+    n = 4096
+    g = bafe.GraphBuilder()
+    a, b, cc, dd = (g.add_input(x, (n, n), 0, 0) for x in "ABCD")
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), g.add("mul", [cc, dd])])]))
+    run("cfg3 relu(add(matmul(A,B),mul(C,D))) 4096^3", g, [(n, n)] * 4, 20, flops=2.0 * n ** 3)
+    return out
+
+
 def run_ours(args):
     import bafe_b200 as bafe
     c = Ctx(args)
@@ -601,6 +664,8 @@ def run_ours(args):
             line["gemm_bf16"] = bench_gemm_bf16(c)
             line["ew"] = bench_ew(c)
             line["transpose"] = bench_transpose(c)
+            if c.rank == 0:
+                line["configs"] = bench_configs(c)
     if c.rank == 0:
         print(json.dumps(line), flush=True)
     if c.dist is not None:

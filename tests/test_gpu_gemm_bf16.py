@@ -43,6 +43,7 @@ def _graph(shape_a, shape_b, a_col, b_col, epi):
     ((512, 384, 256), 1, 1, "relu_add_c"),
     ((304, 264, 520), 0, 1, "relu_add_c"),
     ((304, 264, 520), 1, 0, "none"),
+    ((304, 260, 520), 0, 1, "relu_add_c"),      # 520-byte rows: plain stores, no TMA
     ((1024, 2048, 1024), 0, 0, "relu_add_c"),
     ((3, 256, 512, 128), 0, 0, "relu_add_c"),
 ])

@@ -231,3 +231,97 @@ def test_3xtf32_in_kernel_residuals(cuda, shape, a_col, b_col, pair):
     bound = 1e-4 * math.sqrt(K / 64)
     print(f"3xtf32 in-kernel residuals {shape} pair={pair}: max err {err:.3e} (bound {bound:.1e})")
     assert err <= bound
+
+
+def test_prepared_launch_follows_new_buffers(cuda):
+    """The runtime reuses a step's prepared tensor maps while its buffers stay
+    the same; new input / epilogue / output buffers must be picked up."""
+    torch = cuda
+    bafe.set_option("gemm_precision", "3xtf32")
+    k = bafe.compile_graph(_graph(512, 384, 256, 0, 0, "relu_add_c"))
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    outs = []
+    for it in range(3):
+        A = torch.randn(512, 256, device="cuda", generator=gen)
+        B = torch.randn(256, 384, device="cuda", generator=gen)
+        C = torch.randn(512, 384, device="cuda", generator=gen)
+        out = torch.empty(512, 384, device="cuda")
+        for _ in range(2):                               # second call reuses the prepared launch
+            k.run_torch([A, B, C], out)
+        bafe.synchronize()
+        ref = torch.relu(A.double() @ B.double() + C.double())
+        assert float((out.double() - ref).abs().max()) <= 1e-4 * math.sqrt(256 / 64), it
+        outs.append(out)
+
+
+# ------------------------------------------------------------ epilogue --
+# Epilogue operands are read as 4-element vectors when every one is aligned
+# for that (16 bytes; 8 for 16-bit operands), element by element otherwise;
+# the output is written by TMA stores from shared memory, which clip rows
+# >= M and columns >= N.
+
+@pytest.mark.parametrize("prec", ["tf32", "3xtf32"])
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_epilogue_operands_off_vector_alignment(cuda, prec, pair):
+    """C at a 4-byte and the bias at a 12-byte offset: element reads."""
+    torch = cuda
+    M, N, K = 300, 516, 256
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    A = torch.randn(M, K, device="cuda", generator=gen)
+    B = torch.randn(K, N, device="cuda", generator=gen)
+    C = torch.randn(M * N + 1, device="cuda", generator=gen)[1:].view(M, N)
+    bias = torch.randn(N + 3, device="cuda", generator=gen)[3:]
+    assert C.data_ptr() % 16 == 4 and bias.data_ptr() % 16 == 12
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", (M, K), 0, 0)
+    b = g.add_input("B", (K, N), 0, 0)
+    c = g.add_input("C", (M, N), 0, 0)
+    v = g.add_input("bias", (N,), 0, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("add", [g.add("matmul", [a, b]), c]), v])]))
+    bafe.set_option("gemm_precision", prec)
+    bafe.set_option("tc_pair", pair)
+    try:
+        k = bafe.compile_graph(g)
+        assert "gemm.tc" in k.describe()
+        out = torch.full((M, N), float("nan"), device="cuda")
+        k.run_torch([A, B, C, bias], out)
+        bafe.synchronize()
+    finally:
+        bafe.set_option("tc_pair", "1")
+    ref = torch.relu(A.double() @ B.double() + C.double() + bias.double())
+    err = float((out.double() - ref).abs().max())
+    tol = (1e-4 if prec == "3xtf32" else TF32_TOL) * math.sqrt(K / 64)
+    print(f"misaligned epilogue operands {prec} pair={pair}: max err {err:.3e}")
+    assert err <= tol
+
+
+@pytest.mark.parametrize("pair", ["1", "0"])
+def test_epilogue_half_operands(cuda, pair):
+    """f16 and bf16 epilogue operands (8-byte vectors), f32 output, ragged tiles."""
+    torch = cuda
+    M, N, K = 520, 388, 320
+    gen = torch.Generator(device="cuda").manual_seed(37)
+    A = torch.randn(M, K, device="cuda", generator=gen)
+    B = torch.randn(K, N, device="cuda", generator=gen)
+    C = torch.randn(M, N, device="cuda", generator=gen).to(torch.float16)
+    D = torch.randn(N, device="cuda", generator=gen).to(torch.bfloat16)
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", (M, K), 0, 0)
+    b = g.add_input("B", (K, N), 0, 0)
+    c = g.add_input("C", (M, N), 4, 0)
+    d = g.add_input("D", (N,), 5, 0)
+    g.set_output(g.add("mul", [g.add("add", [g.add("matmul", [a, b]), c]), d]))
+    bafe.set_option("gemm_precision", "3xtf32")
+    bafe.set_option("tc_pair", pair)
+    try:
+        k = bafe.compile_graph(g)
+        assert "gemm.tc.3xtf32" in k.describe()
+        out = torch.full((M, N), float("nan"), device="cuda")
+        k.run_torch([A, B, C.view(torch.int16), D.view(torch.int16)], out)
+        bafe.synchronize()
+    finally:
+        bafe.set_option("tc_pair", "1")
+    ref = (A.double() @ B.double() + C.double()) * D.double()
+    err = float((out.double() - ref).abs().max())
+    print(f"half epilogue operands pair={pair}: max err {err:.3e}")
+    assert err <= 1e-4 * math.sqrt(K / 64) * float(D.double().abs().max())
