@@ -94,7 +94,7 @@ enum class StepKind { Ew, GemmExact, GemmTc, Transpose2d, Gather, Reduce, Zero }
 struct Step {
     StepKind kind = StepKind::Ew;
     std::string kernel;            // entry point (extern "C") in the plan's module
-    std::string kernel_vec;        // Ew: vectorised entry point ("" if none)
+    std::string kernel_vec;        // Ew: vectorised entry point ("" if none); GemmTc: split-tail fixup
     BufRef dst;
     std::vector<BufRef> srcs;      // operands in kernel argument order
     int64_t dst_bytes = 0;

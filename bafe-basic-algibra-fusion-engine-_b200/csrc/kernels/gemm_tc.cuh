@@ -61,6 +61,7 @@ struct TcArgs {
     TmaDesc tmap_a_lo;             // 3xTF32 residuals (same layouts as A, B)
     TmaDesc tmap_b_lo;
     TmaDesc tmap_out;              // output, for TMA stores (valid when out_tma)
+    TmaDesc tmap_ws;               // split partials [parts x tile rows][256] f32 (valid when split > 1)
     void* out;
     i64 M, N, K;
     i64 o_bstride;
@@ -74,8 +75,31 @@ struct TcArgs {
     int a_batched, b_batched;      // operand has its own matrix per batch item
     int out_tma;                   // epilogue stores through tmap_out
     int ep_vec;                    // epilogue operands load as 4-element vectors
+    float* ws;                     // split partials (see unit_range)
+    int split;                     // K ranges per tail tile (1: no split)
+    int split_first;               // first split tile: tiles [split_first, num_tiles) are split
+    int num_units;                 // split_first + (num_tiles - split_first) * split
 };
-static_assert(sizeof(TcArgs) == 832, "TcArgs layout (mirrored by the host)");
+static_assert(sizeof(TcArgs) == 960, "TcArgs layout (mirrored by the host)");
+
+// Work units of the persistent kernels.  Tiles [0, split_first) are whole
+// units; when the last wave would leave CTAs idle, each tile from
+// split_first on becomes `split` units over consecutive ranges of whole
+// TMEM chunks [c0, c1) of K, which store their fp32 partial tile to ws
+// (part p of split tile s at rows (s * split + p) * tile rows); the fixup
+// kernel (gemm_tc_fixup) adds the parts in order and applies the epilogue.
+// part = -1 for a whole tile.
+__device__ __forceinline__ void unit_range(const TcArgs& g, int u, int n_chunks, int& t, int& c0, int& c1, int& part) {
+    if (u < g.split_first) {
+        t = u; c0 = 0; c1 = n_chunks; part = -1;
+        return;
+    }
+    const int v = u - g.split_first;
+    t = g.split_first + v / g.split;
+    part = v % g.split;
+    c0 = (int)((long long)part * n_chunks / g.split);
+    c1 = (int)((long long)(part + 1) * n_chunks / g.split);
+}
 
 template <int VARIANT> struct TcCfg;
 // KB_PER_CHUNK k-blocks (of 32) per TMEM partial sum: the 3xTF32 variant,
@@ -390,7 +414,8 @@ __device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int
 //   * pass 2 stores through TMA: each 32-row x 128-byte sub-tile is written
 //     to this warp's 4 KB staging buffer in shared memory (128B swizzle,
 //     conflict-free 16-byte stores) and one lane issues a bulk tensor store,
-//     which writes whole rows and clips rows >= M and columns >= N.
+//     which writes whole rows and clips rows >= M and columns >= N (L2
+//     evict-first, like streaming stores).
 // Measured on a 256^3 tf32 pair tile: relu(acc + C) 41k -> 12k cycles,
 // plain stores 9.3k -> 4.5k.  Results of at most 4 bytes are kept, as
 // bits, in the accumulator registers between the passes.
@@ -413,6 +438,50 @@ __device__ __forceinline__ uint4 tc_chunk(const float* a) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) w[e] = (__float_as_uint(a[2 * e]) & 0xFFFFu) | (__float_as_uint(a[2 * e + 1]) << 16);
         return make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+// TMA store of one accumulate warp's 32 rows x 128 results (their bits in
+// acc): 32-row x 128-byte sub-tiles through the warp's staging buffer
+// (128B swizzle: lane r writes its 16-byte chunk c at chunk c ^ (r & 7) of
+// row r, conflict-free), one bulk tensor store each, at map coordinates
+// (x0 + sub-tile column, y0, z); sub-tiles from x_end on are skipped.
+// EVICT_FIRST: the rows are not read again soon (final output).
+template <class Out, bool EVICT_FIRST>
+__device__ __forceinline__ void tc_store_rows(const float (&acc)[128], const TmaDesc* map, i64 x0, i64 y0, i64 z, i64 x_end,
+                                              u32 stg, int lane) {
+    constexpr int SUB = 128 / sizeof(Out);            // columns per 128-byte sub-tile
+    constexpr int PER = 16 / sizeof(Out);             // results per 16-byte chunk
+#pragma unroll
+    for (int sb = 0; sb < 128 / SUB; ++sb) {
+        if (x0 + sb * SUB >= x_end) break;            // warp-uniform
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // buffer free
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint4 w = tc_chunk<Out>(acc + sb * SUB + c * PER);
+            const u32 addr = stg + (u32)lane * 128u + (u32)((c ^ (lane & 7)) * 16);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w.x), "r"(w.y), "r"(w.z), "r"(w.w)
+                         : "memory");
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the TMA unit
+        __syncwarp();
+        if (lane == 0) {
+            if (EVICT_FIRST) {
+                // like streaming stores: the output must not push the
+                // operand panels out of L2
+                u64 policy;
+                asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+                asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint"
+                             " [%0, {%1, %2, %3}], [%4], %5;"
+                             ::"l"(map), "r"((int)(x0 + sb * SUB)), "r"((int)y0), "r"((int)z), "r"(stg), "l"(policy)
+                             : "memory");
+            } else {
+                asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
+                             ::"l"(map), "r"((int)(x0 + sb * SUB)), "r"((int)y0), "r"((int)z), "r"(stg) : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
     }
 }
 
@@ -463,29 +532,7 @@ __device__ __forceinline__ void tc_epilogue(float (&acc)[128], const TcArgs& g, 
         }
         // pass 2
         if (g.out_tma) {
-            constexpr int SUB = 128 / sizeof(Out);        // columns per 128-byte sub-tile
-            constexpr int PER = 16 / sizeof(Out);         // results per 16-byte chunk
-#pragma unroll
-            for (int sb = 0; sb < 128 / SUB; ++sb) {
-                if (n0 + sb * SUB >= g.N) break;          // warp-uniform
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // buffer free
-                __syncwarp();
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 w = tc_chunk<Out>(acc + sb * SUB + c * PER);
-                    const u32 addr = stg + (u32)lane * 128u + (u32)((c ^ (lane & 7)) * 16);
-                    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w.x), "r"(w.y), "r"(w.z),
-                                 "r"(w.w) : "memory");
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the TMA unit
-                __syncwarp();
-                if (lane == 0) {
-                    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, %3}], [%4];"
-                                 ::"l"(&g.tmap_out), "r"((int)(n0 + sb * SUB)), "r"((int)i0), "r"((int)bi), "r"(stg)
-                                 : "memory");
-                    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-                }
-            }
+            tc_store_rows<Out, true>(acc, &g.tmap_out, n0, i0, bi, g.N, stg, lane);
         } else if (i < g.M) {
             Out* row = out + bi * g.o_bstride + i * g.N + n0;
 #pragma unroll
@@ -502,8 +549,45 @@ __device__ __forceinline__ void tc_epilogue(float (&acc)[128], const TcArgs& g, 
 }
 // Before the CTA exits or its staging is reused by another kernel role:
 // the warp's bulk stores have completed.
-__device__ __forceinline__ void tc_epilogue_flush(const TcArgs& g, int lane) {
-    if (g.out_tma && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+__device__ __forceinline__ void tc_epilogue_flush(int lane) {
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Split tail tiles: out = epi(sum of the K-range partials in ws, in part
+// order), 4 columns per thread (N % 4 == 0), rows of TILE_M-row tiles.
+template <class Spec, int TILE_M>
+__device__ __forceinline__ void gemm_tc_fixup(const TcArgs& g) {
+    typedef typename Spec::Out Out;
+    const i64 per_tile = (i64)TILE_M * 64;           // 4-column groups of a tile
+    const i64 part_elems = (i64)TILE_M * 256;
+    const i64 total = (i64)(g.num_tiles - g.split_first) * per_tile;
+    Out* out = reinterpret_cast<Out*>(g.out);
+    for (i64 x = (i64)blockIdx.x * blockDim.x + threadIdx.x; x < total; x += (i64)gridDim.x * blockDim.x) {
+        const int tl = (int)(x / per_tile);
+        const int r = (int)(x % per_tile / 64), c = (int)(x % 64) * 4;
+        int mb, nb, bi;
+        tc::tile_coords(g, g.split_first + tl, mb, nb, bi);
+        const i64 i = (i64)mb * TILE_M + r, j = (i64)nb * 256 + c;
+        if (i >= g.M || j >= g.N) continue;
+        const float* p = g.ws + (i64)tl * g.split * part_elems + (i64)r * 256 + c;
+        float4 sum = __ldcs(reinterpret_cast<const float4*>(p));
+        for (int q = 1; q < g.split; ++q) {
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(p + q * part_elems));
+            sum.x = __fadd_rn(sum.x, v.x);
+            sum.y = __fadd_rn(sum.y, v.y);
+            sum.z = __fadd_rn(sum.z, v.z);
+            sum.w = __fadd_rn(sum.w, v.w);
+        }
+        const float a[4] = {sum.x, sum.y, sum.z, sum.w};
+        Vec4<Out> o;
+        if (g.ep_vec) {
+            Spec::apply4(a, g, bi, i, j, o);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o.v[e] = Spec::apply(a[e], g, bi, i, j + e);
+        }
+        st4(out + bi * g.o_bstride + i * g.N + j, o);
+    }
 }
 
 // Operand element types.  A k-block is one 128-byte swizzle row of K: 32
@@ -608,17 +692,20 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             u32 armed[STAGES];
             for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+            for (int u = blockIdx.x; ok && u < g.num_units; u += gridDim.x) {
+                int t, c0, c1, part;
+                unit_range(g, u, n_chunks, t, c0, c1, part);
                 int mb, nb, bi;
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * BM, n0 = nb * BN;
+                const int kb_stop = c1 * KB_PER_CHUNK < k_blocks ? c1 * KB_PER_CHUNK : k_blocks;
                 // Every operand map is 3-D (batch extent 1 when the operand
                 // is shared): the batch coordinate is fixed per tile, so the
                 // k-loop issues one load form without a branch.
                 const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
                 auto load_a = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d(dst, m, bar, x, y, za); };
                 auto load_b = [&](u32 dst, const TmaDesc* m, u32 bar, int x, int y) { tma_load_3d(dst, m, bar, x, y, zb); };
-                for (int kb = 0; kb < k_blocks; ++kb) {
+                for (int kb = c0 * KB_PER_CHUNK; kb < kb_stop; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
                     const u32 b_dst = a_dst + A_BYTES;
@@ -665,8 +752,10 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             u32 phase = 0;
             u32 chunk = 0;                              // chunks issued by this CTA
             bool ok = true;
-            for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
-                for (int c = 0; ok && c < n_chunks; ++c, ++chunk) {
+            for (int u = blockIdx.x; ok && u < g.num_units; u += gridDim.x) {
+                int t, c0, c1, part;
+                unit_range(g, u, n_chunks, t, c0, c1, part);
+                for (int c = c0; ok && c < c1; ++c, ++chunk) {
                     const int buf = (int)(chunk & 1u);
                     const u32 use = (chunk >> 1) & 1u;
                     if (!wait(TEMPTY(buf), use ^ 1u, sh, g, 2u)) { ok = false; break; }
@@ -713,7 +802,6 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
         // ------------------------------------ accumulate + epilogue --
         const int q = warp & 3;                        // TMEM lane quadrant
         const int half = (warp - 2) >> 2;              // column half of the tile
-        const int row_in_tile = q * 32 + lane;
         const u32 lane_addr = (u32)(q * 32) << 16;
         typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
         const u32 stg = base + STAGES * STAGE_BYTES + EPI_OFFSET + (u32)(warp - 2) * EPI_WARP_BYTES;
@@ -745,22 +833,19 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             }
             return true;
         };
-        for (int t = blockIdx.x; ok && t < g.num_tiles; t += gridDim.x) {
+        for (int u = blockIdx.x; ok && u < g.num_units; u += gridDim.x) {
+            int t, c0, c1, part;
+            unit_range(g, u, n_chunks, t, c0, c1, part);
             // k-blocks this CTA still has after the current tile, capped
-            const long long after = (long long)(g.num_tiles - 1 - t) / (int)gridDim.x * k_blocks;
+            // (with converted residuals the tiles are never split: u == t)
+            const long long after = (long long)(g.num_units - 1 - u) / (int)gridDim.x * k_blocks;
             const int limit = k_blocks + (after < KB_PER_CHUNK ? (int)after : KB_PER_CHUNK);
             float acc[128];
 #pragma unroll
             for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
-            for (int c = 0; c < n_chunks; ++c, ++chunk) {
+            for (int c = c0; c < c1; ++c, ++chunk) {
                 const int buf = (int)(chunk & 1u);
                 const u32 use = (chunk >> 1) & 1u;
-                if (c == n_chunks - 1) {               // epilogue operands into L2 meanwhile
-                    int pmb, pnb, pbi;
-                    tile_coords(g, t, pmb, pnb, pbi);
-                    const i64 pi = (i64)pmb * BM + row_in_tile, pn0 = (i64)pnb * BN + half * 128;
-                    if (pi < g.M && pn0 < g.N) Spec::prefetch(g, pbi, pi, pn0, (int)(g.N - pn0 < 128 ? g.N - pn0 : 128));
-                }
                 const int c_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
                 const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
                 // warp-uniform: tcgen05.ld below needs all 32 lanes converged
@@ -783,9 +868,11 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
             tile_coords(g, t, mb, nb, bi);
             const i64 i0 = (i64)mb * BM + q * 32;
             const i64 n0 = (i64)nb * BN + half * 128;
-            tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
+            if (part < 0) tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
+            else tc_store_rows<float, false>(acc, &g.tmap_ws, half * 128, ((i64)(t - g.split_first) * g.split + part) * BM + q * 32,
+                                             0, 256, stg, lane);
         }
-        tc_epilogue_flush(g, lane);
+        tc_epilogue_flush(lane);
     }
 
     // ------------------------------------------------------- teardown --
@@ -883,10 +970,13 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             u32 armed[STAGES];
             for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
             bool ok = true;
-            for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+            for (int u = pair; ok && u < g.num_units; u += num_pairs) {
+                int t, c0, c1, part;
+                unit_range(g, u, n_chunks, t, c0, c1, part);
                 int mb, nb, bi;
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
+                const int kb_stop = c1 * KB_PER_CHUNK < k_blocks ? c1 * KB_PER_CHUNK : k_blocks;
                 const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
                 // With converted residuals each CTA's copies complete on its
                 // own FULL barrier (its converting threads wait there);
@@ -899,7 +989,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     if (CONV) tma_load_3d(dst, m, bar, x, y, zb);
                     else tma_load_3d_pair(dst, m, bar, x, y, zb);
                 };
-                for (int kb = 0; kb < k_blocks; ++kb) {
+                for (int kb = c0 * KB_PER_CHUNK; kb < kb_stop; ++kb) {
                     if (!wait(EMPTY(s), phase ^ 1u, sh, g, 1u)) { ok = false; break; }
                     const u32 a_dst = base + s * STAGE_BYTES;
                     const u32 b_dst = a_dst + A_BYTES;
@@ -954,8 +1044,10 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             u32 phase = 0;
             u32 chunk = 0;
             bool ok = true;
-            for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
-                for (int c = 0; ok && c < n_chunks; ++c, ++chunk) {
+            for (int u = pair; ok && u < g.num_units; u += num_pairs) {
+                int t, c0, c1, part;
+                unit_range(g, u, n_chunks, t, c0, c1, part);
+                for (int c = c0; ok && c < c1; ++c, ++chunk) {
                     const int buf = (int)(chunk & 1u);
                     const u32 use = (chunk >> 1) & 1u;
                     if (!wait(TEMPTY(buf), use ^ 1u, sh, g, 2u)) { ok = false; break; }
@@ -1000,7 +1092,6 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
         // ------------------------- accumulate + epilogue (both CTAs) --
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
-        const int row_in_tile = q * 32 + lane;
         const u32 lane_addr = (u32)(q * 32) << 16;
         typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out);
         const u32 stg = base + STAGES * STAGE_BYTES + EPI_OFFSET + (u32)(warp - 2) * EPI_WARP_BYTES;
@@ -1033,22 +1124,19 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             }
             return true;
         };
-        for (int t = pair; ok && t < g.num_tiles; t += num_pairs) {
+        for (int u = pair; ok && u < g.num_units; u += num_pairs) {
+            int t, c0, c1, part;
+            unit_range(g, u, n_chunks, t, c0, c1, part);
             // k-blocks this CTA still has after the current tile, capped
-            const long long after = (long long)(g.num_tiles - 1 - t) / num_pairs * k_blocks;
+            // (with converted residuals the tiles are never split: u == t)
+            const long long after = (long long)(g.num_units - 1 - u) / num_pairs * k_blocks;
             const int limit = k_blocks + (after < KB_PER_CHUNK ? (int)after : KB_PER_CHUNK);
             float acc[128];
 #pragma unroll
             for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
-            for (int c = 0; c < n_chunks; ++c, ++chunk) {
+            for (int c = c0; c < c1; ++c, ++chunk) {
                 const int buf = (int)(chunk & 1u);
                 const u32 use = (chunk >> 1) & 1u;
-                if (c == n_chunks - 1) {               // epilogue operands into L2 meanwhile
-                    int pmb, pnb, pbi;
-                    tile_coords(g, t, pmb, pnb, pbi);
-                    const i64 pi = (i64)pmb * 2 * BM + (i64)cta * BM + row_in_tile, pn0 = (i64)pnb * BN + half * 128;
-                    if (pi < g.M && pn0 < g.N) Spec::prefetch(g, pbi, pi, pn0, (int)(g.N - pn0 < 128 ? g.N - pn0 : 128));
-                }
                 const int c_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
                 const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
                 const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
@@ -1076,9 +1164,12 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             tile_coords(g, t, mb, nb, bi);
             const i64 i0 = (i64)mb * 2 * BM + (i64)cta * BM + q * 32;
             const i64 n0 = (i64)nb * BN + half * 128;
-            tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
+            if (part < 0) tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
+            else tc_store_rows<float, false>(acc, &g.tmap_ws, half * 128,
+                                             ((i64)(t - g.split_first) * g.split + part) * 2 * BM + cta * BM + q * 32, 0, 256,
+                                             stg, lane);
         }
-        tc_epilogue_flush(g, lane);
+        tc_epilogue_flush(lane);
     }
 
     // ------------------------------------------------------- teardown --

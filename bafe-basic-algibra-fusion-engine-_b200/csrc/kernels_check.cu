@@ -24,10 +24,6 @@ struct CheckSpec {
 #pragma unroll
         for (int e = 0; e < 4; ++e) o4.v[e] = bafe::relu(bafe::add(acc4[e], v0.v[e]));
     }
-    template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0, int n) {
-        const char* p = reinterpret_cast<const char*>(g.ep[0]) + (b * g.o_bstride + i * g.N + j0) * 4;
-        for (int o = 0; o < n * 4; o += 128) asm volatile("prefetch.global.L2 [%0];" :: "l"(p + o));
-    }
 };
 
 extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
@@ -44,6 +40,9 @@ extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) che
 }
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_tc1_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpec, 1>(g);
+}
+extern "C" __global__ void __launch_bounds__(256) check_gemm_tc_fixup_pair(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_fixup<CheckSpec, 256>(g);
 }
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<3>::THREADS, 1) check_gemm_tc3_pair_conv(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpec, 3, bafe::ElemTf32, true>(g);
@@ -62,13 +61,15 @@ struct CheckSpecBf16 {
 #pragma unroll
         for (int e = 0; e < 4; ++e) o4.v[e] = bafe::f32_to_bf16(bafe::relu(acc4[e]));
     }
-    template <class G> static __device__ __forceinline__ void prefetch(const G&, i64, i64, i64, int) {}
 };
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_bf16_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpecBf16, 1, bafe::ElemBf16>(g);
 }
 extern "C" __global__ void __launch_bounds__(bafe::TcCfg<1>::THREADS, 1) check_gemm_bf16(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc<CheckSpecBf16, 1, bafe::ElemBf16>(g);
+}
+extern "C" __global__ void __launch_bounds__(256) check_gemm_tc_fixup_bf16(const __grid_constant__ bafe::TcArgs g) {
+    bafe::gemm_tc_fixup<CheckSpecBf16, 128>(g);
 }
 extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
     bafe::transpose2d<float>(x, out, M, N);

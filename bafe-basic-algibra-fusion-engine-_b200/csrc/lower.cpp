@@ -630,19 +630,7 @@ struct Lowerer {
         };
         emit_apply(false);
         emit_apply(true);
-        // prefetch(g, b, i, j0, n): pull the epilogue operands of output
-        // row i, columns [j0, j0 + n), into L2 ahead of apply() (the
-        // tensor-core kernels call it while their last chunk runs).
-        src << "  template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0, int n) {\n"
-            << "    (void)g; (void)b; (void)i; (void)j0; (void)n;\n";
-        for (size_t k = 0; k < leaves.size(); ++k) {
-            const int node = leaves[k].node;
-            const int es = dtype_size(buf_dtype[node]);
-            const std::string first = leaves[k].access == ROW ? "j0" : "(b * g.o_bstride + i * g.N + j0)";
-            src << "    { const char* p = reinterpret_cast<const char*>(g.ep[" << k << "]) + " << first << " * " << es
-                << "; for (int o = 0; o < n * " << es << "; o += 128) asm volatile(\"prefetch.global.L2 [%0];\" :: \"l\"(p + o)); }\n";
-        }
-        src << "  }\n};\n";
+        src << "};\n";
         for (auto& l : leaves) s.srcs.push_back(buf[l.node]);
         s.n_epi = (int)leaves.size();
         s.src_esize = {dtype_size(buf_dtype[g.ch[0]]), dtype_size(buf_dtype[g.ch[1]])};
@@ -669,6 +657,11 @@ struct Lowerer {
                 << ">::THREADS, 1) " << s.kernel << "(const __grid_constant__ bafe::TcArgs g) { bafe::" << fn << "<"
                 << S_ << ", " << s.tc_variant << ", " << elem << ", " << (s.tc_convert ? "true" : "false")
                 << ">(g); }\n";
+            // the partial sums of split tail tiles -> epilogue (launched only when the tail splits)
+            s.kernel_vec = s.kernel + "_fix";
+            src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel_vec
+                << "(const __grid_constant__ bafe::TcArgs g) { bafe::gemm_tc_fixup<" << S_ << ", "
+                << (s.tc_pair ? 256 : 128) << ">(g); }\n";
         }
         char geo[256];
         snprintf(geo, sizeof(geo), " batch=%lld m=%lld n=%lld k=%lld a=%s b=%s", (long long)batch, (long long)M,

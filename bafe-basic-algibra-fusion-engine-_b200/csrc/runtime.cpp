@@ -276,11 +276,15 @@ struct DeviceState {
     // tensor maps per call is host work that small GEMMs would wait for.
     struct TcCached {
         bool valid = false;
-        const void* key[14] = {};   // a, b, a_lo, b_lo, out, error word, 8 epilogue operands
+        const void* key[15] = {};   // a, b, a_lo, b_lo, out, error word, 8 epilogue operands, workspace
         int64_t rows = 0;
         TcLaunch L;
     };
     std::vector<TcCached> tc_cache;
+    // Partial tiles of split tensor-core GEMMs (grown on demand; every
+    // split step of the plan runs on `stream`, one after another).
+    void* tc_ws = nullptr;
+    size_t tc_ws_bytes = 0;
 };
 
 // Timing events (pairs: before / after kernels) of a host call.
@@ -526,25 +530,41 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 const void* a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
                 if (ds->tc_cache.size() != p.steps.size()) ds->tc_cache.assign(p.steps.size(), DeviceState::TcCached());
                 DeviceState::TcCached& cached = ds->tc_cache[si];
-                const void* key[14] = {a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, err_word};
-                for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
-                bool hit = cached.valid && cached.rows == m_run;
-                for (int k = 0; hit && k < 14; ++k) hit = cached.key[k] == key[k];
-                if (!hit) {
-                    int rc = 0;
-                    if (cut) {
-                        Step t = s;
-                        t.M = m_run;
-                        rc = tc_prepare(t, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, cached.L, err);
+                Step panel;                                  // the step over this call's rows
+                if (cut) {
+                    panel = s;
+                    panel.M = m_run;
+                }
+                const Step& run = cut ? panel : s;
+                // workspace for the partials of a split tail (none if it cannot be had)
+                const size_t ws_need = ds->fn_vec[si] ? tc_split_of(run, sm_count(dev)).ws_bytes : 0;
+                if (ws_need > ds->tc_ws_bytes) {
+                    void* w = nullptr;
+                    if (cudaMalloc(&w, ws_need) == cudaSuccess) {
+                        if (ds->tc_ws) {
+                            cudaStreamSynchronize(stream);   // earlier launches may still read the old one
+                            cudaFree(ds->tc_ws);
+                        }
+                        ds->tc_ws = w;
+                        ds->tc_ws_bytes = ws_need;
                     } else {
-                        rc = tc_prepare(s, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word, cached.L, err);
+                        cudaGetLastError();
                     }
+                }
+                const void* key[15] = {a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, err_word};
+                for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
+                key[14] = ds->tc_ws;
+                bool hit = cached.valid && cached.rows == m_run;
+                for (int k = 0; hit && k < 15; ++k) hit = cached.key[k] == key[k];
+                if (!hit) {
+                    int rc = tc_prepare(run, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word,
+                                        ds->fn_vec[si] ? ds->tc_ws : nullptr, ds->tc_ws_bytes, cached.L, err);
                     if (rc) {
                         cached.valid = false;
                         set_error(rc, err);
                         return rc;
                     }
-                    for (int k = 0; k < 14; ++k) cached.key[k] = key[k];
+                    for (int k = 0; k < 15; ++k) cached.key[k] = key[k];
                     cached.rows = m_run;
                     cached.valid = true;
                 }
@@ -569,6 +589,9 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 CUresult r = driver().launchKernelEx(&cfg, ds->fn[si], params, nullptr);
                 if (r != CUDA_SUCCESS) { set_error(7, "tensor-core GEMM launch failed: " + cu_err(r)); return 7; }
                 ++g_launch_count;
+                if (L.fix_grid) {                            // split tail tiles: sum the partials, epilogue
+                    if (int rc = launch(ds->fn_vec[si], L.fix_grid, 1, 1, 256, 1, 1, 0, stream, params)) return rc;
+                }
                 break;
             }
             case StepKind::Transpose2d: {
@@ -912,6 +935,7 @@ void release_plan_device_state(Plan& p) {
         for (void* t : s->tmp) if (t) cudaFree(t);
         for (void* t : s->in_stage) if (t) cudaFree(t);
         if (s->out_stage) cudaFree(s->out_stage);
+        if (s->tc_ws) cudaFree(s->tc_ws);
         for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
         for (cudaEvent_t ev : s->events) cudaEventDestroy(ev);
         for (cudaEvent_t ev : s->tev) cudaEventDestroy(ev);

@@ -59,8 +59,6 @@ struct PlainSpec {
     static __device__ __forceinline__ void apply4(const float* acc4, const G&, i64, i64, i64, bafe::Vec4<float>& o4) {
         for (int e = 0; e < 4; ++e) o4.v[e] = acc4[e];
     }
-    template <class G>
-    static __device__ __forceinline__ void prefetch(const G&, i64, i64, i64, int) {}
 };
 
 __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1)
@@ -161,7 +159,7 @@ extern "C" __attribute__((visibility("default"))) int bafe_cuda_gemm_3xtf32_stat
     s.tc_pair = false;
     bafe_cuda::TcLaunch L;
     std::string err;
-    if (int rc = bafe_cuda::tc_prepare(s, A, B, a_lo, b_lo, out, {}, ds->sm_count, status, L, err))
+    if (int rc = bafe_cuda::tc_prepare(s, A, B, a_lo, b_lo, out, {}, ds->sm_count, status, nullptr, 0, L, err))
         return fail(rc, err);
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));

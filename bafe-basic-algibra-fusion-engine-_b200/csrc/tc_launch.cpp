@@ -21,6 +21,7 @@ struct alignas(64) TcArgsHost {
     CUtensorMap tmap_a_lo;
     CUtensorMap tmap_b_lo;
     CUtensorMap tmap_out;
+    CUtensorMap tmap_ws;
     void* out;
     int64_t M, N, K;
     int64_t o_bstride;
@@ -34,12 +35,21 @@ struct alignas(64) TcArgsHost {
     int32_t a_batched, b_batched;
     int32_t out_tma;
     int32_t ep_vec;
+    float* ws;
+    int32_t split, split_first, num_units;
 };
 static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
-static_assert(sizeof(TcArgsHost) == 832, "TcArgs layout");
+static_assert(sizeof(TcArgsHost) == 960, "TcArgs layout");
 static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the launch block");
 
 int threads_of(int) { return 320; }
+// k-blocks (one 128-byte row of K) per TMEM promotion chunk, as the kernels
+// have it: bf16 8; tf32 pair 8 (1x) / 2 (3x), single 4 / 2
+int chunk_kblocks(const Step& s) {
+    if (s.tc_elem == 1) return 8;
+    if (s.tc_variant == 3) return 2;
+    return s.tc_pair ? 8 : 4;
+}
 int stages_of(int variant, bool pair) { return pair ? (variant == 3 ? 3 : 6) : (variant == 3 ? 2 : 4); }
 int stage_bytes(int variant, bool pair) {
     return (BM * BK * 4 + (pair ? BN / 2 : BN) * BK * 4) * (variant == 3 ? 2 : 1);
@@ -59,9 +69,36 @@ int tc_smem_bytes(int variant, bool pair) {
     return 1024 + stages_of(variant, pair) * stage_bytes(variant, pair) + 1024 + 8 * 4096;
 }
 
+TcSplit tc_split_of(const Step& s, int sm_count) {
+    TcSplit sp;
+    if (s.tc_convert) return sp;                 // the conversion look-ahead assumes whole tiles
+    const char* e = getenv("BAFE_TC_SPLIT");
+    if (e && *e == '0') return sp;
+    const int64_t tile_m = s.tc_pair ? 2 * BM : BM;
+    const int64_t batch = s.batch > 1 ? s.batch : 1;
+    const int64_t tiles = (s.M + tile_m - 1) / tile_m * ((s.N + BN - 1) / BN) * batch;
+    const int64_t units = s.tc_pair ? sm_count / 2 : sm_count;
+    const int64_t rem = units > 0 ? tiles % units : 0;
+    if (rem == 0) return sp;
+    const int64_t kb = (s.K + (s.tc_elem == 1 ? 64 : 32) - 1) / (s.tc_elem == 1 ? 64 : 32);
+    const int64_t chunks = (kb + chunk_kblocks(s) - 1) / chunk_kblocks(s);
+    // up to 4 K ranges per tail tile, as many as the idle units take, each
+    // of at least 2 chunks and 32 k-blocks (shorter ones lose more to the
+    // extra partial store, fixup launch and pipeline fill than they save)
+    int64_t parts = units / rem;
+    if (parts > 4) parts = 4;
+    if (parts > chunks / 2) parts = chunks / 2;
+    while (parts >= 2 && kb / parts < 32) --parts;
+    if (parts < 2) return sp;
+    sp.parts = (int)parts;
+    sp.first = (int)(tiles - rem);
+    sp.ws_bytes = (size_t)rem * parts * tile_m * BN * 4;
+    return sp;
+}
+
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
-               const std::vector<const void*>& ep, int sm_count, unsigned* err_word, TcLaunch& L,
-               std::string& err) {
+               const std::vector<const void*>& ep, int sm_count, unsigned* err_word, void* ws, size_t ws_bytes,
+               TcLaunch& L, std::string& err) {
     const bool split = s.tc_variant == 3;
     const bool lo_maps = split && !s.tc_convert;     // residuals read from memory
     if (lo_maps && (!a_lo || !b_lo)) {
@@ -162,6 +199,25 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
         return 12;
     }
     h.num_tiles = (int)tiles;
+    // The last wave's tiles split along K when that fills idle CTAs (and
+    // the caller gave the workspace for their partials).
+    h.split = 1;
+    h.split_first = h.num_tiles;
+    L.fix_grid = 0;
+    const TcSplit sp = tc_split_of(s, sm_count);
+    if (sp.parts > 1 && ws && ws_bytes >= sp.ws_bytes && (uintptr_t)ws % 16 == 0) {
+        const uint64_t rows = sp.ws_bytes / (BN * 4);
+        uint64_t dims[3] = {(uint64_t)BN, rows, 1}, strides[2] = {(uint64_t)BN * 4, rows * BN * 4};
+        uint32_t box[3] = {32, 32, 1};
+        if (int rc = tc_encode_tensor_map(&h.tmap_ws, 1, 3, ws, dims, strides, box, 1, err)) return rc;
+        h.ws = (float*)ws;
+        h.split = sp.parts;
+        h.split_first = sp.first;
+        const int64_t groups = (int64_t)(h.num_tiles - sp.first) * (s.tc_pair ? 2 * BM : BM) * (BN / 4);
+        const int64_t fg = (groups + 255) / 256;
+        L.fix_grid = (unsigned)(fg < (int64_t)sm_count * 8 ? fg : (int64_t)sm_count * 8);
+    }
+    h.num_units = h.split_first + (h.num_tiles - h.split_first) * h.split;
     // Tiles are walked in groups of group_m M-tiles (all N-tiles of a group
     // before the next).  One wave of concurrent tiles then reads about
     // group_m A panels and waves/group_m B panels; their sum is smallest for
@@ -171,12 +227,13 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     const char* to = getenv("BAFE_TC_TIMEOUT_MS");
     h.timeout_ns = (unsigned long long)(to ? atof(to) : 2000.0) * 1000000ull;
     memcpy(L.args, &h, sizeof(h));
+    const int64_t work = h.num_units;
     if (s.tc_pair) {
         const int64_t pairs = sm_count / 2;
-        L.grid = (unsigned)(2 * (tiles < pairs ? tiles : pairs));
+        L.grid = (unsigned)(2 * (work < pairs ? work : pairs));
         L.cluster = 2;
     } else {
-        L.grid = (unsigned)(tiles < sm_count ? tiles : sm_count);
+        L.grid = (unsigned)(work < sm_count ? work : sm_count);
         L.cluster = 1;
     }
     L.block = (unsigned)threads_of(s.tc_variant);

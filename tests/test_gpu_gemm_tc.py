@@ -325,3 +325,68 @@ def test_epilogue_half_operands(cuda, pair):
     err = float((out.double() - ref).abs().max())
     print(f"half epilogue operands pair={pair}: max err {err:.3e}")
     assert err <= 1e-4 * math.sqrt(K / 64) * float(D.double().abs().max())
+
+
+# ------------------------------------------------------------ split tail --
+# When the last wave of tiles would leave CTAs idle, its tiles are split
+# into up to 4 ranges of K whose fp32 partials a fixup kernel adds (in
+# order) before the epilogue: one more launch.  Same bounds; the split
+# result differs from the unsplit one only by summation order.
+
+SPLIT_CASES = [
+    # (batch, M, N, K, prec, pair, elem): tiles = 74 (pairs) or 148 + a short tail
+    (1, 1790, 3068, 4096, "3xtf32", "1", 0),     # 7 x 12 = 84 pair tiles: 10 split 4 ways, ragged edges
+    (1, 1792, 3072, 4096, "tf32", "0", 0),       # 14 x 12 = 168 single-CTA tiles: 20 split 4 ways
+    (3, 512, 1536, 8192, "tf32", "1", 0),        # 3 x 2 x 6 = 36 batched pair tiles, all split 2 ways
+    (1, 1792, 3072, 8192, "bf16", "1", 1),       # bf16 operands
+]
+
+
+@pytest.mark.parametrize("batch,M,N,K,prec,pair,elem", SPLIT_CASES)
+def test_split_tail_tiles(cuda, monkeypatch, batch, M, N, K, prec, pair, elem):
+    torch = cuda
+    gen = torch.Generator(device="cuda").manual_seed(M + N + K)
+    dt = torch.bfloat16 if elem else torch.float32
+    shape_a, shape_b, shape_o = ((batch,) if batch > 1 else ()) + (M, K), ((batch,) if batch > 1 else ()) + (K, N), \
+        ((batch,) if batch > 1 else ()) + (M, N)
+    A = torch.randn(*shape_a, device="cuda", generator=gen).to(dt)
+    B = torch.randn(*shape_b, device="cuda", generator=gen).to(dt)
+    C = torch.randn(*shape_o, device="cuda", generator=gen)
+    D = torch.randn(*shape_o, device="cuda", generator=gen)
+    g = bafe.GraphBuilder()
+    a = g.add_input("A", shape_a, 5 if elem else 0, 0)
+    b = g.add_input("B", shape_b, 5 if elem else 0, 0)
+    c = g.add_input("C", shape_o, 0, 0)
+    d = g.add_input("D", shape_o, 0, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), g.add("mul", [c, d])])]))
+    bafe.set_option("gemm_precision", "auto" if elem else prec)
+    bafe.set_option("tc_pair", pair)
+    ins = [A.view(torch.int16), B.view(torch.int16), C, D] if elem else [A, B, C, D]
+    outs, launches = {}, {}
+    try:
+        for split in ("1", "0"):
+            monkeypatch.setenv("BAFE_TC_SPLIT", split)
+            k = bafe.compile_graph(g)
+            assert "gemm.tc" in k.describe()
+            # bf16 operands give a bf16 result (its bits in int16)
+            out = torch.zeros(shape_o, dtype=torch.int16, device="cuda") if elem else \
+                torch.full(shape_o, float("nan"), device="cuda")
+            n0 = bafe.launch_count()
+            k.run_torch(ins, out)
+            bafe.synchronize()
+            launches[split] = bafe.launch_count() - n0
+            # a new output each time: the launch is prepared anew
+            outs[split] = ((out.to(torch.int32) & 0xFFFF) << 16).view(torch.float32) if elem else out
+    finally:
+        bafe.set_option("tc_pair", "1")
+        bafe.set_option("gemm_precision", "auto")
+    assert launches["1"] == launches["0"] + 1, launches        # the fixup kernel ran
+    ref = torch.relu(torch.matmul(A.double(), B.double()) + C.double() * D.double())
+    tol = (1e-4 if prec == "3xtf32" else TF32_TOL) * math.sqrt(K / 64)
+    if elem:                                  # one bf16 ulp of the value + the f32 summation error
+        tol = torch.exp2(torch.floor(torch.log2(ref.abs().clamp_min(1e-30))) - 7) + 1e-4 * math.sqrt(K / 64)
+    for split, out in outs.items():
+        err = (out.double() - ref).abs()
+        print(f"split={split} {prec} pair={pair} {batch}x{M}x{N}x{K}: max err {float(err.max()):.3e}")
+        assert bool((err <= tol).all())
+    assert bool(((outs["1"].double() - outs["0"].double()).abs() <= 2 * tol).all())
