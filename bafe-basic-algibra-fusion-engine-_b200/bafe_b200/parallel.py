@@ -5,7 +5,9 @@
   operand and of the output, and runs the plan of its panel graph on its own
   device.  B is needed whole on every rank: it is broadcast once from the
   root over NCCL and stays resident.  Row-vector operands (bias) are small
-  and replicated.  The output stays sharded; `gather_rows` all-gathers it
+  and replicated.  From host memory (`run_host_shared`), each rank copies
+  only its slab of B over its own host link and an all-gather over NVLink
+  completes B on every rank.  The output stays sharded; `gather_rows` all-gathers it
   when a single copy is needed.
 * Elementwise graphs shard by contiguous element ranges with no collective
   (range starts are multiples of 4 elements so every shard keeps 16-byte
@@ -67,6 +69,58 @@ def gather_rows(panel, full_rows: int, dist, panels: Sequence[Tuple[int, int]]):
     parts = [torch.empty_like(padded) for _ in panels]
     dist.all_gather(parts, padded)
     return torch.cat([p[: b - a] for p, (a, b) in zip(parts, panels)], dim=0)[:full_rows]
+
+
+class SharedInput:
+    """An input every rank reads whole (a row-sharded GEMM's B), assembled on
+    each rank's device from host memory: rank r copies only its 1/world byte
+    slab over its own host link, then one in-place all-gather over NCCL
+    (NVLink) completes the buffer on every rank -- instead of every rank
+    copying the whole input over PCIe.  The device buffer is kept for the
+    next call of the same size."""
+
+    def __init__(self, dist=None, device=None):
+        self.dist = dist
+        self.device = device
+        self.buf = None                    # uint8, world x slab bytes
+
+    def _world(self):
+        d = self.dist
+        if d is not None and d.is_initialized():
+            return d.get_world_size(), d.get_rank()
+        return 1, 0
+
+    def assemble(self, host):
+        """Device copy of the host tensor `host` (same dtype and shape)."""
+        import torch
+        world, rank = self._world()
+        flat = host.contiguous().view(-1).view(torch.uint8)
+        n = flat.numel()
+        slab = (n + world - 1) // world
+        slab = (slab + 15) // 16 * 16                    # 16-byte aligned slabs
+        dev = self.device if self.device is not None else torch.device("cuda", torch.cuda.current_device())
+        if self.buf is None or self.buf.numel() != world * slab or self.buf.device != torch.device(dev):
+            self.buf = torch.empty(world * slab, dtype=torch.uint8, device=dev)
+        lo, hi = min(rank * slab, n), min((rank + 1) * slab, n)
+        mine = self.buf[rank * slab:(rank + 1) * slab]
+        if hi > lo:
+            mine[: hi - lo].copy_(flat[lo:hi], non_blocking=True)
+        if world > 1:
+            self.dist.all_gather_into_tensor(self.buf, mine)
+        return self.buf[:n].view(host.dtype).view(host.shape)
+
+
+def run_host_shared(kernel, host_inputs: Sequence, host_out, shared: dict) -> None:
+    """One host-pointer call of `kernel` (bafe_cuda_run_host_resident) where
+    the inputs at the indices of `shared` (index -> SharedInput) are
+    assembled on the device first (slab copy + all-gather); the other
+    inputs and the output are host tensors, row-streamed as in a plain
+    host call.  Synchronous."""
+    import torch
+    dev_inputs = {k: sh.assemble(host_inputs[k]) for k, sh in shared.items()}
+    torch.cuda.current_stream().synchronize()            # the plan's streams read them next
+    ptrs = [(dev_inputs[k] if k in dev_inputs else t).data_ptr() for k, t in enumerate(host_inputs)]
+    kernel.call_host_resident(ptrs + [host_out.data_ptr()], [k in dev_inputs for k in range(len(host_inputs))])
 
 
 class RowPanelGemm:

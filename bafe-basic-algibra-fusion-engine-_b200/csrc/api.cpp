@@ -25,7 +25,7 @@ Options& options() {
         if (const char* d = getenv("BAFE_DEVICE")) o.device = atoi(d);
         if (const char* t = getenv("BAFE_TC_PAIR")) o.tc_pair = atoi(t) != 0;
         if (const char* h = getenv("BAFE_HOST_PANELS")) o.host_panels = strcmp(h, "auto") == 0 ? -1 : atoi(h);
-        if (const char* c = getenv("BAFE_TC_CONVERT")) o.tc_convert = atoi(c) != 0;
+        if (const char* c = getenv("BAFE_TC_CONVERT")) o.tc_convert = strcmp(c, "auto") == 0 ? -1 : (atoi(c) != 0);
     }
     return o;
 }
@@ -143,7 +143,7 @@ BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* 
     }
     const Options& opt = options();
     std::string key = std::string(hash) + "|prec=" + opt.gemm_precision + (opt.tc_pair ? "|pair" : "|single") +
-                      (opt.tc_convert ? "|conv" : "");
+                      "|conv=" + std::to_string(opt.tc_convert);
     auto it = g_by_key.find(key);
     if (it != g_by_key.end() && plan_ptr(it->second)) {
         int slot = slot_of_plan(it->second);
@@ -303,6 +303,13 @@ BAFE_API int bafe_cuda_run_host(int plan, void* const* ptrs, int n_ptrs) {
     return run_plan_host(*p, ptrs, n_ptrs);
 }
 
+BAFE_API int bafe_cuda_run_host_resident(int plan, void* const* ptrs, int n_ptrs, const unsigned char* resident) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
+    return run_plan_host(*p, ptrs, n_ptrs, resident);
+}
+
 BAFE_API int bafe_cuda_last_error(char* buf, size_t buf_size) {
     std::string msg;
     int code = get_error(msg);
@@ -328,8 +335,8 @@ BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
         return 0;
     }
     if (k == "tc_convert") {
-        if (v != "0" && v != "1") return -1;
-        o.tc_convert = v == "1";
+        if (v != "auto" && v != "0" && v != "1") return -1;
+        o.tc_convert = v == "auto" ? -1 : (v == "1");
         return 0;
     }
     if (k == "host_panels") {
@@ -358,7 +365,7 @@ BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
     if (k == "gemm_precision") v = o.gemm_precision;
     else if (k == "device") v = std::to_string(o.device);
     else if (k == "tc_pair") v = o.tc_pair ? "1" : "0";
-    else if (k == "tc_convert") v = o.tc_convert ? "1" : "0";
+    else if (k == "tc_convert") v = o.tc_convert < 0 ? "auto" : (o.tc_convert ? "1" : "0");
     else if (k == "host_panels") v = o.host_panels < 0 ? "auto" : std::to_string(o.host_panels);
     else return -1;
     if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());

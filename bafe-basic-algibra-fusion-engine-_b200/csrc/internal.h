@@ -78,7 +78,7 @@ struct Options {
     int device = -1;                        // -1: current device
     bool tc_pair = true;                    // tensor-core GEMM on CTA pairs (cta_group::2)
     int host_panels = -1;                   // host calls: -1 auto, 0/1 off, n: n row panels
-    bool tc_convert = false;                // 3xTF32: make the tf32 residuals inside the kernel
+    int tc_convert = -1;                    // 3xTF32 residuals inside the kernel: 1 yes, 0 no, -1 auto (small GEMMs)
 };
 Options& options();
 
@@ -179,7 +179,8 @@ std::string sha256_hex(const void* data, size_t len);
 
 // Runtime (runtime.cpp).
 int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
-int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs);
+// resident: per input, nonzero = ptrs[k] is already a device buffer (or null: none)
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident = nullptr);
 // Synchronises the current device and reports a kernel-raised error word.
 int synchronize_current_device();
 void release_plan_device_state(Plan& p);

@@ -550,7 +550,11 @@ struct Lowerer {
                 // 3xTF32 residuals: a pre-pass into plan scratch (default), or
                 // made in shared memory by the kernel (tc_convert: no scratch,
                 // half the operand traffic, more shared-memory traffic)
-                s.tc_convert = s.tc_variant == 3 && opt.tc_convert;
+                // auto: in the kernel below 2 x 256^3 multiply-adds, where the
+                // two pre-pass launches cost more than the conversion (measured
+                // on B200: 256^3 24.6 -> 20.5 us; even at 512^3, slower above)
+                const bool small = (double)M * (double)Nn * (double)K * (double)batch < 2.0 * 16777216.0;
+                s.tc_convert = s.tc_variant == 3 && (opt.tc_convert > 0 || (opt.tc_convert < 0 && small));
                 s.tc_pair = opt.tc_pair;
             }
         }

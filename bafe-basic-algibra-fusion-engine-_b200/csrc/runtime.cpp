@@ -742,7 +742,7 @@ int copy_async(void* dst, const void* src, int64_t bytes, cudaStream_t st, const
 // each panel's output rows after its steps.  All copies of one direction
 // are issued before the other's, so with pageable host memory (whose copies
 // the driver makes synchronous) the input copies still overlap the kernels.
-int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels) {
+int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels, const unsigned char* resident) {
     const int64_t R = p.stream_rows, align = p.stream_align;
     int64_t rows_per = (R + panels - 1) / panels;
     rows_per = (rows_per + align - 1) / align * align;
@@ -768,7 +768,10 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
     cudaEvent_t whole = ds->events[0];
     auto in_done = [&](int i) { return ds->events[1 + 2 * i]; };
     auto run_done = [&](int i) { return ds->events[2 + 2 * i]; };
+    auto here = [&](int k) { return resident && resident[k]; };   // input already on the device
     std::vector<void*> dptrs(ds->in_stage);
+    for (int k = 0; k < p.n_inputs; ++k)
+        if (here(k)) dptrs[k] = ptrs[k];
     dptrs.push_back(ds->out_stage);
     int rc = 0;
     auto fail = [&](int code) {
@@ -781,7 +784,8 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
 
     // inputs every panel reads whole
     for (int k = 0; k < p.n_inputs && !rc; ++k)
-        if (p.in_rb[k] == 0) rc = copy_async(ds->in_stage[k], ptrs[k], p.in_bytes[k], ds->h2d, "host-to-device copy");
+        if (p.in_rb[k] == 0 && !here(k))
+            rc = copy_async(ds->in_stage[k], ptrs[k], p.in_bytes[k], ds->h2d, "host-to-device copy");
     if (rc) return fail(rc);
     cudaEventRecord(whole, ds->h2d);
     cudaStreamWaitEvent(ds->stream, whole, 0);
@@ -793,7 +797,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
         const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
         for (int k = 0; k < p.n_inputs && !rc; ++k) {
             const int64_t b = p.in_rb[k];
-            if (b == 0) continue;
+            if (b == 0 || here(k)) continue;
             rc = copy_async(static_cast<char*>(ds->in_stage[k]) + r0 * b, static_cast<const char*>(ptrs[k]) + r0 * b,
                             rows * b, ds->h2d, "host-to-device copy");
         }
@@ -822,7 +826,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
 
 }  // namespace
 
-int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident) {
     if (n_ptrs != p.n_inputs + 1) {
         set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
         return 8;
@@ -857,13 +861,15 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs) {
     }
     if (int rc = ensure_tmps(p, ds)) return rc;
     const int panels = host_panel_count(p);
-    if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels);
+    if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels, resident);
     for (int k = 0; k < p.n_inputs; ++k) {
-        if (p.in_bytes[k] == 0) continue;
+        if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
         cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], ptrs[k], (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
         if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e)); return 7; }
     }
     std::vector<void*> dptrs(ds->in_stage);
+    for (int k = 0; k < p.n_inputs; ++k)
+        if (resident && resident[k]) dptrs[k] = ptrs[k];
     dptrs.push_back(ds->out_stage);
     if (int rc = ensure_timing_events(ds, 2)) return rc;
     cudaEventRecord(ds->tev[0], ds->stream);

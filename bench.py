@@ -202,6 +202,19 @@ def time_e2e(torch, kernel, host_ins, host_out, steps):
     return (time.perf_counter() - t0) / steps * 1e3
 
 
+def time_e2e_shared(torch, kernel, host_ins, host_out, shared, steps):
+    """Host-pointer calls whose `shared` inputs each rank assembles on its
+    device from its own slab plus an NCCL all-gather (parallel.run_host_shared),
+    every copy and collective inside the timed region."""
+    from bafe_b200.parallel import run_host_shared
+    run_host_shared(kernel, host_ins, host_out, shared)   # warm: buffers, module
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run_host_shared(kernel, host_ins, host_out, shared)
+    return (time.perf_counter() - t0) / steps * 1e3
+
+
 def reduce_max(torch, dist, x: float, dev) -> float:
     if dist is None:
         return x
@@ -406,11 +419,21 @@ def bench_gemm(c: Ctx) -> dict:
         hA, hB, hC = A.cpu().pin_memory(), B.cpu().pin_memory(), C.cpu().pin_memory()
         hO = torch.empty(rows, S).pin_memory()
         c.barrier()
-        e2e_ms = c.max(time_e2e(torch, k, [hA, hB, hC], hO, args.e2e_steps))
+        if c.world > 1:
+            # B: each rank copies its 1/N slab from the host, NCCL all-gathers it
+            from bafe_b200.parallel import SharedInput
+            e2e_ms = c.max(time_e2e_shared(torch, k, [hA, hB, hC], hO, {1: SharedInput(c.dist, c.dev)},
+                                           args.e2e_steps))
+            h2d = float(4 * (A.numel() + C.numel())) * c.world + float(4 * B.numel())
+            path = ("bafe_cuda_run_host_resident (A, C, output: pinned host buffers, row-streamed; "
+                    "B: 1/N slab per rank from pinned host memory + NCCL all-gather)")
+        else:
+            e2e_ms = c.max(time_e2e(torch, k, [hA, hB, hC], hO, args.e2e_steps))
+            h2d = float(4 * (A.numel() + B.numel() + C.numel()))
+            path = "bafe_cuda_jit_get_or_compile host function, pinned host buffers"
         res["e2e"] = {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-                      "h2d_bytes_per_step": float(4 * (A.numel() + B.numel() + C.numel())) * c.world,
-                      "d2h_bytes_per_step": float(4 * out.numel()) * c.world, "ms_per_step": round(e2e_ms, 2),
-                      "path": "bafe_cuda_jit_get_or_compile host function, pinned host buffers"}
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": float(4 * out.numel()) * c.world,
+                      "ms_per_step": round(e2e_ms, 2), "path": path}
         if c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
             res["cpu_baseline"] = cpu_baseline_gemm(hA[:8].numpy(), hB.numpy(), hC[:8].numpy())
         del hA, hB, hC, hO

@@ -239,6 +239,16 @@ int bafe_cuda_run_device(int plan, void *const *ptrs, int n_ptrs, void *stream);
  * Returns 0 or a nonzero code. */
 int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);
 
+/* bafe_cuda_run_host where some inputs are already on the plan's device:
+ * resident[k] != 0 makes ptrs[k] (k < n_inputs) a device buffer of the
+ * input, read in place instead of copied from the host; the other inputs
+ * and the output are host pointers as in bafe_cuda_run_host (row-streamed
+ * the same way).  Synchronous.  Used by multi-GPU callers that assemble an
+ * input every rank reads whole (a GEMM's B) over NVLink instead of copying
+ * it from the host on every rank.  Extension: the reference has no device
+ * memory.  Returns 0 or a nonzero code. */
+int bafe_cuda_run_host_resident(int plan, void *const *ptrs, int n_ptrs, const unsigned char *resident);
+
 /* Waits for all work on the current device and reports an error a kernel
  * raised asynchronously (a pipeline wait that exceeded its deadline; the
  * outputs of that launch are then invalid).  Returns 0 or a nonzero code
@@ -259,10 +269,13 @@ void bafe_cuda_clear_error(void);
  *   "tc_pair":        "1" (default): tensor-core GEMMs run on CTA pairs
  *                     (256x256 tiles over two SMs); "0": one CTA per tile
  *                     (read when a plan is built)
- *   "tc_convert":     "0" (default): 3xTF32 residuals come from a pre-pass
- *                     into plan scratch; "1": the GEMM kernel makes them in
- *                     shared memory (no scratch, half the operand traffic,
- *                     lower throughput on B200) (read when a plan is built)
+ *   "tc_convert":     "auto" (default) | "0" | "1": "0": 3xTF32 residuals
+ *                     come from a pre-pass into plan scratch; "1": the GEMM
+ *                     kernel makes them in shared memory (no scratch, half
+ *                     the operand traffic, lower throughput on B200 at
+ *                     large sizes); auto = "1" below 2 x 256^3
+ *                     multiply-adds (one launch instead of three), else "0"
+ *                     (read when a plan is built)
  *   "host_panels":    "auto" (default) | "0" | n: host-pointer calls of a
  *                     row-separable plan copy, compute and copy back in n
  *                     row panels on three streams, overlapping the copies

@@ -224,7 +224,7 @@ def test_3xtf32_in_kernel_residuals(cuda, shape, a_col, b_col, pair):
     try:
         k, out, err = _run(cuda, M, N, K, a_col, b_col, "relu_add_c", "3xtf32", seed=11)
     finally:
-        bafe.set_option("tc_convert", "0")
+        bafe.set_option("tc_convert", "auto")
         bafe.set_option("tc_pair", "1")
     steps = k.describe().strip().splitlines()
     assert len(steps) == 1 and steps[0].startswith("gemm.tc.3xtf32"), steps

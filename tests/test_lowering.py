@@ -149,10 +149,17 @@ def test_tc_convert_option_drops_the_residual_pre_pass():
     bafe.set_option("gemm_precision", "3xtf32")
     default = bafe.compile_graph(g).describe().strip().splitlines()
     assert [l.split()[0] for l in default][:2] == ["ew", "ew"] and default[2].startswith("gemm.tc.3xtf32")
-    assert bafe.get_option("tc_convert") == "0"
+    assert bafe.get_option("tc_convert") == "auto"
     bafe.set_option("tc_convert", "1")
     try:
         conv = bafe.compile_graph(g).describe().strip().splitlines()
+        bafe.set_option("tc_convert", "auto")
+        g2 = GraphBuilder()                  # 256^3: auto makes the residuals in the kernel
+        a2 = g2.add_input("A", (256, 256), 0, 0)
+        b2 = g2.add_input("B", (256, 256), 0, 0)
+        g2.set_output(g2.add("matmul", [a2, b2]))
+        small = bafe.compile_graph(g2).describe().strip().splitlines()
     finally:
-        bafe.set_option("tc_convert", "0")
+        bafe.set_option("tc_convert", "auto")
     assert len(conv) == 1 and conv[0].startswith("gemm.tc.3xtf32")
+    assert len(small) == 1 and small[0].startswith("gemm.tc.3xtf32")

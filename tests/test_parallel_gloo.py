@@ -168,3 +168,50 @@ def test_broadcast_of_raw_half_buffers():
     while not q.empty():
         out.append(q.get())
     assert out == [("ok", True), ("ok", True)], out
+
+
+def _shared_worker(rank, world, port, q):
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from bafe_b200.parallel import SharedInput
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        sh = SharedInput(dist, device="cpu")
+        ok = True
+        for shape, dtype in [((37, 53), torch.float32), ((1001,), torch.int16), ((3, 5, 7), torch.float64)]:
+            host = (torch.arange(int(np.prod(shape))) * 7 - 11).to(dtype).reshape(shape)
+            got = sh.assemble(host)
+            ok = ok and got.dtype == host.dtype and got.shape == host.shape and bool(torch.equal(got, host))
+        q.put(("ok", ok))
+    except Exception as e:
+        q.put(("error", f"rank {rank}: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_shared_input_assembled_from_slabs(world):
+    """Each rank copies its byte slab of the host buffer; the all-gather
+    completes it on every rank (odd sizes: the last slab is short)."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_shared_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    assert out == [("ok", True)] * world, out

@@ -151,3 +151,31 @@ def test_auto_streaming_on_pinned_buffers(cuda):
     k.call_host_ptrs([t.data_ptr() for t in (X, Y, Z)] + [out.data_ptr()])
     want = torch.relu(X * Y + Z)     # three separately rounded fp32 ops, relu(-0) = 0
     assert torch.equal(out, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("panels", ["0", "4"])
+def test_host_call_with_a_resident_input(cuda, panels):
+    """bafe_cuda_run_host_resident: B already on the device (a multi-GPU
+    caller assembles it over NVLink), A, C and the output on the host;
+    bit-identical to the plain host call and the oracle, streamed or in one
+    piece."""
+    torch = cuda
+    bafe.set_option("gemm_precision", "exact")
+    M, K, N = 1000, 96, 40
+    gen = torch.Generator().manual_seed(10)
+    A, B, C = (torch.randn(*s, generator=gen) for s in ((M, K), (K, N), (M, N)))
+    k, g = _kernel(_gemm_relu_add, ("A", (M, K), 0, 0), ("B", (K, N), 0, 0), ("C", (M, N), 0, 0))
+    bafe.set_option("host_panels", panels)
+    try:
+        want = torch.zeros(M, N)
+        k.call_host_ptrs([A.data_ptr(), B.data_ptr(), C.data_ptr(), want.data_ptr()])
+        Bd = B.cuda()
+        torch.cuda.synchronize()
+        got = torch.zeros(M, N)
+        k.call_host_resident([A.data_ptr(), Bd.data_ptr(), C.data_ptr(), got.data_ptr()], [False, True, False])
+    finally:
+        bafe.set_option("host_panels", "auto")
+    assert torch.equal(got, want)
+    ref = oracle.evaluate(g.to_list(), dict(zip(g.inputs, (A.numpy(), B.numpy(), C.numpy()))), g.output)
+    assert got.numpy().tobytes() == ref.reshape(M, N).tobytes()
