@@ -62,21 +62,30 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
         // outside the matrices are zero on BOTH sides, so padded products
         // are +0 and leave every partial sum unchanged (an accumulator that
         // starts at +0 never holds -0, and x + +0 == x for every other x).
+        // All 16 loads first, branch-free (an element outside the matrix
+        // reads the matrix's first element and is replaced by zero), so they
+        // are in flight together; guarded loads each waited for the last.
+        TA av[8];
+        TB bv[8];
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
             const int e = tid + 256 * t;
-            int mm, kk;
-            if (g.a_col) { mm = e & 63; kk = e >> 6; } else { kk = e & 31; mm = e >> 5; }
+            const int mm = g.a_col ? (e & 63) : (e >> 5), kk = g.a_col ? (e >> 6) : (e & 31);
             const i64 gm = m0 + mm, gk = k0 + kk;
-            TA val = (TA)0;
-            if (gm < M && gk < K) val = Spec::loadA(g.a, aoff + (g.a_col ? gm + M * gk : gm * K + gk));
-            As[kk][mm] = val;
-            int nn, kb;
-            if (g.b_col) { kb = e & 31; nn = e >> 5; } else { nn = e & 63; kb = e >> 6; }
+            const bool ina = gm < M && gk < K;
+            av[t] = Spec::loadA(g.a, aoff + (ina ? (g.a_col ? gm + M * gk : gm * K + gk) : 0));
+            if (!ina) av[t] = (TA)0;
+            const int nn = g.b_col ? (e >> 5) : (e & 63), kb = g.b_col ? (e & 31) : (e >> 6);
             const i64 gn = n0 + nn, gkb = k0 + kb;
-            TB bv = (TB)0;
-            if (gn < N && gkb < K) bv = Spec::loadB(g.b, boff + (g.b_col ? K * gn + gkb : gkb * N + gn));
-            Bs[kb][nn] = bv;
+            const bool inb = gn < N && gkb < K;
+            bv[t] = Spec::loadB(g.b, boff + (inb ? (g.b_col ? K * gn + gkb : gkb * N + gn) : 0));
+            if (!inb) bv[t] = (TB)0;
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int e = tid + 256 * t;
+            As[g.a_col ? (e >> 6) : (e & 31)][g.a_col ? (e & 63) : (e >> 5)] = av[t];
+            Bs[g.b_col ? (e & 31) : (e >> 6)][g.b_col ? (e >> 5) : (e & 63)] = bv[t];
         }
         __syncthreads();
 #pragma unroll 4
@@ -101,7 +110,22 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
                 for (int c = 0; c < 4; ++c) { v[r][c] = add(v[r][c], acc[r][c]); acc[r][c] = (T)0; }
         }
     }
-    typename Spec::Out* out = reinterpret_cast<typename Spec::Out*>(g.out) + bz * g.o_bstride;
+    // Epilogue in two passes: every apply (operand loads only), then every
+    // store -- an operand load cannot move above a store to `out` that may
+    // alias it, so interleaved the 16 outputs' loads ran one after another
+    // (a 64^3 relu(matmul + C) took 16 us, nearly all of it there).
+    typedef typename Spec::Out Out;
+    Out* out = reinterpret_cast<Out*>(g.out) + bz * g.o_bstride;
+    Out res[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+        const i64 i = m0 + ty + 16 * r;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            const i64 j = n0 + tx + 16 * c;
+            if (i < M && j < N) res[r][c] = Spec::apply(DIRECT ? acc[r][c] : v[r][c], g, bz, i, j);
+        }
+    }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
         const i64 i = m0 + ty + 16 * r;
@@ -109,8 +133,7 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             const i64 j = n0 + tx + 16 * c;
-            if (j >= N) continue;
-            out[i * N + j] = Spec::apply(DIRECT ? acc[r][c] : v[r][c], g, bz, i, j);
+            if (j < N) out[i * N + j] = res[r][c];
         }
     }
 }

@@ -117,6 +117,11 @@ template <int VARIANT> struct TcPairCfg;
 template <> struct TcPairCfg<1> {
     static constexpr int STAGES = 6, THREADS = 320, KB_PER_CHUNK = 8;
 };
+// 3xTF32 pair: 64-deep chunks.  The MMA issuer then waits on a TMEM
+// buffer still being drained ~27 % of its time, and 96-deep chunks remove
+// most of that (+11.7 % per clock, within the error bound) -- but under the
+// 1 kW power cap the denser MMA stream drew the clock from 1.49 to 1.19 GHz
+// on real data (same box, A/B): -11 % net, so the 64-deep form stays.
 template <> struct TcPairCfg<3> {
     static constexpr int STAGES = 3, THREADS = 320, KB_PER_CHUNK = 2;
 };
