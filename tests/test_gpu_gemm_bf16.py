@@ -46,6 +46,7 @@ def _graph(shape_a, shape_b, a_col, b_col, epi):
     ((304, 260, 520), 0, 1, "relu_add_c"),      # 520-byte rows: plain stores, no TMA
     ((1024, 2048, 1024), 0, 0, "relu_add_c"),
     ((3, 256, 512, 128), 0, 0, "relu_add_c"),
+    ((512, 512, 16384), 0, 0, "relu_add_c"),     # several TMEM promotion chunks
 ])
 @pytest.mark.parametrize("pair", ["1", "0"])
 def test_bf16_tensor_core_gemm_within_one_ulp(cuda, shape, a_col, b_col, epi, pair):
