@@ -114,8 +114,10 @@ template <> struct TcCfg<3> {      // 3xTF32
 // half (128 columns) of B per k-block, so a stage is a third smaller and
 // the ring deeper.
 template <int VARIANT> struct TcPairCfg;
+// 1xTF32 pair: 1024-deep chunks (its error is the operands' tf32
+// rounding; promoting every 256 k cost 5 % under the power cap).
 template <> struct TcPairCfg<1> {
-    static constexpr int STAGES = 6, THREADS = 320, KB_PER_CHUNK = 8;
+    static constexpr int STAGES = 6, THREADS = 320, KB_PER_CHUNK = 32;
 };
 // 3xTF32 pair: 64-deep chunks.  The MMA issuer then waits on a TMEM
 // buffer still being drained ~27 % of its time, and 96-deep chunks remove

@@ -279,9 +279,9 @@ void bafe_cuda_clear_error(void);
  *   "host_panels":    "auto" (default) | "0" | n: host-pointer calls of a
  *                     row-separable plan copy, compute and copy back in n
  *                     row panels on three streams, overlapping the copies
- *                     with the kernels; auto = 8 panels when the row-split
- *                     bytes exceed 64 MiB; 0 or 1 = one piece (read at
- *                     each call)
+ *                     with the kernels; auto = one panel per 96 MiB of
+ *                     row-split bytes, 8 to 32, once they exceed 64 MiB;
+ *                     0 or 1 = one piece (read at each call)
  *   "device":         CUDA device ordinal used by host-pointer calls
  *                     (default: the current device)
  * Environment variables BAFE_GEMM_PRECISION, BAFE_TC_PAIR, BAFE_TC_CONVERT,
