@@ -79,8 +79,9 @@ struct TcArgs {
     int split;                     // K ranges per tail tile (1: no split)
     int split_first;               // first split tile: tiles [split_first, num_tiles) are split
     int num_units;                 // split_first + (num_tiles - split_first) * split
+    unsigned* wave_ctr;            // wave alignment counter (zero at launch), or null
 };
-static_assert(sizeof(TcArgs) == 960, "TcArgs layout (mirrored by the host)");
+static_assert(sizeof(TcArgs) == 1024, "TcArgs layout (mirrored by the host)");
 
 // Work units of the persistent kernels.  Tiles [0, split_first) are whole
 // units; when the last wave would leave CTAs idle, each tile from
@@ -981,6 +982,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             u32 armed[STAGES];
             for (int i = 0; i < STAGES; ++i) armed[i] = 0xFFFFFFFFu;
             bool ok = true;
+            bool align_on = true;
             for (int u = pair; ok && u < g.num_units; u += num_pairs) {
                 int t, c0, c1, part;
                 unit_range(g, u, n_chunks, t, c0, c1, part);
@@ -989,6 +991,25 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
                 const int kb_stop = c1 * KB_PER_CHUNK < k_blocks ? c1 * KB_PER_CHUNK : k_blocks;
                 const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
+                // Wave alignment (advisory): the leader's producer starts the
+                // loads of wave w once every pair has issued all of wave
+                // w-1's, so the pairs of a wave walk K together and share the
+                // operand panels' slices in L2 instead of re-reading them
+                // from HBM as they drift apart.  The wait is bounded; when it
+                // runs out this CTA stops aligning (results do not depend on
+                // it).
+                const bool aligned = g.wave_ctr && cta == 0 && u < g.split_first;
+                if (aligned && align_on && u >= num_pairs) {
+                    const unsigned need = (unsigned)(u - pair);   // pairs x waves before this one
+                    const u64 t0 = now_ns();
+                    for (;;) {
+                        unsigned v;
+                        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(g.wave_ctr) : "memory");
+                        if (v >= need) break;
+                        if (now_ns() - t0 > 2000000ull) { align_on = false; break; }
+                        __nanosleep(256);
+                    }
+                }
                 // With converted residuals each CTA's copies complete on its
                 // own FULL barrier (its converting threads wait there);
                 // otherwise on the leader's, which the MMA issuer waits on.
@@ -1033,6 +1054,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     }
                     if (++s == STAGES) { s = 0; phase ^= 1u; }
                 }
+                if (aligned && ok) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(g.wave_ctr) : "memory");
             }
             // Drain (bounded): wait for the copies on this CTA's armed FULL
             // phases (the leader's count both CTAs' copies unless converting).

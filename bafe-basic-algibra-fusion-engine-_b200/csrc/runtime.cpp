@@ -285,6 +285,9 @@ struct DeviceState {
     // split step of the plan runs on `stream`, one after another).
     void* tc_ws = nullptr;
     size_t tc_ws_bytes = 0;
+    // Wave-alignment counter of the tensor-core GEMMs (zeroed before each
+    // launch that uses it; the plan's GEMMs run one after another).
+    unsigned* tc_ctr = nullptr;
 };
 
 // Timing events (pairs: before / after kernels) of a host call.
@@ -551,6 +554,11 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                         cudaGetLastError();
                     }
                 }
+                if (!ds->tc_ctr) {
+                    void* c = nullptr;
+                    if (cudaMalloc(&c, sizeof(unsigned)) == cudaSuccess) ds->tc_ctr = static_cast<unsigned*>(c);
+                    else cudaGetLastError();                    // no alignment then
+                }
                 const void* key[15] = {a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, err_word};
                 for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
                 key[14] = ds->tc_ws;
@@ -558,7 +566,7 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 for (int k = 0; hit && k < 15; ++k) hit = cached.key[k] == key[k];
                 if (!hit) {
                     int rc = tc_prepare(run, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word,
-                                        ds->fn_vec[si] ? ds->tc_ws : nullptr, ds->tc_ws_bytes, cached.L, err);
+                                        ds->fn_vec[si] ? ds->tc_ws : nullptr, ds->tc_ws_bytes, ds->tc_ctr, cached.L, err);
                     if (rc) {
                         cached.valid = false;
                         set_error(rc, err);
@@ -569,6 +577,10 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                     cached.valid = true;
                 }
                 TcLaunch& L = cached.L;
+                if (L.wave_sync) {
+                    cudaError_t e = cudaMemsetAsync(ds->tc_ctr, 0, sizeof(unsigned), stream);
+                    if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e)); return 7; }
+                }
                 void* params[] = {L.args};
                 CUlaunchConfig cfg;
                 memset(&cfg, 0, sizeof(cfg));
@@ -947,6 +959,7 @@ void release_plan_device_state(Plan& p) {
         for (void* t : s->in_stage) if (t) cudaFree(t);
         if (s->out_stage) cudaFree(s->out_stage);
         if (s->tc_ws) cudaFree(s->tc_ws);
+        if (s->tc_ctr) cudaFree(s->tc_ctr);
         for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
         for (cudaEvent_t ev : s->events) cudaEventDestroy(ev);
         for (cudaEvent_t ev : s->tev) cudaEventDestroy(ev);

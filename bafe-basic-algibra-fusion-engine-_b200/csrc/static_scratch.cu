@@ -159,7 +159,7 @@ extern "C" __attribute__((visibility("default"))) int bafe_cuda_gemm_3xtf32_stat
     s.tc_pair = false;
     bafe_cuda::TcLaunch L;
     std::string err;
-    if (int rc = bafe_cuda::tc_prepare(s, A, B, a_lo, b_lo, out, {}, ds->sm_count, status, nullptr, 0, L, err))
+    if (int rc = bafe_cuda::tc_prepare(s, A, B, a_lo, b_lo, out, {}, ds->sm_count, status, nullptr, 0, nullptr, L, err))
         return fail(rc, err);
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));

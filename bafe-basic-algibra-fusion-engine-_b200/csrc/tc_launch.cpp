@@ -37,9 +37,10 @@ struct alignas(64) TcArgsHost {
     int32_t ep_vec;
     float* ws;
     int32_t split, split_first, num_units;
+    unsigned* wave_ctr;
 };
 static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
-static_assert(sizeof(TcArgsHost) == 960, "TcArgs layout");
+static_assert(sizeof(TcArgsHost) == 1024, "TcArgs layout");
 static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the launch block");
 
 int threads_of(int) { return 320; }
@@ -98,7 +99,7 @@ TcSplit tc_split_of(const Step& s, int sm_count) {
 
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, void* ws, size_t ws_bytes,
-               TcLaunch& L, std::string& err) {
+               unsigned* wave_ctr, TcLaunch& L, std::string& err) {
     const bool split = s.tc_variant == 3;
     const bool lo_maps = split && !s.tc_convert;     // residuals read from memory
     if (lo_maps && (!a_lo || !b_lo)) {
@@ -218,6 +219,20 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
         L.fix_grid = (unsigned)(fg < (int64_t)sm_count * 8 ? fg : (int64_t)sm_count * 8);
     }
     h.num_units = h.split_first + (h.num_tiles - h.split_first) * h.split;
+    // Wave alignment of the pair kernel's producers (advisory, bounded):
+    // for GEMMs of at least two whole waves of long tiles, where pairs that
+    // drift apart along K re-read shared operand panels from HBM.
+    L.wave_sync = false;
+    {
+        const char* ws_env = getenv("BAFE_TC_WAVE_SYNC");
+        const int64_t pairs = sm_count / 2;
+        const int64_t kb = (s.K + (s.tc_elem == 1 ? 64 : 32) - 1) / (s.tc_elem == 1 ? 64 : 32);
+        if (wave_ctr && s.tc_pair && !(ws_env && *ws_env == '0') && pairs > 0 && h.split_first >= 2 * pairs &&
+            kb >= 128) {
+            h.wave_ctr = wave_ctr;
+            L.wave_sync = true;
+        }
+    }
     // Tiles are walked in groups of group_m M-tiles (all N-tiles of a group
     // before the next).  One wave of concurrent tiles then reads about
     // group_m A panels and waves/group_m B panels; their sum is smallest for

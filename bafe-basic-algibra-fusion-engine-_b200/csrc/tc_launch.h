@@ -10,6 +10,7 @@ struct TcLaunch {
     unsigned grid = 0, block = 0, smem = 0;
     unsigned cluster = 1;          // CTAs per cluster (2 for the CTA-pair kernel)
     unsigned fix_grid = 0;         // > 0: split tail tiles; launch the fixup kernel (256 threads) after
+    bool wave_sync = false;        // the wave counter must be zeroed before the launch
 };
 
 // K split of the tail tiles (gemm_tc.cuh, unit_range): parts per tile (1:
@@ -25,9 +26,10 @@ bool tc_kernel_enabled();
 int tc_smem_bytes(int variant, bool pair = false);
 // a_lo / b_lo: 3xTF32 residual operands (same layouts as a / b), or null.
 // ws / ws_bytes: workspace for split tail tiles (tc_split_of), or null: no split.
+// wave_ctr: a device word for the pair kernel's wave alignment, or null: none.
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, void* ws, size_t ws_bytes,
-               TcLaunch& L, std::string& err);
+               unsigned* wave_ctr, TcLaunch& L, std::string& err);
 // elem: 0 = u8, 1 = f32, 2 = bf16; swizzle: 0 none, 1 = 128B, 2 = 128B with 32-byte atoms
 int tc_encode_tensor_map(void* map, int elem, int rank, void* gaddr, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err);

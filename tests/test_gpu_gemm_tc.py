@@ -390,3 +390,27 @@ def test_split_tail_tiles(cuda, monkeypatch, batch, M, N, K, prec, pair, elem):
         print(f"split={split} {prec} pair={pair} {batch}x{M}x{N}x{K}: max err {float(err.max()):.3e}")
         assert bool((err <= tol).all())
     assert bool(((outs["1"].double() - outs["0"].double()).abs() <= 2 * tol).all())
+
+
+def test_wave_alignment_changes_no_bit(cuda, monkeypatch):
+    """The pair kernel's producers align their waves (for two or more whole
+    waves of tiles with K >= 128 k-blocks); it reorders no sum, so the
+    result is bit for bit the unaligned one."""
+    torch = cuda
+    M, N, K = 4096, 2560, 4096               # 16 x 10 = 160 pair tiles: 148 whole, 12 split
+    gen = torch.Generator(device="cuda").manual_seed(41)
+    A = torch.randn(M, K, device="cuda", generator=gen)
+    B = torch.randn(K, N, device="cuda", generator=gen)
+    C = torch.randn(M, N, device="cuda", generator=gen)
+    bafe.set_option("gemm_precision", "3xtf32")
+    k = bafe.compile_graph(_graph(M, N, K, 0, 0, "relu_add_c"))
+    outs = {}
+    for on in ("1", "0"):
+        monkeypatch.setenv("BAFE_TC_WAVE_SYNC", on)
+        out = torch.full((M, N), float("nan"), device="cuda")   # a new output: prepared anew
+        k.run_torch([A, B, C], out)
+        bafe.synchronize()
+        outs[on] = out
+    assert torch.equal(outs["1"], outs["0"])
+    ref = torch.relu(A.double() @ B.double() + C.double())
+    assert float((outs["1"].double() - ref).abs().max()) <= 1e-4 * math.sqrt(K / 64)
