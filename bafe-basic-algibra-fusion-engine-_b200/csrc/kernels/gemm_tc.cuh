@@ -129,6 +129,13 @@ template <> struct TcPairCfg<3> {
     static constexpr int STAGES = 3, THREADS = 320, KB_PER_CHUNK = 2;
 };
 
+// Two IEEE round-to-nearest fp32 additions in one instruction (Blackwell
+// packed fp32): a0 += b0, a1 += b1, the same results as two __fadd_rn.
+__device__ __forceinline__ void fadd2_rn(float& a0, float& a1, u32 b0, u32 b1) {
+    asm("{\n\t.reg .b64 x, y;\n\tmov.b64 x, {%0, %1};\n\tmov.b64 y, {%2, %3};\n\tadd.rn.f32x2 x, x, y;\n\tmov.b64 {%0, %1}, x;\n\t}"
+        : "+f"(a0), "+f"(a1) : "r"(b0), "r"(b1));
+}
+
 // Residual of the tf32 truncation: x - (x with the low 13 mantissa bits
 // cleared), exact in fp32; 0 for inf / NaN (whose hi part carries them).
 __device__ __forceinline__ float tf32_lo(float x) {
@@ -869,7 +876,7 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                     u32 r[32];
                     tmem_ld32(tmem + lane_addr + (u32)(buf * BN + half * 128 + 32 * j), r);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) acc[32 * j + e] = __fadd_rn(acc[32 * j + e], __uint_as_float(r[e]));
+                    for (int e = 0; e < 32; e += 2) fadd2_rn(acc[32 * j + e], acc[32 * j + e + 1], r[e], r[e + 1]);
                 }
                 tc_fence_before();
                 mbar_arrive(TEMPTY(buf));
@@ -1182,9 +1189,9 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     tmem_ld32_nowait(tmem + lane_addr + (u32)(buf * BN + half * 128 + 32 * (j + 1)), r1);
                     tmem_wait_ld(r0, r1);
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        acc[32 * j + e] = __fadd_rn(acc[32 * j + e], __uint_as_float(r0[e]));
-                        acc[32 * (j + 1) + e] = __fadd_rn(acc[32 * (j + 1) + e], __uint_as_float(r1[e]));
+                    for (int e = 0; e < 32; e += 2) {
+                        fadd2_rn(acc[32 * j + e], acc[32 * j + e + 1], r0[e], r0[e + 1]);
+                        fadd2_rn(acc[32 * (j + 1) + e], acc[32 * (j + 1) + e + 1], r1[e], r1[e + 1]);
                     }
                 }
                 tc_fence_before();
