@@ -1002,9 +1002,11 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 // loads of wave w once every pair has issued all of wave
                 // w-1's, so the pairs of a wave walk K together and share the
                 // operand panels' slices in L2 instead of re-reading them
-                // from HBM as they drift apart.  The wait is bounded; when it
-                // runs out this CTA stops aligning (results do not depend on
-                // it).
+                // from HBM as they drift apart.  The wait is bounded (100 us;
+                // aligned pairs stay microseconds apart, and a pair that is not
+                // resident -- other kernels holding SMs -- costs one such wait);
+                // when it runs out this CTA stops aligning (results do not
+                // depend on it).
                 const bool aligned = g.wave_ctr && cta == 0 && u < g.split_first;
                 if (aligned && align_on && u >= num_pairs) {
                     const unsigned need = (unsigned)(u - pair);   // pairs x waves before this one
@@ -1013,7 +1015,7 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         unsigned v;
                         asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(g.wave_ctr) : "memory");
                         if (v >= need) break;
-                        if (now_ns() - t0 > 2000000ull) { align_on = false; break; }
+                        if (now_ns() - t0 > 100000ull) { align_on = false; break; }
                         __nanosleep(256);
                     }
                 }
