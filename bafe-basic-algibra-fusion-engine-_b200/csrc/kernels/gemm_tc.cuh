@@ -7,15 +7,17 @@
 //                 swizzled shared-memory stages.  No multicast.
 //   warp 1        allocates TMEM; one lane issues tcgen05.mma (kind::tf32,
 //                 M=128, N=256, K=8 per instruction).  The K loop is cut
-//                 into chunks (KC = 128 for 1xTF32, 64 for 3xTF32); each
-//                 chunk accumulates into one of two TMEM buffers, starting
-//                 from zero.
+//                 into chunks (KC k-blocks: TcCfg / TcPairCfg, or the
+//                 element trait's KB_CHUNK); each chunk accumulates into
+//                 one of two TMEM buffers, starting from zero.
 //   warps 2-9     accumulate: each thread owns one tile row (TMEM lane) and
 //                 128 columns; after every chunk it tcgen05.ld's the chunk
 //                 partial sums and adds them into 128 fp32 registers with
-//                 round-to-nearest, then releases the TMEM buffer to the
+//                 round-to-nearest (packed fp32x2 adds), then releases the
+//                 TMEM buffer to the
 //                 MMA warp.  After the last chunk it applies the generated
-//                 epilogue (Spec::apply: relu(acc + C), ...) and stores.
+//                 epilogue (Spec::apply4: relu(acc + C), ...) and stores
+//                 through TMA (tc_epilogue).
 //                 For 3xTF32 with CONVERT the same threads also write the
 //                 tf32 residuals of every stage, one chunk ahead of the
 //                 drain they wait for (see below).
