@@ -147,6 +147,11 @@ struct Plan {
     int64_t stream_rows = 0;       // rows of the output (leading dimension)
     int64_t stream_align = 1;      // panel boundaries are multiples of this
     std::vector<int64_t> in_rb;    // bytes per output row of each input (0: whole)
+    // A plan that is one rank-2 transpose of input 0 into the output streams
+    // by output rows too, but each panel's input is a band of x's COLUMNS
+    // (a strided copy); stream_ok stays false (bafe_cuda_plan_row_split
+    // reports row splits only).
+    bool stream_cols = false;
     int64_t out_rb = 0;
     std::string source;            // generated CUDA for every step's kernel
     std::string source_hash;       // key of the cubin

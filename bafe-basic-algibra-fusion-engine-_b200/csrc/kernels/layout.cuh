@@ -10,7 +10,9 @@
 namespace bafe {
 
 // Rank-2 transpose materialisation: out has shape (M, N) and
-// out[i*N + j] = x[j*M + i] (codegen.c:363-369; x is (N, M) row-major).
+// out[i*N + j] = x[j*ldx + i] (codegen.c:363-369; x is (N, M) row-major,
+// ldx = M; a panel of output rows [r0, r0 + M') is the launch with x moved
+// r0 columns, out moved r0 rows, M = M' and ldx the full row length).
 // 32x32 tiles staged through shared memory so that both the global read
 // (along x's rows) and the global write (along out's rows) are coalesced;
 // the +1 column pad keeps the transposed shared-memory read conflict-free.
@@ -18,10 +20,10 @@ namespace bafe {
 // (ceil(N/32), ceil(M/32)) tiles, batched over blockIdx.z.
 template <class T>
 __device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restrict__ out,
-                                            i64 M, i64 N) {
+                                            i64 M, i64 N, i64 ldx) {
     __shared__ T tile[32][33];
     const i64 b = blockIdx.z;
-    x += b * M * N;
+    x += b * ldx * N;
     out += b * M * N;
     const i64 j0 = (i64)blockIdx.x * 32;   // output column block == x row block
     const i64 i0 = (i64)blockIdx.y * 32;   // output row block == x column block
@@ -29,7 +31,7 @@ __device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restri
 #pragma unroll
     for (int r = 0; r < 32; r += 8) {
         const i64 xr = j0 + ty + r, xc = i0 + tx;       // x[xr][xc], x is (N, M)
-        if (xr < N && xc < M) tile[ty + r][tx] = x[xr * M + xc];
+        if (xr < N && xc < M) tile[ty + r][tx] = x[xr * ldx + xc];
     }
     __syncthreads();
 #pragma unroll
@@ -40,7 +42,7 @@ __device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restri
 }
 
 // The same transpose for 4-byte element types with 16-byte global accesses
-// (M % 4 == 0 and N % 4 == 0, 16-byte aligned buffers): a CTA of 256
+// (M, N and ldx multiples of 4, 16-byte aligned buffers): a CTA of 256
 // threads moves a 64 x 64 tile.  Each thread first issues its four 16-byte
 // loads (four rows of x, 64 B in flight), then scatters the 16 elements into
 // the tile stored transposed -- S[c][r] for x's row r, column c -- and after
@@ -50,7 +52,7 @@ __device__ __forceinline__ void transpose2d(const T* __restrict__ x, T* __restri
 // that the scattering stores spread over the banks (2-way at most) while
 // every vector read stays one aligned chunk.
 template <class T>
-__device__ __forceinline__ void transpose2d_w4(const T* __restrict__ x, T* __restrict__ out, i64 M, i64 N) {
+__device__ __forceinline__ void transpose2d_w4(const T* __restrict__ x, T* __restrict__ out, i64 M, i64 N, i64 ldx) {
     static_assert(sizeof(T) == 4, "4-byte element types only");
     __shared__ __align__(16) u32 S[64 * 64];
     const i64 j0 = (i64)blockIdx.x * 64;   // x row block == out column block
@@ -61,7 +63,7 @@ __device__ __forceinline__ void transpose2d_w4(const T* __restrict__ x, T* __res
 #pragma unroll
     for (int pass = 0; pass < 4; ++pass) {
         const i64 xr = j0 + r0 + 16 * pass, xc = i0 + 4 * q;
-        if (xr < N && xc < M) v[pass] = __ldcs(reinterpret_cast<const uint4*>(x + xr * M + xc));
+        if (xr < N && xc < M) v[pass] = __ldcs(reinterpret_cast<const uint4*>(x + xr * ldx + xc));
         else v[pass] = make_uint4(0u, 0u, 0u, 0u);
     }
 #pragma unroll

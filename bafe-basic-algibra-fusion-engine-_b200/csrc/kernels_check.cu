@@ -71,11 +71,11 @@ extern "C" __global__ void __launch_bounds__(bafe::TcCfg<1>::THREADS, 1) check_g
 extern "C" __global__ void __launch_bounds__(256) check_gemm_tc_fixup_bf16(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_fixup<CheckSpecBf16, 128>(g);
 }
-extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N) {
-    bafe::transpose2d<float>(x, out, M, N);
+extern "C" __global__ void __launch_bounds__(256) check_transpose(const float* x, float* out, i64 M, i64 N, i64 ldx) {
+    bafe::transpose2d<float>(x, out, M, N, ldx);
 }
-extern "C" __global__ void __launch_bounds__(256) check_transpose_w4(const float* x, float* out, i64 M, i64 N) {
-    bafe::transpose2d_w4<float>(x, out, M, N);
+extern "C" __global__ void __launch_bounds__(256) check_transpose_w4(const float* x, float* out, i64 M, i64 N, i64 ldx) {
+    bafe::transpose2d_w4<float>(x, out, M, N, ldx);
 }
 extern "C" __global__ void __launch_bounds__(256) check_gather(const float* x, float* out, const bafe::GatherArgs g) {
     bafe::gather_nd<float>(x, out, g);

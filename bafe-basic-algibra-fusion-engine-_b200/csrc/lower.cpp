@@ -813,11 +813,12 @@ struct Lowerer {
             s.N = x.shape.d[1];
             s.kernel = kname("transpose");
             src << "\nextern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const " << ty << "* x, " << ty
-                << "* out, i64 M, i64 N) { bafe::transpose2d<" << ty << ">(x, out, M, N); }\n";
+                << "* out, i64 M, i64 N, i64 ldx) { bafe::transpose2d<" << ty << ">(x, out, M, N, ldx); }\n";
             if (dtype_size(T) == 4) {
                 s.kernel_vec = s.kernel + "_v4";
                 src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel_vec << "(const " << ty
-                    << "* x, " << ty << "* out, i64 M, i64 N) { bafe::transpose2d_w4<" << ty << ">(x, out, M, N); }\n";
+                    << "* x, " << ty << "* out, i64 M, i64 N, i64 ldx) { bafe::transpose2d_w4<" << ty
+                    << ">(x, out, M, N, ldx); }\n";
             }
             s.describe = "transpose2d m=" + std::to_string((long long)s.M) + " n=" + std::to_string((long long)s.N);
         } else {

@@ -607,19 +607,23 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 break;
             }
             case StepKind::Transpose2d: {
-                if (s.M == 0 || s.N == 0) break;
-                const void* x = ptr_of(s.srcs[0]);
-                int64_t M = s.M, Nn = s.N;
-                void* params[] = {&x, &dst, &M, &Nn};
-                if (ds->fn_vec[si] && s.M % 4 == 0 && s.N % 4 == 0 && ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
-                    if ((s.M + 63) / 64 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((s.M + 63) / 64), 1,
+                // a panel (column-streamed host call) is output rows
+                // [r0, r0 + rows): x moved r0 columns (src_rb = one element),
+                // out moved r0 rows (dst_rb), x's row length stays s.M
+                if (m_run == 0 || s.N == 0) break;
+                const void* x = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
+                int64_t M = m_run, Nn = s.N, ldx = s.M;
+                void* params[] = {&x, &dst, &M, &Nn, &ldx};
+                if (ds->fn_vec[si] && M % 4 == 0 && s.N % 4 == 0 && ldx % 4 == 0 &&
+                    ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
+                    if ((M + 63) / 64 > 65535) { set_error(8, "transpose grid too large"); return 8; }
+                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((M + 63) / 64), 1,
                                         256, 1, 1, 0, stream, params))
                         return rc;
                     break;
                 }
-                if ((s.M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((s.M + 31) / 32), 1, 32, 8, 1,
+                if ((M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
+                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((M + 31) / 32), 1, 32, 8, 1,
                                     0, stream, params))
                     return rc;
                 break;
@@ -709,7 +713,7 @@ namespace {
 
 // Number of row panels a host call of plan p is split into (1 = not split).
 int host_panel_count(const Plan& p) {
-    if (!p.stream_ok) return 1;
+    if (!p.stream_ok && !p.stream_cols) return 1;
     const int want = options().host_panels;
     if (want == 0 || want == 1) return 1;
     const int64_t R = p.stream_rows, align = p.stream_align;
@@ -815,6 +819,21 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
         for (int k = 0; k < p.n_inputs && !rc; ++k) {
             const int64_t b = p.in_rb[k];
             if (b == 0 || here(k)) continue;
+            if (p.stream_cols) {
+                // columns [r0, r0 + rows) of x (N rows of M elements): one
+                // strided copy, the same band in the staged x
+                const Step& t = p.steps[0];
+                const size_t es = (size_t)t.dst_esize, pitch = (size_t)t.M * es;
+                cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(ds->in_stage[k]) + r0 * es, pitch,
+                                                  static_cast<const char*>(ptrs[k]) + r0 * es, pitch, (size_t)rows * es,
+                                                  (size_t)t.N, cudaMemcpyDefault, ds->h2d);
+                if (e != cudaSuccess) {
+                    cudaGetLastError();
+                    set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
+                    rc = 7;
+                }
+                continue;
+            }
             rc = copy_async(static_cast<char*>(ds->in_stage[k]) + r0 * b, static_cast<const char*>(ptrs[k]) + r0 * b,
                             rows * b, ds->h2d, "host-to-device copy");
         }

@@ -31,7 +31,30 @@
 
 namespace bafe_cuda {
 
+// A plan that is exactly one rank-2 transpose, input 0 -> output (out (M, N),
+// out[i][j] = x[j][i]): output rows [r0, r1) are x's columns [r0, r1), one
+// element of every x row per output row.  The host call streams it like a
+// row-split plan, copying each panel's band of columns with one strided
+// copy, so the input and output copies run at the same time.
+static void analyse_column_streaming(Plan& P, int64_t R) {
+    P.stream_cols = false;
+    if (P.steps.size() != 1 || P.n_inputs != 1) return;
+    Step& s = P.steps[0];
+    if (s.kind != StepKind::Transpose2d || s.M != R || s.M < 2 || s.N < 1) return;
+    if (s.srcs.size() != 1 || s.srcs[0].kind != BufRef::In || s.srcs[0].idx != 0 || s.dst.kind != BufRef::Out) return;
+    if (s.dst_esize <= 0 || P.in_bytes[0] != s.M * s.N * s.dst_esize) return;
+    s.panel = true;
+    s.dst_rb = s.N * s.dst_esize;          // output: whole rows
+    s.src_rb.assign(1, s.dst_esize);       // input: r0 columns in
+    P.in_rb[0] = s.N * s.dst_esize;        // bytes per output row, moved by the strided copy
+    P.out_rb = s.N * s.dst_esize;
+    P.stream_rows = R;
+    P.stream_align = 64;                   // whole 64 x 64 tiles, 16-byte aligned column offsets
+    P.stream_cols = true;
+}
+
 void analyse_row_streaming(Plan& P, const Shape& out_shape) {
+    P.stream_cols = false;
     P.stream_ok = false;
     P.stream_rows = 0;
     P.in_rb.assign(P.n_inputs, 0);
@@ -122,6 +145,7 @@ void analyse_row_streaming(Plan& P, const Shape& out_shape) {
             s.src_rb.assign(s.srcs.size(), 0);
             s.aux_rb.assign(s.aux.size(), 0);
         }
+        analyse_column_streaming(P, R);
         return;
     }
     for (int k = 0; k < P.n_inputs; ++k) {

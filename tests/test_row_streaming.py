@@ -179,3 +179,23 @@ def test_host_call_with_a_resident_input(cuda, panels):
     assert torch.equal(got, want)
     ref = oracle.evaluate(g.to_list(), dict(zip(g.inputs, (A.numpy(), B.numpy(), C.numpy()))), g.output)
     assert got.numpy().tobytes() == ref.reshape(M, N).tobytes()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape,dtype,panels", [
+    ((1000, 768), np.float32, 4),      # 16-byte kernel; panels of 192 output rows
+    ((517, 333), np.float32, 3),       # scalar kernel; panels of 128, 128, 77 rows
+    ((300, 260), np.float64, 2),       # 8-byte elements
+])
+def test_streamed_transpose_is_bit_identical(cuda, shape, dtype, panels):
+    """A plan that is one transpose streams by output rows: each panel's
+    input is a band of x's columns (one strided copy), so the input and
+    output copies overlap.  Same bits as one piece and as x.T."""
+    rng = np.random.default_rng(12)
+    X = rng.standard_normal(shape).astype(dtype)
+    dt = 0 if dtype == np.float32 else 1
+    k, g = _kernel(lambda g, X_: g.add("transpose", [X_], perm=[1, 0]), ("X", shape, dt, 0))
+    assert k.row_split() is None              # not a row split: x splits by columns
+    whole, split = _both(k, (X,), panels)
+    assert split.tobytes() == whole.tobytes()
+    assert split.tobytes() == np.ascontiguousarray(X.T).tobytes()
