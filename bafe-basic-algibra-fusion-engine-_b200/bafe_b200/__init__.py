@@ -147,14 +147,17 @@ class Kernel:
         if code:
             raise RuntimeError(f"bafe_cuda kernel failed (code {code}): {msg}")
 
-    def call_host_resident(self, ptrs: Sequence[int], resident: Sequence[bool]) -> None:
+    def call_host_resident(self, ptrs: Sequence[int], resident: Sequence[bool], ready=None) -> None:
         """bafe_cuda_run_host_resident: host pointers, except the inputs whose
-        `resident` flag is set, which are device buffers read in place."""
+        `resident` flag is set, which are device buffers read in place;
+        `ready` (a torch.cuda.Event or a raw cudaEvent_t) is recorded after
+        the work that fills them: the copies start at once, the kernels wait."""
         if len(resident) != self.n_inputs:
             raise TypeError(f"kernel takes {self.n_inputs} inputs, got {len(resident)} resident flags")
         arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
         flags = (ctypes.c_ubyte * self.n_inputs)(*[1 if r else 0 for r in resident])
-        if lib.bafe_cuda_run_host_resident(self.plan, arr, len(ptrs), flags):
+        ev = getattr(ready, "cuda_event", ready)
+        if lib.bafe_cuda_run_host_resident(self.plan, arr, len(ptrs), flags, ctypes.c_void_p(ev) if ev else None):
             code, msg = last_error()
             raise RuntimeError(f"bafe_cuda_run_host_resident failed (code {code}): {msg}")
 

@@ -138,7 +138,7 @@ def _load() -> ctypes.CDLL:
         "bafe_cuda_plan_row_split": ([c_int, POINTER(c_int64), POINTER(c_int64), c_int, POINTER(c_int64)], c_int),
         "bafe_cuda_run_device": ([c_int, POINTER(c_void_p), c_int, c_void_p], c_int),
         "bafe_cuda_run_host": ([c_int, POINTER(c_void_p), c_int], c_int),
-        "bafe_cuda_run_host_resident": ([c_int, POINTER(c_void_p), c_int, POINTER(ctypes.c_ubyte)], c_int),
+        "bafe_cuda_run_host_resident": ([c_int, POINTER(c_void_p), c_int, POINTER(ctypes.c_ubyte), c_void_p], c_int),
         "bafe_cuda_synchronize": ([], c_int),
         "bafe_cuda_last_error": ([c_char_p, c_size_t], c_int),
         "bafe_cuda_clear_error": ([], None),

@@ -90,8 +90,9 @@ class SharedInput:
             return d.get_world_size(), d.get_rank()
         return 1, 0
 
-    def assemble(self, host):
-        """Device copy of the host tensor `host` (same dtype and shape)."""
+    def copy_slab(self, host):
+        """Copy this rank's byte slab of the host tensor `host` into the device
+        buffer (enqueued on the current stream)."""
         import torch
         world, rank = self._world()
         flat = host.contiguous().view(-1).view(torch.uint8)
@@ -101,26 +102,46 @@ class SharedInput:
         dev = self.device if self.device is not None else torch.device("cuda", torch.cuda.current_device())
         if self.buf is None or self.buf.numel() != world * slab or self.buf.device != torch.device(dev):
             self.buf = torch.empty(world * slab, dtype=torch.uint8, device=dev)
+        self._host, self._n, self._slab = host, n, slab
         lo, hi = min(rank * slab, n), min((rank + 1) * slab, n)
-        mine = self.buf[rank * slab:(rank + 1) * slab]
         if hi > lo:
-            mine[: hi - lo].copy_(flat[lo:hi], non_blocking=True)
+            self.buf[rank * slab: rank * slab + hi - lo].copy_(flat[lo:hi], non_blocking=True)
+
+    def gather(self):
+        """All-gather the slabs (after copy_slab); returns the device copy of
+        the host tensor (same dtype and shape)."""
+        world, rank = self._world()
         if world > 1:
+            mine = self.buf[rank * self._slab:(rank + 1) * self._slab]
             self.dist.all_gather_into_tensor(self.buf, mine)
-        return self.buf[:n].view(host.dtype).view(host.shape)
+        return self.buf[:self._n].view(self._host.dtype).view(self._host.shape)
+
+    def assemble(self, host):
+        """Device copy of the host tensor `host` (same dtype and shape)."""
+        self.copy_slab(host)
+        return self.gather()
 
 
 def run_host_shared(kernel, host_inputs: Sequence, host_out, shared: dict) -> None:
     """One host-pointer call of `kernel` (bafe_cuda_run_host_resident) where
     the inputs at the indices of `shared` (index -> SharedInput) are
-    assembled on the device first (slab copy + all-gather); the other
-    inputs and the output are host tensors, row-streamed as in a plain
-    host call.  Synchronous."""
+    assembled on the device (slab copy, then all-gather); the other inputs
+    and the output are host tensors, row-streamed as in a plain host call.
+    The call starts once the slab copies are done: its own input copies run
+    during the all-gather and its kernels wait for it (an event).
+    Synchronous."""
     import torch
-    dev_inputs = {k: sh.assemble(host_inputs[k]) for k, sh in shared.items()}
-    torch.cuda.current_stream().synchronize()            # the plan's streams read them next
+    for k, sh in shared.items():
+        sh.copy_slab(host_inputs[k])
+    slabs = torch.cuda.Event()
+    slabs.record()
+    dev_inputs = {k: sh.gather() for k, sh in shared.items()}
+    ready = torch.cuda.Event()
+    ready.record()
+    slabs.synchronize()                                  # this rank's host link is free again
     ptrs = [(dev_inputs[k] if k in dev_inputs else t).data_ptr() for k, t in enumerate(host_inputs)]
-    kernel.call_host_resident(ptrs + [host_out.data_ptr()], [k in dev_inputs for k in range(len(host_inputs))])
+    kernel.call_host_resident(ptrs + [host_out.data_ptr()], [k in dev_inputs for k in range(len(host_inputs))],
+                              ready)
 
 
 class RowPanelGemm:

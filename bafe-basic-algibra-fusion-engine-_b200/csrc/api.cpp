@@ -303,11 +303,12 @@ BAFE_API int bafe_cuda_run_host(int plan, void* const* ptrs, int n_ptrs) {
     return run_plan_host(*p, ptrs, n_ptrs);
 }
 
-BAFE_API int bafe_cuda_run_host_resident(int plan, void* const* ptrs, int n_ptrs, const unsigned char* resident) {
+BAFE_API int bafe_cuda_run_host_resident(int plan, void* const* ptrs, int n_ptrs, const unsigned char* resident,
+                                         void* ready) {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     Plan* p = plan_ptr(plan);
     if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
-    return run_plan_host(*p, ptrs, n_ptrs, resident);
+    return run_plan_host(*p, ptrs, n_ptrs, resident, ready);
 }
 
 BAFE_API int bafe_cuda_last_error(char* buf, size_t buf_size) {

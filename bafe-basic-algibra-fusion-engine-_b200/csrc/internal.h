@@ -184,8 +184,10 @@ std::string sha256_hex(const void* data, size_t len);
 
 // Runtime (runtime.cpp).
 int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
-// resident: per input, nonzero = ptrs[k] is already a device buffer (or null: none)
-int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident = nullptr);
+// resident: per input, nonzero = ptrs[k] is already a device buffer (or null: none);
+// ready: cudaEvent_t the kernels wait for before reading them (or null)
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident = nullptr,
+                  void* ready = nullptr);
 // Synchronises the current device and reports a kernel-raised error word.
 int synchronize_current_device();
 void release_plan_device_state(Plan& p);

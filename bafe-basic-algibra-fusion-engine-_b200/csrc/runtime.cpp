@@ -763,7 +763,8 @@ int copy_async(void* dst, const void* src, int64_t bytes, cudaStream_t st, const
 // each panel's output rows after its steps.  All copies of one direction
 // are issued before the other's, so with pageable host memory (whose copies
 // the driver makes synchronous) the input copies still overlap the kernels.
-int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels, const unsigned char* resident) {
+int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels, const unsigned char* resident,
+                           void* ready) {
     const int64_t R = p.stream_rows, align = p.stream_align;
     int64_t rows_per = (R + panels - 1) / panels;
     rows_per = (rows_per + align - 1) / align * align;
@@ -810,6 +811,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
     if (rc) return fail(rc);
     cudaEventRecord(whole, ds->h2d);
     cudaStreamWaitEvent(ds->stream, whole, 0);
+    if (ready) cudaStreamWaitEvent(ds->stream, (cudaEvent_t)ready, 0);   // resident inputs filled
     cudaEventRecord(ds->tev[0], ds->stream);
     if ((rc = run_steps(p, ds, ds->device, dptrs.data(), ds->stream, Pass{Pass::Once, 0, 0}))) return fail(rc);
     cudaEventRecord(ds->tev[1], ds->stream);
@@ -862,7 +864,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
 
 }  // namespace
 
-int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident) {
+int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident, void* ready) {
     if (n_ptrs != p.n_inputs + 1) {
         set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
         return 8;
@@ -897,7 +899,8 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
     }
     if (int rc = ensure_tmps(p, ds)) return rc;
     const int panels = host_panel_count(p);
-    if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels, resident);
+    if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels, resident, ready);
+    if (ready) cudaStreamWaitEvent(ds->stream, (cudaEvent_t)ready, 0);   // resident inputs filled
     for (int k = 0; k < p.n_inputs; ++k) {
         if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
         cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], ptrs[k], (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);

@@ -243,11 +243,15 @@ int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);
  * resident[k] != 0 makes ptrs[k] (k < n_inputs) a device buffer of the
  * input, read in place instead of copied from the host; the other inputs
  * and the output are host pointers as in bafe_cuda_run_host (row-streamed
- * the same way).  Synchronous.  Used by multi-GPU callers that assemble an
- * input every rank reads whole (a GEMM's B) over NVLink instead of copying
- * it from the host on every rank.  Extension: the reference has no device
- * memory.  Returns 0 or a nonzero code. */
-int bafe_cuda_run_host_resident(int plan, void *const *ptrs, int n_ptrs, const unsigned char *resident);
+ * the same way).  `ready` is a cudaEvent_t recorded after the work that
+ * fills the resident inputs (NULL: they are ready): the host-to-device
+ * copies start at once and the kernels wait for it.  Synchronous.  Used by
+ * multi-GPU callers that assemble an input every rank reads whole (a GEMM's
+ * B) over NVLink instead of copying it from the host on every rank.
+ * Extension: the reference has no device memory.  Returns 0 or a nonzero
+ * code. */
+int bafe_cuda_run_host_resident(int plan, void *const *ptrs, int n_ptrs, const unsigned char *resident,
+                                void *ready);
 
 /* Waits for all work on the current device and reports an error a kernel
  * raised asynchronously (a pipeline wait that exceeded its deadline; the

@@ -199,3 +199,35 @@ def test_streamed_transpose_is_bit_identical(cuda, shape, dtype, panels):
     whole, split = _both(k, (X,), panels)
     assert split.tobytes() == whole.tobytes()
     assert split.tobytes() == np.ascontiguousarray(X.T).tobytes()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("panels", ["0", "4"])
+def test_resident_input_filled_after_the_call_starts(cuda, panels):
+    """The resident input is written on another stream, behind ~25 ms of
+    other work, and the call gets the event recorded after it: the kernels
+    wait (reading the buffer early would compute with its zeros)."""
+    torch = cuda
+    bafe.set_option("gemm_precision", "exact")
+    M, K, N = 1000, 96, 40
+    gen = torch.Generator().manual_seed(13)
+    A, B, C = (torch.randn(*s, generator=gen) for s in ((M, K), (K, N), (M, N)))
+    Bpin = B.pin_memory()
+    k, _ = _kernel(_gemm_relu_add, ("A", (M, K), 0, 0), ("B", (K, N), 0, 0), ("C", (M, N), 0, 0))
+    want = torch.zeros(M, N)
+    k.call_host_ptrs([A.data_ptr(), B.data_ptr(), C.data_ptr(), want.data_ptr()])
+    Bd = torch.zeros(K, N, device="cuda")
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    ready = torch.cuda.Event()
+    with torch.cuda.stream(side):
+        torch.cuda._sleep(50_000_000)             # a bounded spin, then the real values
+        Bd.copy_(Bpin, non_blocking=True)
+        ready.record(side)
+    bafe.set_option("host_panels", panels)
+    try:
+        got = torch.zeros(M, N)
+        k.call_host_resident([A.data_ptr(), Bd.data_ptr(), C.data_ptr(), got.data_ptr()], [False, True, False], ready)
+    finally:
+        bafe.set_option("host_panels", "auto")
+    assert torch.equal(got, want)
