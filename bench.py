@@ -27,7 +27,10 @@ value:   device-resident inputs, CUDA events around every step on the
          (126 MB), so no flush is needed between steps.
 e2e:     the same metric through the C-ABI host function (host pointers,
          pinned): every step copies its inputs host->device and the
-         result device->host inside the timed region.
+         result device->host inside the timed region (row-streamed).  For
+         the GEMM under torchrun each rank copies its row panels of A and C
+         and a 1/N slab of B, and an NCCL all-gather completes B on every
+         rank (bafe_cuda_run_host_resident), all inside the timed region.
 cpu_baseline: the reference's own generated C kernel (oracle/_ref, built
          from the reference sources) on a bounded row-panel / chunk sample,
          1 core, rank 0 only.  Falls back to the oracle restatement.
