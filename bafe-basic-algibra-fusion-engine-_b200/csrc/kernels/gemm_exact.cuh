@@ -14,7 +14,10 @@
 //
 // Tiling: 64x64 output tile per 256-thread block, k staged 32 at a time
 // through shared memory (the chunk width, so a chunk never spans two
-// stages).  Thread (tx, ty) owns rows ty + 16r and columns tx + 16c.
+// stages).  Thread (tx, ty) owns rows 4ty .. 4ty+3 and columns 4tx ..
+// 4tx+3, so each k-step reads its four A and four B values as two
+// contiguous runs (vector shared-memory loads; rows padded to 68 elements
+// keep them 16-byte aligned) instead of eight scalar loads.
 #pragma once
 #include "bafe_dev.cuh"
 
@@ -42,8 +45,8 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
     typedef typename Spec::T T;
     typedef typename Spec::P P;
     typedef typename Spec::S S;
-    __shared__ TA As[32][65];   // As[k][m]
-    __shared__ TB Bs[32][65];   // Bs[k][n]
+    __shared__ __align__(16) TA As[32][68];   // As[k][m]
+    __shared__ __align__(16) TB Bs[32][68];   // Bs[k][n]
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const i64 bz = blockIdx.z;
@@ -93,9 +96,9 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
             TA a[4];
             TB b[4];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) a[r] = As[k][ty + 16 * r];
+            for (int r = 0; r < 4; ++r) a[r] = As[k][4 * ty + r];
 #pragma unroll
-            for (int c = 0; c < 4; ++c) b[c] = Bs[k][tx + 16 * c];
+            for (int c = 0; c < 4; ++c) b[c] = Bs[k][4 * tx + c];
 #pragma unroll
             for (int r = 0; r < 4; ++r)
 #pragma unroll
@@ -119,20 +122,20 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
     Out res[4][4];
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-        const i64 i = m0 + ty + 16 * r;
+        const i64 i = m0 + 4 * ty + r;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const i64 j = n0 + tx + 16 * c;
+            const i64 j = n0 + 4 * tx + c;
             if (i < M && j < N) res[r][c] = Spec::apply(DIRECT ? acc[r][c] : v[r][c], g, bz, i, j);
         }
     }
 #pragma unroll
     for (int r = 0; r < 4; ++r) {
-        const i64 i = m0 + ty + 16 * r;
+        const i64 i = m0 + 4 * ty + r;
         if (i >= M) continue;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            const i64 j = n0 + tx + 16 * c;
+            const i64 j = n0 + 4 * tx + c;
             if (j < N) out[i * N + j] = res[r][c];
         }
     }
