@@ -75,7 +75,7 @@ def parse():
     p.add_argument("--precision", default=os.environ.get("BAFE_GEMM_PRECISION", "auto"))
     p.add_argument("--e2e-steps", type=int, default=3, help="0 skips the host-pointer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--only", choices=["gemm", "ew", "transpose"], default=None,
+    p.add_argument("--only", choices=["gemm", "gemm_bf16", "ew", "transpose"], default=None,
                    help="run one workload (profiling); prints its own line")
     p.add_argument("--gemm-size", type=int, default=GEMM_M, help="M=N=K (profiling smaller cases)")
     p.add_argument("--ew-elements", type=int, default=EW_N)
@@ -684,6 +684,8 @@ def run_ours(args):
         fn = bench_ew if args.only == "ew" else bench_transpose
         line = dict(fn(c), **{k: v for k, v in common.items() if k != "steps"})
         line["scaling"] = "strong"
+    elif args.only == "gemm_bf16":
+        line = dict(common, **bench_gemm_bf16(c))
     else:
         line = dict(common, **bench_gemm(c))
         if args.only is None:
