@@ -176,12 +176,8 @@ __device__ __forceinline__ void mbar_arrive(u32 bar) {
 __device__ __forceinline__ void mbar_expect_tx(u32 bar, u32 bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void tma_load_2d(u32 dst, const TmaDesc* map, u32 bar, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-        ::"r"(dst), "l"(reinterpret_cast<u64>(map)), "r"(bar), "r"(x), "r"(y) : "memory");
-}
-// The same with a third (batch) coordinate.
+// TMA tile load of a 3-D map (x, y, batch) into this CTA's shared memory,
+// completing on the mbarrier at `bar`.
 __device__ __forceinline__ void tma_load_3d(u32 dst, const TmaDesc* map, u32 bar, int x, int y, int z) {
     asm volatile(
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
