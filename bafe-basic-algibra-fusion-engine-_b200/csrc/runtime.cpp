@@ -766,9 +766,27 @@ int copy_async(void* dst, const void* src, int64_t bytes, cudaStream_t st, const
 int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int panels, const unsigned char* resident,
                            void* ready) {
     const int64_t R = p.stream_rows, align = p.stream_align;
-    int64_t rows_per = (R + panels - 1) / panels;
-    rows_per = (rows_per + align - 1) / align * align;
-    panels = (int)((R + rows_per - 1) / rows_per);
+    // Panel boundaries (multiples of align): the first and the last panel
+    // are at most align rows each when there is room -- the kernels start
+    // after a short first copy and the last output copy is short -- and the
+    // rows between are split evenly into the remaining panels, large enough
+    // to keep the kernels efficient.
+    std::vector<std::pair<int64_t, int64_t>> bounds;   // (first row, rows)
+    {
+        int64_t lo = 0, hi = R;
+        const bool ends = panels >= 4 && R >= (int64_t)(panels + 2) * align;
+        if (ends) {
+            bounds.push_back({0, align});
+            lo = align;
+            hi = (R - 1) / align * align;                // the last panel starts on a boundary too
+        }
+        const int mid = ends ? panels - 2 : panels;
+        int64_t per = (hi - lo + mid - 1) / mid;
+        per = (per + align - 1) / align * align;
+        for (int64_t r = lo; r < hi; r += per) bounds.push_back({r, hi - r < per ? hi - r : per});
+        if (ends) bounds.push_back({hi, R - hi});
+        panels = (int)bounds.size();
+    }
     for (cudaStream_t* st : {&ds->h2d, &ds->d2h}) {
         if (!*st && cudaStreamCreateWithFlags(st, cudaStreamNonBlocking) != cudaSuccess) {
             cudaGetLastError();
@@ -817,7 +835,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
     cudaEventRecord(ds->tev[1], ds->stream);
 
     for (int i = 0; i < panels; ++i) {
-        const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
+        const int64_t r0 = bounds[i].first, rows = bounds[i].second;
         for (int k = 0; k < p.n_inputs && !rc; ++k) {
             const int64_t b = p.in_rb[k];
             if (b == 0 || here(k)) continue;
@@ -849,7 +867,7 @@ int run_plan_host_streamed(Plan& p, DeviceState* ds, void* const* ptrs, int pane
         cudaEventRecord(run_done(i), ds->stream);
     }
     for (int i = 0; i < panels; ++i) {
-        const int64_t r0 = i * rows_per, rows = R - r0 < rows_per ? R - r0 : rows_per;
+        const int64_t r0 = bounds[i].first, rows = bounds[i].second;
         cudaStreamWaitEvent(ds->d2h, run_done(i), 0);
         if ((rc = copy_async(static_cast<char*>(ptrs[p.n_inputs]) + r0 * p.out_rb,
                              static_cast<char*>(ds->out_stage) + r0 * p.out_rb, rows * p.out_rb, ds->d2h,
