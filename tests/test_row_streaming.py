@@ -231,3 +231,24 @@ def test_resident_input_filled_after_the_call_starts(cuda, panels):
     finally:
         bafe.set_option("host_panels", "auto")
     assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+def test_run_host_shared_on_one_rank(cuda):
+    """parallel.run_host_shared without a process group: the shared input is
+    copied to the device (one slab), the call reads it in place after the
+    ready event; same bits as the plain host call."""
+    torch = cuda
+    from bafe_b200.parallel import SharedInput, run_host_shared
+    bafe.set_option("gemm_precision", "exact")
+    M, K, N = 1000, 96, 40
+    gen = torch.Generator().manual_seed(14)
+    A, B, C = (torch.randn(*s, generator=gen).pin_memory() for s in ((M, K), (K, N), (M, N)))
+    k, _ = _kernel(_gemm_relu_add, ("A", (M, K), 0, 0), ("B", (K, N), 0, 0), ("C", (M, N), 0, 0))
+    want = torch.zeros(M, N)
+    k.call_host_ptrs([A.data_ptr(), B.data_ptr(), C.data_ptr(), want.data_ptr()])
+    sh = SharedInput(None)
+    for _ in range(2):                               # the device buffer is reused
+        got = torch.zeros(M, N).pin_memory()
+        run_host_shared(k, [A, B, C], got, {1: sh})
+        assert torch.equal(got, want)
