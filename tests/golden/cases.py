@@ -143,40 +143,40 @@ CASES = [
          inputs=[("X", (4096,), "float32", False, 0, SPECIAL(159)), ("Y", (4096,), "float32", False, 0, SPECIAL(160)),
                  ("Z", (4096,), "float32", False, 0, SPECIAL(161))]),
     # ---- workload configs -----------------------------------------------------
-    dict(name="cfg1_seed0", cite="relu(matmul(A,B)+C) 64x64x64 (configs[0])",
+    dict(name="cfg1_seed0", cite="benchmark configuration: relu(matmul(A,B)+C) 64x64x64",
          build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
          inputs=[("A", (64, 64), "float32", False, 0, N01(0)), ("B", (64, 64), "float32", False, 0, N01(1)),
                  ("C", (64, 64), "float32", False, 0, N01(2))]),
-    dict(name="cfg2_row_col", cite="matmul 256^3, B Fortran order (configs[1])",
+    dict(name="cfg2_row_col", cite="benchmark configuration: matmul 256^3, B Fortran order",
          build=lambda g, A, B: g.add("matmul", [A, B]),
          inputs=[("A", (256, 256), "float32", False, 0, N01(10)), ("B", (256, 256), "float32", True, 1, N01(11))],
          store_inputs=False),
-    dict(name="cfg2_row_row", cite="matmul 256^3, B row-major (configs[1])",
+    dict(name="cfg2_row_row", cite="benchmark configuration: matmul 256^3, B row-major",
          build=lambda g, A, B: g.add("matmul", [A, B]),
          inputs=[("A", (256, 256), "float32", False, 0, N01(10)), ("B", (256, 256), "float32", False, 0, N01(11))],
          store_inputs=False),
-    dict(name="cfg3_panel_top", cite="relu(add(matmul(A,B), mul(C,D))) 4096^3 rows 0:8 (configs[2])",
+    dict(name="cfg3_panel_top", cite="benchmark configuration: relu(add(matmul(A,B), mul(C,D))) 4096^3, rows 0:8",
          build=lambda g, A, B, C, D: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), g.add("mul", [C, D])])]),
          inputs=[("A", (4096, 4096), "float32", False, 0, N01(20)), ("B", (4096, 4096), "float32", False, 0, N01(21)),
                  ("C", (4096, 4096), "float32", False, 0, N01(22)), ("D", (4096, 4096), "float32", False, 0, N01(23))],
          panel=(0, 8), panel_inputs=("A", "C", "D"), store_inputs=False),
-    dict(name="cfg3_panel_bottom", cite="relu(add(matmul(A,B), mul(C,D))) 4096^3 rows 4088:4096 (configs[2])",
+    dict(name="cfg3_panel_bottom", cite="benchmark configuration: relu(add(matmul(A,B), mul(C,D))) 4096^3, rows 4088:4096",
          build=lambda g, A, B, C, D: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), g.add("mul", [C, D])])]),
          inputs=[("A", (4096, 4096), "float32", False, 0, N01(20)), ("B", (4096, 4096), "float32", False, 0, N01(21)),
                  ("C", (4096, 4096), "float32", False, 0, N01(22)), ("D", (4096, 4096), "float32", False, 0, N01(23))],
          panel=(4088, 4096), panel_inputs=("A", "C", "D"), store_inputs=False),
-    dict(name="cfg4_chunk", cite="relu(add(mul(X,Y),Z)) U(-1,1) (configs[3]); first 2^17 of each vector",
+    dict(name="cfg4_chunk", cite="benchmark configuration: relu(add(mul(X,Y),Z)) U(-1,1), first 2^17 of each vector",
          build=_ew3,
          inputs=[("X", (1 << 17,), "float32", False, 0, U11(30)), ("Y", (1 << 17,), "float32", False, 0, U11(31)),
                  ("Z", (1 << 17,), "float32", False, 0, U11(32))],
          store_inputs=False),
-    dict(name="cfg5_panel_top", cite="relu(matmul(A,B)+C) 16384^3, B BLOCKED, std 1/sqrt(K), rows 0:4 (configs[4])",
+    dict(name="cfg5_panel_top", cite="benchmark configuration: relu(matmul(A,B)+C) 16384^3, B BLOCKED, std 1/sqrt(K), rows 0:4",
          build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
          inputs=[("A", (16384, 16384), "float32", False, 0, N01(40, 0.0078125)),
                  ("B", (16384, 16384), "float32", False, 2, N01(41, 0.0078125)),
                  ("C", (16384, 16384), "float32", False, 0, N01(42, 0.0078125))],
          panel=(0, 4), panel_inputs=("A", "C"), store_inputs=False),
-    dict(name="cfg5_panel_mid", cite="relu(matmul(A,B)+C) 16384^3, B TENSOR_CORE, rows 8190:8194 (configs[4])",
+    dict(name="cfg5_panel_mid", cite="benchmark configuration: relu(matmul(A,B)+C) 16384^3, B TENSOR_CORE, rows 8190:8194",
          build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
          inputs=[("A", (16384, 16384), "float32", False, 0, N01(40, 0.0078125)),
                  ("B", (16384, 16384), "float32", False, 3, N01(41, 0.0078125)),
