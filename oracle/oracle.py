@@ -1,7 +1,7 @@
 """CPU oracle for the BAFE hot path -- TEST INFRASTRUCTURE ONLY.
 
 Nothing in the product imports this module: only tests/, __graft_entry__.smoke()
-and bench.py's cpu_baseline leg do, as the checker.
+and bench.py's cpu_baseline leg do, to check results and time the CPU baseline.
 
 `evaluate(nodes, arrays)` interprets a BAFE graph node by node the way the
 reference's C99 emitter compiles it (bafe/src/codegen.c:172-551): one
