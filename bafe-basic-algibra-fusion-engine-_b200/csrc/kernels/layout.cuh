@@ -55,6 +55,8 @@ template <class T>
 __device__ __forceinline__ void transpose2d_w4(const T* __restrict__ x, T* __restrict__ out, i64 M, i64 N, i64 ldx) {
     static_assert(sizeof(T) == 4, "4-byte element types only");
     __shared__ __align__(16) u32 S[64 * 64];
+    x += (i64)blockIdx.z * ldx * N;        // batched: one (N, ldx) x / (M, N) out per z
+    out += (i64)blockIdx.z * M * N;
     const i64 j0 = (i64)blockIdx.x * 64;   // x row block == out column block
     const i64 i0 = (i64)blockIdx.y * 64;   // x column block == out row block
     const int t = threadIdx.x;

@@ -806,11 +806,20 @@ struct Lowerer {
         s.dst_esize = dtype_size(T);
         s.dst_bytes = x.shape.numel() * s.dst_esize;
         const char* ty = ctype(T);
-        if (x.shape.rank == 2 && c.shape.rank == 2) {
-            // codegen.c:363-369: out (M,N), out[i*N+j] = x[j*M+i]
+        // rank >= 3 with the last two axes swapped and the others in place:
+        // a batch of rank-2 transposes (self-inverse, so the emitter's own
+        // rank-N indexing, codegen.c:371-404, agrees)
+        bool batched2d = x.shape.rank >= 3 && c.shape.rank == x.shape.rank && (int)x.perm.size() == x.shape.rank;
+        for (int d = 0; batched2d && d < x.shape.rank - 2; ++d) batched2d = x.perm[d] == d;
+        batched2d = batched2d && x.perm[x.shape.rank - 2] == x.shape.rank - 1 && x.perm[x.shape.rank - 1] == x.shape.rank - 2;
+        if ((x.shape.rank == 2 && c.shape.rank == 2) || batched2d) {
+            // codegen.c:363-369: out (M,N), out[i*N+j] = x[j*M+i], per batch item
+            const int R2 = x.shape.rank;
             s.kind = StepKind::Transpose2d;
-            s.M = x.shape.d[0];
-            s.N = x.shape.d[1];
+            s.M = x.shape.d[R2 - 2];
+            s.N = x.shape.d[R2 - 1];
+            s.batch = 1;
+            for (int d = 0; d < R2 - 2; ++d) s.batch *= x.shape.d[d];
             s.kernel = kname("transpose");
             src << "\nextern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const " << ty << "* x, " << ty
                 << "* out, i64 M, i64 N, i64 ldx) { bafe::transpose2d<" << ty << ">(x, out, M, N, ldx); }\n";
@@ -820,7 +829,8 @@ struct Lowerer {
                     << "* x, " << ty << "* out, i64 M, i64 N, i64 ldx) { bafe::transpose2d_w4<" << ty
                     << ">(x, out, M, N, ldx); }\n";
             }
-            s.describe = "transpose2d m=" + std::to_string((long long)s.M) + " n=" + std::to_string((long long)s.N);
+            s.describe = "transpose2d m=" + std::to_string((long long)s.M) + " n=" + std::to_string((long long)s.N) +
+                         (s.batch > 1 ? " batch=" + std::to_string((long long)s.batch) : std::string());
         } else {
             // Rank-N: out[o] = x[i] with i_{perm[d]} = o_d.  The emitter's
             // own rank-N indexing (codegen.c:371-404) is only right for

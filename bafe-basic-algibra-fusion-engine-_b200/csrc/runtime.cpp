@@ -610,20 +610,22 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 // a panel (column-streamed host call) is output rows
                 // [r0, r0 + rows): x moved r0 columns (src_rb = one element),
                 // out moved r0 rows (dst_rb), x's row length stays s.M
-                if (m_run == 0 || s.N == 0) break;
+                if (m_run == 0 || s.N == 0 || s.batch < 1) break;
+                if (s.batch > 65535) { set_error(8, "transpose batch too large"); return 8; }
                 const void* x = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
                 int64_t M = m_run, Nn = s.N, ldx = s.M;
+                const unsigned nb = (unsigned)s.batch;
                 void* params[] = {&x, &dst, &M, &Nn, &ldx};
                 if (ds->fn_vec[si] && M % 4 == 0 && s.N % 4 == 0 && ldx % 4 == 0 &&
                     ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
                     if ((M + 63) / 64 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((M + 63) / 64), 1,
+                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((M + 63) / 64), nb,
                                         256, 1, 1, 0, stream, params))
                         return rc;
                     break;
                 }
                 if ((M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((M + 31) / 32), 1, 32, 8, 1,
+                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((M + 31) / 32), nb, 32, 8, 1,
                                     0, stream, params))
                     return rc;
                 break;

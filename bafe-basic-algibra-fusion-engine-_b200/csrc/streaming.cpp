@@ -40,7 +40,7 @@ static void analyse_column_streaming(Plan& P, int64_t R) {
     P.stream_cols = false;
     if (P.steps.size() != 1 || P.n_inputs != 1) return;
     Step& s = P.steps[0];
-    if (s.kind != StepKind::Transpose2d || s.M != R || s.M < 2 || s.N < 1) return;
+    if (s.kind != StepKind::Transpose2d || s.batch != 1 || s.M != R || s.M < 2 || s.N < 1) return;
     if (s.srcs.size() != 1 || s.srcs[0].kind != BufRef::In || s.srcs[0].idx != 0 || s.dst.kind != BufRef::Out) return;
     if (s.dst_esize <= 0 || P.in_bytes[0] != s.M * s.N * s.dst_esize) return;
     s.panel = true;

@@ -49,3 +49,25 @@ def test_transpose_of_special_values_is_a_bit_copy(cuda):
     x.view(np.uint32)[0, 0] = 0x7FC12345              # NaN payload survives
     out, _, _ = _transpose(x)
     assert out.view(np.uint32).tobytes() == np.ascontiguousarray(x.T).view(np.uint32).tobytes()
+
+
+@pytest.mark.parametrize("shape,perm", [
+    ((3, 68, 132), (0, 2, 1)),         # batch of 16-byte-kernel transposes
+    ((5, 37, 53), (0, 2, 1)),          # scalar kernel, ragged tiles
+    ((2, 3, 64, 40), (0, 1, 3, 2)),    # two leading axes
+    ((4, 6, 8), (1, 0, 2)),            # other permutation: the strided gather
+])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64])
+def test_rank_n_transpose_is_exact(cuda, shape, perm, dtype):
+    """Swapping the last two axes runs as a batch of tiled rank-2 transposes;
+    other permutations take the strided gather.  Bit copies either way."""
+    rng = np.random.default_rng(sum(shape) + len(perm))
+    x = rng.standard_normal(shape).astype(dtype)
+    g = GraphBuilder()
+    xi = g.add_input("X", x.shape, DT[x.dtype.type], 0)
+    g.set_output(g.add("transpose", [xi], perm=list(perm)))
+    k = bafe.compile_graph(g)
+    swap_last = tuple(perm[:-2]) == tuple(range(len(perm) - 2)) and tuple(perm[-2:]) == (len(perm) - 1, len(perm) - 2)
+    assert ("transpose2d" in k.describe()) == swap_last, k.describe()
+    out = k(x)
+    assert out.tobytes() == np.ascontiguousarray(np.transpose(x, perm)).tobytes()
