@@ -115,6 +115,28 @@ __device__ __forceinline__ void gather_nd(const T* __restrict__ x, T* __restrict
     }
 }
 
+// The same gather when the innermost output axis is contiguous in x
+// (stride 1) and a multiple of 4 long, every other stride a multiple of 4
+// (or 0): four consecutive outputs are four consecutive, aligned inputs --
+// one address computation and one vector load / store per four elements.
+// x and out 16-byte aligned.
+template <class T>
+__device__ __forceinline__ void gather_nd_v4(const T* __restrict__ x, T* __restrict__ out,
+                                             const GatherArgs& g) {
+    const i64 L4 = g.dims[g.rank - 1] / 4;
+    const i64 n4 = g.numel / 4;
+    for (i64 q = (i64)blockIdx.x * blockDim.x + threadIdx.x; q < n4; q += (i64)gridDim.x * blockDim.x) {
+        const i64 row = q / L4;
+        i64 rem = row, src = (q - row * L4) * 4;
+        for (int d = g.rank - 2; d >= 0; --d) {
+            const i64 c = rem % g.dims[d];
+            rem /= g.dims[d];
+            src += c * g.stride[d];
+        }
+        st4(out + q * 4, ld4(x + src));
+    }
+}
+
 // Single-axis reduction of an (M, N) tensor, sequential per output element
 // exactly as codegen.c:410-445 loops: axis 0 -> one output per column j
 // (consecutive threads read consecutive columns: coalesced), axis 1 -> one

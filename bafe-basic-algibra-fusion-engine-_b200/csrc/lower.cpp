@@ -852,11 +852,24 @@ struct Lowerer {
             s.kernel = kname("gather");
             src << "\nextern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const " << ty << "* x, " << ty
                 << "* out, const bafe::GatherArgs g) { bafe::gather_nd<" << ty << ">(x, out, g); }\n";
+            emit_gather_v4(s, ty);
             s.describe = "transpose rank " + std::to_string(R) + " n=" + std::to_string((long long)s.n);
         }
         P.steps.push_back(s);
         if (conv) emit_store_convert(dst, id);
         return 0;
+    }
+
+    // The vector entry of a gather step (kernel_vec), when its innermost axis
+    // reads contiguous, 4-aligned runs of x (gather_nd_v4).
+    void emit_gather_v4(Step& s, const char* ty) {
+        const int R = s.grank;
+        if (R < 1 || s.gstride[R - 1] != 1 || s.gdims[R - 1] % 4 != 0) return;
+        for (int d = 0; d < R - 1; ++d)
+            if (s.gstride[d] % 4 != 0) return;
+        s.kernel_vec = s.kernel + "_v4";
+        src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel_vec << "(const " << ty << "* x, " << ty
+            << "* out, const bafe::GatherArgs g) { bafe::gather_nd_v4<" << ty << ">(x, out, g); }\n";
     }
 
     int emit_broadcast(int id) {
@@ -892,6 +905,7 @@ struct Lowerer {
         const char* ty = ctype(T);
         src << "\nextern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const " << ty << "* x, " << ty
             << "* out, const bafe::GatherArgs g) { bafe::gather_nd<" << ty << ">(x, out, g); }\n";
+        emit_gather_v4(s, ty);
         s.describe = "broadcast_to " + c.shape.str() + " -> " + x.shape.str();
         P.steps.push_back(s);
         if (conv) emit_store_convert(dst, id);

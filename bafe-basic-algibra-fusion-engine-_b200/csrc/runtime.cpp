@@ -639,6 +639,11 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 g.rank = s.grank;
                 for (int d = 0; d < s.grank; ++d) { g.dims[d] = s.gdims[d]; g.stride[d] = s.gstride[d]; }
                 void* params[] = {&x, &dst, &g};
+                if (ds->fn_vec[si] && ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
+                    if (int rc = launch(ds->fn_vec[si], grid_for(s.n / 4, dev), 1, 1, 256, 1, 1, 0, stream, params))
+                        return rc;
+                    break;
+                }
                 if (int rc = launch(ds->fn[si], grid_for(s.n, dev), 1, 1, 256, 1, 1, 0, stream, params)) return rc;
                 break;
             }

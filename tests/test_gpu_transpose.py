@@ -71,3 +71,35 @@ def test_rank_n_transpose_is_exact(cuda, shape, perm, dtype):
     assert ("transpose2d" in k.describe()) == swap_last, k.describe()
     out = k(x)
     assert out.tobytes() == np.ascontiguousarray(np.transpose(x, perm)).tobytes()
+
+
+@pytest.mark.parametrize("shape,perm", [
+    ((4, 6, 8), (1, 0, 2)),            # innermost axis kept, length % 4 == 0: vector gather
+    ((16, 64, 128), (1, 0, 2)),
+    ((2, 3, 4, 8), (2, 0, 1, 3)),
+    ((3, 5, 7), (1, 0, 2)),            # length 7: element gather
+])
+@pytest.mark.parametrize("dtype", [np.float32, np.float64, np.float16])
+def test_gather_transposes_keeping_the_last_axis(cuda, shape, perm, dtype):
+    rng = np.random.default_rng(sum(shape))
+    x = rng.standard_normal(shape).astype(dtype)
+    g = GraphBuilder()
+    xi = g.add_input("X", x.shape, DT[x.dtype.type], 0)
+    g.set_output(g.add("transpose", [xi], perm=list(perm)))
+    k = bafe.compile_graph(g)
+    want = oracle.evaluate(g.to_list(), {xi: x}, g.output).reshape(np.transpose(x, perm).shape)
+    out = k(x)
+    assert out.tobytes() == want.tobytes()
+    if dtype != np.float16:
+        assert out.tobytes() == np.ascontiguousarray(np.transpose(x, perm)).tobytes()
+
+
+@pytest.mark.parametrize("src,dst", [((8,), (3, 8)), ((1, 12), (5, 12)), ((5, 1), (5, 8)), ((2, 1, 16), (2, 3, 16))])
+def test_broadcast_to(cuda, src, dst):
+    rng = np.random.default_rng(len(dst))
+    x = rng.standard_normal(src).astype(np.float32)
+    g = GraphBuilder()
+    xi = g.add_input("X", src, 0, 0)
+    g.set_output(g.add("broadcast_to", [xi], shape=list(dst)))
+    out = bafe.compile_graph(g)(x)
+    assert out.tobytes() == np.ascontiguousarray(np.broadcast_to(x, dst)).tobytes()
