@@ -142,6 +142,25 @@ CASES = [
          build=_ew3,
          inputs=[("X", (4096,), "float32", False, 0, SPECIAL(159)), ("Y", (4096,), "float32", False, 0, SPECIAL(160)),
                  ("Z", (4096,), "float32", False, 0, SPECIAL(161))]),
+    # ---- zero-size dimensions (shapes may hold 0: types.c:70-73; the
+    # emitted loops then run zero times over a zeroed node buffer) ----------
+    dict(name="empty_k_matmul_plus_c", cite="bafe/src/types.c:70-73, codegen.c:241-247 (K=0: relu(0 + C))",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (8, 0), "float32", False, 0, N01(162)), ("B", (0, 12), "float32", False, 0, N01(163)),
+                 ("C", (8, 12), "float32", False, 0, N01(164))]),
+    dict(name="empty_m_matmul", cite="bafe/src/types.c:70-73, codegen.c:241-247 (M=0)",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (0, 16), "float32", False, 0, N01(165)), ("B", (16, 12), "float32", False, 0, N01(166))]),
+    dict(name="empty_batch_matmul", cite="bafe/src/types.c:70-73, codegen.c:231-235 (batch of 0)",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (0, 4, 8), "float32", False, 0, N01(167)), ("B", (0, 8, 4), "float32", False, 0, N01(168))]),
+    dict(name="empty_ew_chain", cite="bafe/src/types.c:70-73, codegen.c:294-344 (n=0)",
+         build=_ew3,
+         inputs=[("X", (0,), "float32", False, 0, U11(169)), ("Y", (0,), "float32", False, 0, U11(170)),
+                 ("Z", (0,), "float32", False, 0, U11(171))]),
+    dict(name="empty_transpose", cite="bafe/src/types.c:70-73, codegen.c:360-369 (0x7 -> 7x0)",
+         build=lambda g, X: g.add("transpose", [X], perm=[1, 0]),
+         inputs=[("X", (0, 7), "float32", False, 0, N01(172))]),
     # ---- workload configs -----------------------------------------------------
     dict(name="cfg1_seed0", cite="benchmark configuration: relu(matmul(A,B)+C) 64x64x64",
          build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
