@@ -31,6 +31,9 @@ struct GemmArgs {
     i64 a_bstride, b_bstride, o_bstride;   // elements between batch items
     int a_col, b_col;                      // operand stored column-major
     const void* ep[8];                     // epilogue operands
+    i64 z0, y0;                            // first batch item / 64-row tile of this launch
+                                           // (a grid's y and z stop at 65535: larger
+                                           // problems take several launches)
 };
 
 // Spec (generated per step) provides the operand value types TA/TB, the
@@ -49,8 +52,8 @@ __device__ __forceinline__ void gemm_exact(const GemmArgs& g) {
     __shared__ __align__(16) TB Bs[32][68];   // Bs[k][n]
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
-    const i64 bz = blockIdx.z;
-    const i64 m0 = (i64)blockIdx.y * 64, n0 = (i64)blockIdx.x * 64;
+    const i64 bz = g.z0 + blockIdx.z;
+    const i64 m0 = (g.y0 + (i64)blockIdx.y) * 64, n0 = (i64)blockIdx.x * 64;
     const i64 M = g.M, N = g.N, K = g.K;
     const i64 aoff = bz * g.a_bstride, boff = bz * g.b_bstride;
 

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 #include <nvrtc.h>
 
+#include <algorithm>
 #include <cerrno>
 #include <cstdio>
 #include <cstdlib>
@@ -425,8 +426,9 @@ struct GemmArgsHost {
     int64_t a_bstride, b_bstride, o_bstride;
     int32_t a_col, b_col;
     const void* ep[8];
+    int64_t z0, y0;
 };
-static_assert(sizeof(GemmArgsHost) == 152, "GemmArgs layout");
+static_assert(sizeof(GemmArgsHost) == 168, "GemmArgs layout");
 struct GatherArgsHost {
     int64_t numel;
     int32_t rank;
@@ -515,10 +517,19 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 for (int k = 0; k < s.n_epi; ++k)
                     g.ep[k] = at_row(ptr_of(s.srcs[2 + k]), s.src_rb.empty() ? 0 : s.src_rb[2 + k]);
                 void* params[] = {&g};
-                if (s.batch > 65535 || (m_run + 63) / 64 > 65535) { set_error(8, "GEMM grid too large"); return 8; }
-                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 63) / 64), (unsigned)((m_run + 63) / 64),
-                                    (unsigned)s.batch, 256, 1, 1, 0, stream, params))
-                    return rc;
+                // grid (N tiles, M tiles, batch); y and z stop at 65535, so
+                // larger problems launch in blocks of 65535 (z0 / y0 offsets)
+                const int64_t kMaxYZ = 65535, m_tiles = (m_run + 63) / 64, nx = (s.N + 63) / 64;
+                if (nx > 0x7fffffff) { set_error(8, "GEMM grid too large"); return 8; }
+                for (int64_t z0 = 0; z0 < s.batch; z0 += kMaxYZ)
+                    for (int64_t y0 = 0; y0 < m_tiles; y0 += kMaxYZ) {
+                        g.z0 = z0;
+                        g.y0 = y0;
+                        const int64_t nz = std::min(kMaxYZ, s.batch - z0), ny = std::min(kMaxYZ, m_tiles - y0);
+                        if (int rc = launch(ds->fn[si], (unsigned)nx, (unsigned)ny, (unsigned)nz, 256, 1, 1, 0,
+                                            stream, params))
+                            return rc;
+                    }
                 break;
             }
             case StepKind::GemmTc: {
@@ -611,23 +622,35 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 // [r0, r0 + rows): x moved r0 columns (src_rb = one element),
                 // out moved r0 rows (dst_rb), x's row length stays s.M
                 if (m_run == 0 || s.N == 0 || s.batch < 1) break;
-                if (s.batch > 65535) { set_error(8, "transpose batch too large"); return 8; }
-                const void* x = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
-                int64_t M = m_run, Nn = s.N, ldx = s.M;
-                const unsigned nb = (unsigned)s.batch;
-                void* params[] = {&x, &dst, &M, &Nn, &ldx};
-                if (ds->fn_vec[si] && M % 4 == 0 && s.N % 4 == 0 && ldx % 4 == 0 &&
-                    ((uintptr_t)x | (uintptr_t)dst) % 16 == 0) {
-                    if ((M + 63) / 64 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                    if (int rc = launch(ds->fn_vec[si], (unsigned)((s.N + 63) / 64), (unsigned)((M + 63) / 64), nb,
-                                        256, 1, 1, 0, stream, params))
-                        return rc;
-                    break;
-                }
-                if ((M + 31) / 32 > 65535) { set_error(8, "transpose grid too large"); return 8; }
-                if (int rc = launch(ds->fn[si], (unsigned)((s.N + 31) / 32), (unsigned)((M + 31) / 32), nb, 32, 8, 1,
-                                    0, stream, params))
-                    return rc;
+                const char* x0 = (const char*)at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
+                char* d0 = (char*)dst;
+                const int64_t Nn = s.N, ldx = s.M, es = s.dst_esize;
+                const bool vec = ds->fn_vec[si] && m_run % 4 == 0 && Nn % 4 == 0 && ldx % 4 == 0 &&
+                                 ((uintptr_t)x0 | (uintptr_t)d0) % 16 == 0;
+                // grid (N tiles, M tiles, batch); y and z stop at 65535.
+                // Batch items go 65535 to a launch (base pointers moved by
+                // whole items, which keeps the 16-byte alignment above).  If
+                // M alone needs more than 65535 tiles, each item launches on
+                // its own in blocks of rows: x moves by columns, out by rows,
+                // ldx stays.
+                const int64_t kMaxYZ = 65535, tile = vec ? 64 : 32;
+                const int64_t m_tiles = (m_run + tile - 1) / tile;
+                if ((Nn + tile - 1) / tile > 0x7fffffff) { set_error(8, "transpose grid too large"); return 8; }
+                const int64_t rows_per = m_tiles > kMaxYZ ? kMaxYZ * tile : m_run;
+                const int64_t items_per = m_tiles > kMaxYZ ? 1 : kMaxYZ;
+                for (int64_t b0 = 0; b0 < s.batch; b0 += items_per)
+                    for (int64_t r0 = 0; r0 < m_run; r0 += rows_per) {
+                        const void* x = x0 + (b0 * ldx * Nn + r0) * es;
+                        void* o = d0 + (b0 * m_run + r0) * Nn * es;
+                        int64_t M = std::min(rows_per, m_run - r0);
+                        const unsigned nb = (unsigned)std::min(items_per, s.batch - b0);
+                        void* params[] = {&x, &o, &M, (void*)&Nn, (void*)&ldx};
+                        const int rc = vec ? launch(ds->fn_vec[si], (unsigned)((Nn + 63) / 64), (unsigned)((M + 63) / 64),
+                                                    nb, 256, 1, 1, 0, stream, params)
+                                           : launch(ds->fn[si], (unsigned)((Nn + 31) / 32), (unsigned)((M + 31) / 32),
+                                                    nb, 32, 8, 1, 0, stream, params);
+                        if (rc) return rc;
+                    }
                 break;
             }
             case StepKind::Gather: {

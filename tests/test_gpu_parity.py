@@ -178,3 +178,41 @@ def test_errors_do_not_poison_the_context(cuda):
     arrays = _inputs(meta, stored, False)
     out = k(*[arrays[meta["nodes"][i]["name"]] for i in meta["input_ids"]])
     assert out.tobytes() == golden.tobytes()
+
+
+@pytest.mark.parametrize("a_shape,b_shape,with_c", [
+    ((70000, 3, 5), (70000, 5, 2), False),    # 70000 batch items: two launches of <= 65535
+    ((4194368, 1), (1, 4), True),             # 65537 tiles of 64 rows
+])
+def test_exact_gemm_beyond_one_grid(cuda, a_shape, b_shape, with_c):
+    """The exact kernel's grid is (N tiles, M tiles, batch), and y and z stop
+    at 65535: larger problems run as several launches and still match the
+    oracle bit for bit.  Device-resident call, so that no host row panel
+    splits the problem."""
+    torch = cuda
+    from bafe_b200.graph import GraphBuilder
+    from oracle import oracle
+    bafe.set_option("gemm_precision", "exact")
+    rng = np.random.default_rng(11)
+    a = rng.standard_normal(a_shape).astype(np.float32)
+    b = rng.standard_normal(b_shape).astype(np.float32)
+    g = GraphBuilder()
+    ai, bi = g.add_input("A", a.shape, 0, 0), g.add_input("B", b.shape, 0, 0)
+    root = g.add("matmul", [ai, bi])
+    arrays = {ai: a, bi: b}
+    if with_c:
+        c = rng.standard_normal(a_shape[:-1] + b_shape[-1:]).astype(np.float32)
+        ci = g.add_input("C", c.shape, 0, 0)
+        root = g.add("relu", [g.add("add", [root, ci])])
+        arrays[ci] = c
+    g.set_output(root)
+    k = bafe.compile_graph(g)
+    assert k.describe().startswith("gemm.exact"), k.describe()
+    want = oracle.evaluate(g.to_list(), arrays, g.output)
+    dev = [torch.from_numpy(arrays[i]).cuda() for i in sorted(arrays)]
+    out = torch.empty(want.size, device="cuda")
+    before = bafe.launch_count()
+    k.run_torch(dev, out)
+    torch.cuda.synchronize()
+    assert bafe.launch_count() - before == 2
+    assert out.cpu().numpy().tobytes() == want.tobytes()

@@ -103,3 +103,29 @@ def test_broadcast_to(cuda, src, dst):
     g.set_output(g.add("broadcast_to", [xi], shape=list(dst)))
     out = bafe.compile_graph(g)(x)
     assert out.tobytes() == np.ascontiguousarray(np.broadcast_to(x, dst)).tobytes()
+
+
+@pytest.mark.parametrize("shape,perm", [
+    ((70000, 3, 5), (0, 2, 1)),        # scalar kernel, 70000 items: two launches of <= 65535
+    ((66000, 4, 8), (0, 2, 1)),        # 16-byte kernel, 66000 items
+    ((3, 2100000), (1, 0)),            # scalar kernel, 65625 row tiles of 32
+    ((4, 4200000), (1, 0)),            # 16-byte kernel, 65625 row tiles of 64
+])
+def test_transpose_beyond_one_grid(cuda, shape, perm):
+    """A grid's y and z stop at 65535: more batch items or row tiles than
+    that run as several launches, with the same bits as one would give.
+    Device-resident call, so that no host row panel splits the problem."""
+    torch = cuda
+    g = GraphBuilder()
+    xi = g.add_input("X", shape, 0, 0)
+    g.set_output(g.add("transpose", [xi], perm=list(perm)))
+    k = bafe.compile_graph(g)
+    assert "transpose2d" in k.describe()
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(shape, device="cuda", generator=gen)
+    out = torch.empty(x.numel(), device="cuda")
+    before = bafe.launch_count()
+    k.run_torch([x], out)
+    torch.cuda.synchronize()
+    assert bafe.launch_count() - before == 2
+    assert torch.equal(out, x.permute(*perm).contiguous().reshape(-1))
