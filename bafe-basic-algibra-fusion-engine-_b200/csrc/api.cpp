@@ -42,9 +42,13 @@ bafe_jit_stats g_stats = {0, 0, 0, 0};
 // gets a bare function pointer and calls f(in_0, ..., in_{n-1}, out).  Each
 // live plan is therefore bound to one of kSlots distinct functions; the
 // function reads the first n+1 pointer arguments (n = the plan's input
-// count, at most kMaxArgs-1) and runs the plan on them.
+// count, at most kMaxArgs-1) and runs the plan on them.  Plans with more
+// inputs are bound to the same slot in a second bank of functions that take
+// kMaxArgsWide pointers, so that a function never reads many more argument
+// slots than its caller passes.
 constexpr int kSlots = 256;          // the reference caches 256 kernels (jit.c:164)
 constexpr int kMaxArgs = 17;         // 16 inputs + out
+constexpr int kMaxArgsWide = 65;     // 64 inputs + out
 int g_slot_plan[kSlots];
 bool g_slots_init = false;
 
@@ -64,6 +68,40 @@ constexpr std::array<TrampolineFn, sizeof...(I)> make_trampolines(std::index_seq
     return {{&trampoline<(int)I>...}};
 }
 const std::array<TrampolineFn, kSlots> kTrampolines = make_trampolines(std::make_index_sequence<kSlots>{});
+
+template <size_t>
+using ArgPtr = void*;
+template <int S, class Seq>
+struct WideTrampoline;
+template <int S, size_t... I>
+struct WideTrampoline<S, std::index_sequence<I...>> {
+    static void fn(ArgPtr<I>... p) {
+        void* a[sizeof...(I)] = {p...};
+        run_slot(S, a);
+    }
+};
+template <int S>
+using WideOf = WideTrampoline<S, std::make_index_sequence<kMaxArgsWide>>;
+typedef decltype(&WideOf<0>::fn) WideFn;
+template <size_t... I>
+constexpr std::array<WideFn, sizeof...(I)> make_wide_trampolines(std::index_sequence<I...>) {
+    return {{&WideOf<(int)I>::fn...}};
+}
+const std::array<WideFn, kSlots> kWideTrampolines = make_wide_trampolines(std::make_index_sequence<kSlots>{});
+
+// The function handed out for a slot: the narrow bank up to 16 inputs.
+bafe_kernel_fn slot_function(int slot, int n_inputs) {
+    return n_inputs <= kMaxArgs - 1 ? reinterpret_cast<bafe_kernel_fn>(kTrampolines[slot])
+                                    : reinterpret_cast<bafe_kernel_fn>(kWideTrampolines[slot]);
+}
+// Slot of a handed-out function, either bank; -1 if it is none of them.
+int slot_of_function(bafe_kernel_fn fn) {
+    for (int i = 0; i < kSlots; ++i)
+        if (reinterpret_cast<bafe_kernel_fn>(kTrampolines[i]) == fn ||
+            reinterpret_cast<bafe_kernel_fn>(kWideTrampolines[i]) == fn)
+            return i;
+    return -1;
+}
 
 void init_slots() {
     if (g_slots_init) return;
@@ -116,9 +154,8 @@ Plan* find_plan(int id) { return plan_ptr(id); }
 int plan_id_of(bafe_kernel_fn fn) {
     if (!fn) return -1;
     init_slots();
-    for (int i = 0; i < kSlots; ++i)
-        if (reinterpret_cast<bafe_kernel_fn>(kTrampolines[i]) == fn) return g_slot_plan[i];
-    return -1;
+    const int slot = slot_of_function(fn);
+    return slot < 0 ? -1 : g_slot_plan[slot];
 }
 void drop_memory_cache() { drop_all_plans(); }
 
@@ -149,7 +186,7 @@ BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* 
         int slot = slot_of_plan(it->second);
         if (slot >= 0) {
             g_stats.hits++;
-            return reinterpret_cast<bafe_kernel_fn>(kTrampolines[slot]);
+            return slot_function(slot, plan_ptr(it->second)->n_inputs);
         }
     }
     g_stats.misses++;
@@ -161,8 +198,8 @@ BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* 
         g_stats.compile_failures++;
         return nullptr;
     }
-    if ((int)G.inputs.size() > kMaxArgs - 1) {
-        err = "graph has more than 16 inputs";
+    if ((int)G.inputs.size() > kMaxArgsWide - 1) {
+        err = "graph has more than 64 inputs (the kernel function takes at most 65 pointers)";
         write_err(err_buf, err_buf_size, err);
         set_error(2, err);
         g_stats.compile_failures++;
@@ -213,7 +250,7 @@ BAFE_API bafe_kernel_fn bafe_cuda_jit_get_or_compile(const bafe_graph* g, char* 
     g_plans.push_back(p);
     g_by_key[key] = p->id;
     g_slot_plan[slot] = p->id;
-    return reinterpret_cast<bafe_kernel_fn>(kTrampolines[slot]);
+    return slot_function(slot, p->n_inputs);
 }
 
 BAFE_API void bafe_cuda_jit_set_cache_dir(const char* dir) {
@@ -245,9 +282,8 @@ BAFE_API void bafe_cuda_jit_invalidate_memory_cache(void) {
 BAFE_API int bafe_cuda_plan_of(bafe_kernel_fn fn) {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     init_slots();
-    for (int i = 0; i < kSlots; ++i)
-        if (reinterpret_cast<bafe_kernel_fn>(kTrampolines[i]) == fn) return g_slot_plan[i];
-    return -1;
+    const int slot = slot_of_function(fn);
+    return slot < 0 ? -1 : g_slot_plan[slot];
 }
 
 BAFE_API int bafe_cuda_plan_num_inputs(int plan) {

@@ -199,8 +199,60 @@ struct Lowerer {
             fused_into[id] = c;
             mat[id] = 0;
         }
+        // Operand limits of the generated kernels: a region reads at most
+        // kRegionLeaves distinct operands, a GEMM epilogue at most
+        // kEpilogueLeaves (fixed-size parameter blocks).  Wider expressions
+        // are cut until every kernel fits: a GEMM whose epilogue would read
+        // too many writes its product to a buffer of its own instead, and
+        // an oversized region gets an internal node materialised: of the
+        // nodes whose own region then fits, the one that leaves the fewest
+        // operands to the rest (else the one that removes the most, and
+        // the rest is cut again).  The emitter gives every node
+        // a buffer anyway (codegen.c:188), so a cut adds a launch and
+        // leaves every value as it was.
+        for (bool changed = true; changed;) {
+            changed = false;
+            for (int id = 0; id < nn && !changed; ++id) {
+                if (!reach[id] || !ew[id] || !mat[id]) continue;
+                const Region R = collect_region(id);
+                if (R.acc >= 0) {
+                    const Op gop = N(R.acc).op;
+                    const size_t bias = (gop == Op::FusedMatmulBias || gop == Op::FusedMatmulBiasRelu) ? 1 : 0;
+                    if (R.leaves.size() + bias <= kEpilogueLeaves) continue;
+                    fused_into[R.acc] = -1;
+                    fused_gemm[id] = -1;
+                    mat[R.acc] = 1;
+                    changed = true;
+                    continue;
+                }
+                if (R.leaves.size() <= kRegionLeaves) continue;
+                int best = -1;
+                bool best_fits = false;
+                size_t best_n = R.leaves.size();
+                for (int x : R.order) {
+                    if (x == id) continue;
+                    mat[x] = 1;
+                    const size_t n = collect_region(id).leaves.size();
+                    const bool fits = collect_region(x).leaves.size() <= kRegionLeaves;
+                    mat[x] = 0;
+                    if (n >= R.leaves.size()) continue;            // removes nothing
+                    if ((fits && !best_fits) || (fits == best_fits && n < best_n)) {
+                        best = x;
+                        best_fits = fits;
+                        best_n = n;
+                    }
+                }
+                if (best >= 0) {
+                    mat[best] = 1;
+                } else {
+                    for (int x : R.order) if (x != id) mat[x] = 1;   // no single cut helps: one kernel per node
+                }
+                changed = true;
+            }
+        }
         return 0;
     }
+    static constexpr size_t kRegionLeaves = 16, kEpilogueLeaves = 8;
 
     // ------------------------------------------------------------ buffers --
     void assign_buffers() {
@@ -529,7 +581,7 @@ struct Lowerer {
             leaves.push_back({g.ch[2], ROW});
         }
         if (R) for (auto& l : R->leaves) leaves.push_back(l);
-        if (leaves.size() > 8) { err = "GEMM epilogue reads more than 8 operands"; return 2; }
+        if (leaves.size() > kEpilogueLeaves) { err = "GEMM epilogue reads more than 8 operands"; return 2; }
 
         // Tensor-core path choice.  f32 operands: tf32 MMAs (3xTF32 split by
         // default).  bf16 operands: kind::f16 MMAs -- the emitter converts
@@ -978,7 +1030,7 @@ struct Lowerer {
             if (ew[id]) {
                 Region R = collect_region(id);
                 if (R.acc >= 0) return emit_gemm(R.acc, &R);
-                if (R.leaves.size() > 16) { err = "elementwise region reads more than 16 operands"; return 2; }
+                if (R.leaves.size() > kRegionLeaves) { err = "elementwise region reads more than 16 operands"; return 2; }
                 return emit_ew(R);
             }
             switch (x.op) {

@@ -170,7 +170,7 @@ int bafe_cuda_jit_hash_graph(const bafe_graph *g, char *out, size_t out_size);
  * Lowers the graph to a plan of sm_100a kernels (generated CUDA compiled
  * once by NVRTC into a cubin, cached on disk by key), and returns a host
  * function pointer f(in_0, ..., in_{n-1}, out) taking host pointers, in the
- * graph's input order (g->inputs).  Returns NULL and writes a message into
+ * graph's input order (g->inputs; up to 64 inputs).  Returns NULL and writes a message into
  * err_buf on failure (unsupported graph, compile failure, no CUDA device).
  * The pointer stays valid until bafe_cuda_jit_clear /
  * bafe_cuda_jit_invalidate_memory_cache, like the reference's. */

@@ -216,3 +216,55 @@ def test_exact_gemm_beyond_one_grid(cuda, a_shape, b_shape, with_c):
     torch.cuda.synchronize()
     assert bafe.launch_count() - before == 2
     assert out.cpu().numpy().tobytes() == want.tobytes()
+
+
+@pytest.mark.parametrize("n,tree", [(20, False), (32, True), (40, False), (64, False)])
+def test_wide_elementwise_expressions_are_exact(cuda, n, tree):
+    """More operands than one region reads: the expression is cut into
+    several kernels and stays bit-exact; the call goes through the host
+    function BAFE receives (the wider function bank beyond 16 inputs)."""
+    from bafe_b200.graph import GraphBuilder
+    from oracle import oracle
+    rng = np.random.default_rng(n)
+    g = GraphBuilder()
+    ids = [g.add_input(f"X{i}", (3001,), 0, 0) for i in range(n)]
+    arrays = {i: rng.standard_normal(3001).astype(np.float32) for i in ids}
+    if tree:
+        level = list(ids)
+        while len(level) > 1:
+            level = [g.add("add", [level[i], level[i + 1]]) for i in range(0, len(level), 2)]
+        root = level[0]
+    else:
+        root = ids[0]
+        for k, i in enumerate(ids[1:]):
+            root = g.add("mul" if k % 5 == 4 else "add", [root, i])
+    g.set_output(g.add("relu", [root]))
+    k = bafe.compile_graph(g)
+    assert len(k.describe().strip().splitlines()) > 1
+    want = oracle.evaluate(g.to_list(), arrays, g.output)
+    out = k(*[arrays[i] for i in ids])
+    assert out.tobytes() == want.tobytes(), k.describe()
+
+
+def test_wide_gemm_epilogue_is_exact(cuda):
+    """A GEMM epilogue with more than 8 operands runs as GEMM + region, bit-exact."""
+    from bafe_b200.graph import GraphBuilder
+    from oracle import oracle
+    bafe.set_option("gemm_precision", "exact")
+    rng = np.random.default_rng(3)
+    g = GraphBuilder()
+    a = rng.standard_normal((96, 70)).astype(np.float32)
+    b = rng.standard_normal((70, 52)).astype(np.float32)
+    ai, bi = g.add_input("A", a.shape, 0, 0), g.add_input("B", b.shape, 0, 0)
+    arrays = {ai: a, bi: b}
+    r = g.add("matmul", [ai, bi])
+    for i in range(11):
+        ci = g.add_input(f"C{i}", (96, 52), 0, 0)
+        arrays[ci] = rng.standard_normal((96, 52)).astype(np.float32)
+        r = g.add("add", [r, ci])
+    g.set_output(g.add("relu", [r]))
+    k = bafe.compile_graph(g)
+    assert len(k.describe().strip().splitlines()) == 2, k.describe()
+    want = oracle.evaluate(g.to_list(), arrays, g.output)
+    out = k(*[arrays[i] for i in sorted(arrays)])
+    assert out.reshape(-1).tobytes() == want.tobytes()

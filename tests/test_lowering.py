@@ -163,3 +163,58 @@ def test_tc_convert_option_drops_the_residual_pre_pass():
         bafe.set_option("tc_convert", "auto")
     assert len(conv) == 1 and conv[0].startswith("gemm.tc.3xtf32")
     assert len(small) == 1 and small[0].startswith("gemm.tc.3xtf32")
+
+
+def _sum_chain(n, tree=False):
+    g = GraphBuilder()
+    ids = [g.add_input(f"X{i}", (1000,), 0, 0) for i in range(n)]
+    if tree:
+        while len(ids) > 1:
+            ids = [g.add("add", [ids[i], ids[i + 1]]) for i in range(0, len(ids), 2)]
+        root = ids[0]
+    else:
+        root = ids[0]
+        for i in ids[1:]:
+            root = g.add("add", [root, i])
+    g.set_output(root)
+    return g
+
+
+def _operands(step):
+    import re
+    return len(set(re.findall(r"\b(?:X\d+|C\d+|%\d+)\b", step)))
+
+
+@pytest.mark.parametrize("n,tree,kernels", [(20, False, 2), (40, False, 3), (32, True, 3), (64, False, 5)])
+def test_wide_expressions_are_cut_into_kernels_that_fit(n, tree, kernels):
+    """A region reads at most 16 operands: wider elementwise expressions are
+    cut at internal nodes (each becomes a buffer, as every node is in the
+    emitter), with few kernels."""
+    steps = bafe.compile_graph(_sum_chain(n, tree)).describe().strip().splitlines()
+    assert len(steps) == kernels, steps
+    assert all(s.startswith("ew ") and _operands(s) <= 16 for s in steps), steps
+
+
+def test_wide_gemm_epilogue_is_unfused():
+    """A GEMM epilogue reads at most 8 operands: a wider one leaves the
+    product in a buffer and runs as an elementwise region."""
+    def build(n):
+        g = GraphBuilder()
+        r = g.add("matmul", [g.add_input("A", (64, 32), 0, 0), g.add_input("B", (32, 48), 0, 0)])
+        for i in range(n):
+            r = g.add("add", [r, g.add_input(f"C{i}", (64, 48), 0, 0)])
+        g.set_output(g.add("relu", [r]))
+        return g
+    fused = bafe.compile_graph(build(7)).describe().strip().splitlines()
+    assert len(fused) == 1 and "epi=relu(" in fused[0]
+    split = bafe.compile_graph(build(10)).describe().strip().splitlines()
+    assert len(split) == 2 and "epi=acc -> tmp0" in split[0] and split[1].startswith("ew "), split
+
+
+def test_input_count_limit():
+    """The returned host function takes up to 64 inputs plus out (graphs with
+    more than 16 get a function of a wider bank); 65 inputs are refused."""
+    k = bafe.compile_graph(_sum_chain(64))
+    assert k.n_inputs == 64
+    with pytest.raises(RuntimeError, match="more than 64 inputs"):
+        bafe.compile_graph(_sum_chain(65))
