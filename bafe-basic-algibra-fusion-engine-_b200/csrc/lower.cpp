@@ -737,6 +737,10 @@ struct Lowerer {
         if (!tc_available()) return false;
         if (s.batch < 1 || s.batch > (1 << 20)) return false;
         if (s.M < 1 || s.N < 1 || s.K < 1) return false;
+        // tile origins and TMA coordinates are 32-bit, tile indices too
+        const int64_t lim = (int64_t(1) << 31) - 1024;
+        if (s.M > lim || s.N > lim || s.K > lim) return false;
+        if (((s.M + 255) / 256) * ((s.N + 255) / 256) * s.batch > lim) return false;
         const int64_t a_ld = s.a_col ? s.M : s.K;
         const int64_t b_ld = s.b_col ? s.K : s.N;
         if ((a_ld * esize) % 16 || (b_ld * esize) % 16) return false;

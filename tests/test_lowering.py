@@ -218,3 +218,16 @@ def test_input_count_limit():
     assert k.n_inputs == 64
     with pytest.raises(RuntimeError, match="more than 64 inputs"):
         bafe.compile_graph(_sum_chain(65))
+
+
+def test_gemm_beyond_32_bit_tile_coordinates_takes_the_exact_kernel():
+    """The tensor-core kernel keeps tile origins and TMA coordinates in 32
+    bits: a GEMM with ~2^31 rows (the exact kernel indexes in 64 bits and
+    launches in blocks of rows) is planned on the exact kernel."""
+    def plan(m):
+        g = GraphBuilder()
+        g.set_output(g.add("matmul", [g.add_input("A", (m, 64), 0, 0), g.add_input("B", (64, 64), 0, 0)]))
+        return bafe.compile_graph(g).describe().strip()
+    if gpu_available():
+        assert plan(1 << 20).startswith("gemm.tc")
+    assert plan((1 << 31) - 100).startswith("gemm.exact")
