@@ -289,7 +289,19 @@ struct DeviceState {
     // Wave-alignment counter of the tensor-core GEMMs (zeroed before each
     // launch that uses it; the plan's GEMMs run one after another).
     unsigned* tc_ctr = nullptr;
+    // Pinned host buffer of small host calls (kPackedCallBytes at most).
+    void* host_stage = nullptr;
+    size_t host_stage_bytes = 0;
+    // Pinned copy of the device error word, read on `stream` at the end of
+    // a host call (a synchronous read would add a blocking copy per call).
+    unsigned* err_host = nullptr;
 };
+
+// Host calls moving at most this many bytes in total copy through one
+// pinned buffer: a copy from pageable memory is a synchronous staged copy
+// with a fixed cost that dominates small calls; from pinned memory the
+// copies queue behind one another and run asynchronously.
+constexpr int64_t kPackedCallBytes = int64_t(256) << 10;
 
 // Timing events (pairs: before / after kernels) of a host call.
 static int ensure_timing_events(DeviceState* ds, size_t n) {
@@ -709,6 +721,15 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
 // A kernel whose bounded wait expired wrote a nonzero code into the
 // device's error word: report it (the output is not valid) and reset it.
 // The caller has synchronised the work in question.
+// A nonzero error word read back from device `dev`: clear it and report.
+static int report_error_word(int dev, unsigned code) {
+    if (!code) return 0;
+    cudaMemset(g_err_word[dev], 0, 4);
+    set_error(13, "tensor-core GEMM timed out waiting on a pipeline barrier (role code " + std::to_string(code) +
+                      "); the output is invalid");
+    return 13;
+}
+
 int check_device_error_word(int dev) {
     if (dev < 0 || dev >= 64 || !g_err_word[dev]) return 0;
     unsigned code = 0;
@@ -716,11 +737,7 @@ int check_device_error_word(int dev) {
         cudaGetLastError();
         return 0;
     }
-    if (!code) return 0;
-    cudaMemset(g_err_word[dev], 0, 4);
-    set_error(13, "tensor-core GEMM timed out waiting on a pipeline barrier (role code " + std::to_string(code) +
-                      "); the output is invalid");
-    return 13;
+    return report_error_word(dev, code);
 }
 
 int synchronize_current_device() {
@@ -949,9 +966,44 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
     const int panels = host_panel_count(p);
     if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels, resident, ready);
     if (ready) cudaStreamWaitEvent(ds->stream, (cudaEvent_t)ready, 0);   // resident inputs filled
+    // Small calls: the operands in pageable host memory pass through the
+    // pinned buffer, each at a 256-byte offset (one CPU copy per operand);
+    // pinned host and device pointers are copied from directly, as before.
+    std::vector<int64_t> stage_off(p.n_inputs + 1, -1);
+    {
+        auto pageable = [](const void* q) {
+            cudaPointerAttributes a;
+            if (cudaPointerGetAttributes(&a, q) != cudaSuccess) { cudaGetLastError(); return false; }
+            return a.type == cudaMemoryTypeUnregistered;
+        };
+        int64_t total = 0;
+        for (int k = 0; k <= p.n_inputs; ++k) {
+            const int64_t b = k < p.n_inputs ? ((resident && resident[k]) ? 0 : p.in_bytes[k]) : p.out_bytes;
+            if (b == 0 || !pageable(ptrs[k])) continue;
+            stage_off[k] = total;
+            total += (b + 255) / 256 * 256;
+        }
+        bool packed = total > 0 && total <= kPackedCallBytes;
+        if (packed && !ds->host_stage) {
+            if (cudaHostAlloc(&ds->host_stage, (size_t)kPackedCallBytes, cudaHostAllocDefault) == cudaSuccess) {
+                ds->host_stage_bytes = (size_t)kPackedCallBytes;
+            } else {
+                cudaGetLastError();
+                ds->host_stage = nullptr;
+                packed = false;   // direct copies instead
+            }
+        }
+        if (!packed) stage_off.assign(p.n_inputs + 1, -1);
+    }
+    char* const stage = (char*)ds->host_stage;
     for (int k = 0; k < p.n_inputs; ++k) {
         if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
-        cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], ptrs[k], (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
+        const void* src = ptrs[k];
+        if (stage_off[k] >= 0) {
+            memcpy(stage + stage_off[k], ptrs[k], (size_t)p.in_bytes[k]);
+            src = stage + stage_off[k];
+        }
+        cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], src, (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
         if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e)); return 7; }
     }
     std::vector<void*> dptrs(ds->in_stage);
@@ -965,9 +1017,25 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
         return rc;
     }
     cudaEventRecord(ds->tev[1], ds->stream);
+    const int64_t out_off = stage_off[p.n_inputs];
     if (p.out_bytes) {
-        cudaError_t e = cudaMemcpyAsync(ptrs[p.n_inputs], ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
+        void* to = out_off >= 0 ? (void*)(stage + out_off) : ptrs[p.n_inputs];
+        cudaError_t e = cudaMemcpyAsync(to, ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
         if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e)); return 7; }
+    }
+    // The device error word rides on the same stream into a pinned word.
+    const int edev = ds->device;
+    bool err_async = false;
+    if (edev >= 0 && edev < 64 && g_err_word[edev]) {
+        if (!ds->err_host && cudaHostAlloc((void**)&ds->err_host, 4, cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            ds->err_host = nullptr;
+        }
+        if (ds->err_host) {
+            *ds->err_host = 0;
+            err_async = cudaMemcpyAsync(ds->err_host, g_err_word[edev], 4, cudaMemcpyDeviceToHost, ds->stream) == cudaSuccess;
+            if (!err_async) cudaGetLastError();
+        }
     }
     cudaError_t e = cudaStreamSynchronize(ds->stream);
     if (e != cudaSuccess) {
@@ -975,8 +1043,9 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
         set_error(9, std::string("device error: ") + cudaGetErrorString(e));
         return 9;
     }
+    if (p.out_bytes && out_off >= 0) memcpy(ptrs[p.n_inputs], stage + out_off, (size_t)p.out_bytes);
     p.last_device_ms = timed_ms(ds, 1);
-    return check_device_error_word(ds->device);
+    return err_async ? report_error_word(edev, *ds->err_host) : check_device_error_word(edev);
 }
 
 int time_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v, int iters, double& ms) {
@@ -1030,6 +1099,8 @@ void release_plan_device_state(Plan& p) {
         if (s->out_stage) cudaFree(s->out_stage);
         if (s->tc_ws) cudaFree(s->tc_ws);
         if (s->tc_ctr) cudaFree(s->tc_ctr);
+        if (s->host_stage) cudaFreeHost(s->host_stage);
+        if (s->err_host) cudaFreeHost(s->err_host);
         for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }
         for (cudaEvent_t ev : s->events) cudaEventDestroy(ev);
         for (cudaEvent_t ev : s->tev) cudaEventDestroy(ev);

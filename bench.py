@@ -194,6 +194,16 @@ def time_steps(torch, kernel, ins, out, steps, warmup):
     return per, ev[0].elapsed_time(ev[steps]), launches
 
 
+class _NpPtr:
+    """A numpy array seen through time_e2e's data_ptr() (pageable host memory)."""
+
+    def __init__(self, a):
+        self.a = np.ascontiguousarray(a)
+
+    def data_ptr(self):
+        return self.a.ctypes.data
+
+
 def time_e2e(torch, kernel, host_ins, host_out, steps):
     """Host-pointer C-ABI calls (H2D + kernels + D2H + sync per call)."""
     ptrs = [t.data_ptr() for t in host_ins] + [host_out.data_ptr()]
@@ -643,9 +653,14 @@ def bench_configs(c: Ctx) -> dict:
         hins = [t.cpu().pin_memory() for t in ins]
         hout = torch.empty(*k.out_shape).pin_memory()
         e2e_ms = time_e2e(torch, k, hins, hout, 20)
+        # the same call on pageable numpy arrays, as BAFE's Python binding passes them
+        nins = [t.numpy().copy() for t in hins]   # a fresh (pageable) numpy allocation
+        nout = np.empty(tuple(k.out_shape), np.float32)
+        e2e_np_ms = time_e2e(torch, k, [_NpPtr(a) for a in nins], _NpPtr(nout), 20)
         ms = total / steps
         r = {"plan": k.describe().strip(), "device_us_per_call": round(dev_ms.value * 1e3, 2),
-             "python_loop_us_per_call": round(ms * 1e3, 2), "e2e_us_per_call": round(e2e_ms * 1e3, 1)}
+             "python_loop_us_per_call": round(ms * 1e3, 2), "e2e_us_per_call": round(e2e_ms * 1e3, 1),
+             "e2e_pageable_us_per_call": round(e2e_np_ms * 1e3, 1)}
         if flops:
             achieved = flops / (statistics.mean(per) * 1e-3) / 1e12
             basis = c.bf16_peak / 2.0 / (3.0 if "3xtf32" in r["plan"] else 1.0)

@@ -268,3 +268,30 @@ def test_wide_gemm_epilogue_is_exact(cuda):
     want = oracle.evaluate(g.to_list(), arrays, g.output)
     out = k(*[arrays[i] for i in sorted(arrays)])
     assert out.reshape(-1).tobytes() == want.tobytes()
+
+
+def test_small_host_calls_repeat_with_fresh_inputs(cuda):
+    """Small host calls copy pageable operands through a pinned buffer of
+    the plan and pinned ones directly: back-to-back calls with new inputs
+    (pageable and pinned mixed) each return their own result."""
+    torch = cuda
+    from bafe_b200.graph import GraphBuilder
+    from oracle import oracle
+    bafe.set_option("gemm_precision", "exact")
+    g = GraphBuilder()
+    ai, bi, ci = (g.add_input(n, (48, 40) if n == "A" else (40, 24) if n == "B" else (48, 24), 0, 0) for n in "ABC")
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [ai, bi]), ci])]))
+    k = bafe.compile_graph(g)
+    rng = np.random.default_rng(5)
+    for it in range(4):
+        a = rng.standard_normal((48, 40)).astype(np.float32)
+        b = rng.standard_normal((40, 24)).astype(np.float32)
+        c = rng.standard_normal((48, 24)).astype(np.float32)
+        want = oracle.evaluate(g.to_list(), {ai: a, bi: b, ci: c}, g.output)
+        if it % 2:
+            bp = torch.from_numpy(b).pin_memory()
+            out = np.empty((48, 24), np.float32)
+            k.call_host_ptrs([a.ctypes.data, bp.data_ptr(), c.ctypes.data, out.ctypes.data])
+        else:
+            out = k(a, b, c)
+        assert out.reshape(-1).tobytes() == want.tobytes(), it
