@@ -301,7 +301,7 @@ struct DeviceState {
 // pinned buffer: a copy from pageable memory is a synchronous staged copy
 // with a fixed cost that dominates small calls; from pinned memory the
 // copies queue behind one another and run asynchronously.
-constexpr int64_t kPackedCallBytes = int64_t(256) << 10;
+constexpr int64_t kPackedCallBytes = int64_t(1) << 20;
 
 // Timing events (pairs: before / after kernels) of a host call.
 static int ensure_timing_events(DeviceState* ds, size_t n) {
