@@ -11,6 +11,7 @@ import bafe_b200
 import cases
 from bafe_b200 import _binding
 from bafe_b200.graph import GraphBuilder
+from conftest import gpu_available
 from oracle import refbafe
 
 ROOT = Path(__file__).resolve().parent.parent
@@ -109,3 +110,24 @@ def test_options_roundtrip():
         bafe_b200.set_option("gemm_precision", "fp8")
     with pytest.raises(ValueError):
         bafe_b200.set_option("nonsense", "1")
+
+
+@pytest.mark.parametrize("n", [3, 20, 64])
+def test_host_function_reaches_its_plan_without_a_gpu(n):
+    """The returned function (17-pointer bank up to 16 inputs, 65-pointer
+    bank above) runs the plan of its own slot: on a machine without a GPU the
+    call records "no CUDA device" instead of failing silently or crashing."""
+    if gpu_available():
+        pytest.skip("covered by the GPU parity tests on a machine with a GPU")
+    import bafe_b200 as bafe
+    import numpy as np
+    g = GraphBuilder()
+    ids = [g.add_input(f"X{i}", (64,), 0, 0) for i in range(n)]
+    root = ids[0]
+    for i in ids[1:]:
+        root = g.add("add", [root, i])
+    g.set_output(root)
+    k = bafe.compile_graph(g)
+    xs = [np.ones(64, np.float32) for _ in range(n)]
+    with pytest.raises(RuntimeError, match="no CUDA device"):
+        k(*xs)
