@@ -38,6 +38,28 @@ __device__ __forceinline__ i64 add(i64 a, i64 b) { return (i64)((u64)a + (u64)b)
 __device__ __forceinline__ i64 sub(i64 a, i64 b) { return (i64)((u64)a - (u64)b); }
 __device__ __forceinline__ i64 mul(i64 a, i64 b) { return (i64)((u64)a * (u64)b); }
 
+// a + b with the NaN results of the host's scalar SSE add (`addss a, b`,
+// which the reference's sequential `acc += x` loops compile to): a NaN
+// operand propagates quieted, the first one winning, and an invalid sum
+// (inf - inf) gives the negative default NaN.  The device add returns one
+// canonical NaN instead, which differs in sign and payload bits.
+__device__ __forceinline__ float add_host_nan(float a, float b) {
+    const float r = __fadd_rn(a, b);
+    if (r == r) return r;
+    if (a != a) return __uint_as_float(__float_as_uint(a) | 0x00400000u);
+    if (b != b) return __uint_as_float(__float_as_uint(b) | 0x00400000u);
+    return __uint_as_float(0xffc00000u);
+}
+__device__ __forceinline__ double add_host_nan(double a, double b) {
+    const double r = __dadd_rn(a, b);
+    if (r == r) return r;
+    if (a != a) return __longlong_as_double(__double_as_longlong(a) | 0x0008000000000000ll);
+    if (b != b) return __longlong_as_double(__double_as_longlong(b) | 0x0008000000000000ll);
+    return __longlong_as_double((long long)0xfff8000000000000ull);
+}
+__device__ __forceinline__ i32 add_host_nan(i32 a, i32 b) { return add(a, b); }
+__device__ __forceinline__ i64 add_host_nan(i64 a, i64 b) { return add(a, b); }
+
 // sigmoid / tanh as emitted (codegen.c:345-356): `1.0f / (1.0f + expf(-x))`
 // and `tanhf(x)` -- float libm calls and float literals whatever the buffer
 // type, so the argument is converted to float first.  These go through

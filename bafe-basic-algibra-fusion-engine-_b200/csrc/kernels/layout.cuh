@@ -140,8 +140,9 @@ __device__ __forceinline__ void gather_nd_v4(const T* __restrict__ x, T* __restr
 // Single-axis reduction of an (M, N) tensor, sequential per output element
 // exactly as codegen.c:410-445 loops: axis 0 -> one output per column j
 // (consecutive threads read consecutive columns: coalesced), axis 1 -> one
-// output per row i.  Sum starts from 0; max starts from the first element
-// and replaces on a strict `>`.
+// output per row i.  Sum starts from 0 and accumulates with the host's NaN
+// results (acc first, as `out[i] += x[...]`); max starts from the first
+// element and replaces on a strict `>`.
 template <class T, bool IS_MAX>
 __device__ __forceinline__ void reduce_axis(const T* __restrict__ x, T* __restrict__ out,
                                             i64 M, i64 N, int axis) {
@@ -151,7 +152,7 @@ __device__ __forceinline__ void reduce_axis(const T* __restrict__ x, T* __restri
         T v = IS_MAX ? x[t] : (T)0;
         for (i64 i = IS_MAX ? 1 : 0; i < M; ++i) {
             const T e = x[i * N + t];
-            if (IS_MAX) { if (e > v) v = e; } else { v = add(v, e); }
+            if (IS_MAX) { if (e > v) v = e; } else { v = add_host_nan(v, e); }
         }
         out[t] = v;
     } else {
@@ -160,7 +161,7 @@ __device__ __forceinline__ void reduce_axis(const T* __restrict__ x, T* __restri
         T v = IS_MAX ? row[0] : (T)0;
         for (i64 j = IS_MAX ? 1 : 0; j < N; ++j) {
             const T e = row[j];
-            if (IS_MAX) { if (e > v) v = e; } else { v = add(v, e); }
+            if (IS_MAX) { if (e > v) v = e; } else { v = add_host_nan(v, e); }
         }
         out[t] = v;
     }

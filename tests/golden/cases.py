@@ -161,6 +161,46 @@ CASES = [
     dict(name="empty_transpose", cite="bafe/src/types.c:70-73, codegen.c:360-369 (0x7 -> 7x0)",
          build=lambda g, X: g.add("transpose", [X], perm=[1, 0]),
          inputs=[("X", (0, 7), "float32", False, 0, N01(172))]),
+    # ---- single-axis reductions, sequential per output (codegen.c:405-452) --
+    dict(name="reduce_sum_axis0", cite="bafe/src/codegen.c:419-428",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[0]),
+         inputs=[("X", (37, 53), "float32", False, 0, N01(173))]),
+    dict(name="reduce_sum_axis1", cite="bafe/src/codegen.c:429-434",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[1]),
+         inputs=[("X", (37, 53), "float32", False, 0, N01(174))]),
+    dict(name="reduce_sum_axis_neg1", cite="bafe/src/codegen.c:418 (axis % 2 of -1 is -1: the row branch)",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[-1]),
+         inputs=[("X", (16, 40), "float32", False, 0, N01(175))]),
+    dict(name="reduce_max_axis0", cite="bafe/src/codegen.c:424-427",
+         build=lambda g, X: g.add("reduce_max", [X], axes=[0]),
+         inputs=[("X", (37, 53), "float32", False, 0, N01(176))]),
+    dict(name="reduce_max_axis1_keepdims", cite="bafe/src/codegen.c:435-438, types.c:113-136",
+         build=lambda g, X: g.add("reduce_max", [X], axes=[1], keepdims=True),
+         inputs=[("X", (37, 53), "float32", False, 0, N01(177))]),
+    dict(name="reduce_sum_1d", cite="bafe/src/codegen.c:409-415",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[0]),
+         inputs=[("X", (1000,), "float32", False, 0, U11(178))]),
+    dict(name="reduce_max_1d_special_values", cite="bafe/src/codegen.c:413-415 (NaN / -0 / inf: first wins ties)",
+         build=lambda g, X: g.add("reduce_max", [X], axes=[0]),
+         inputs=[("X", (4096,), "float32", False, 0, SPECIAL(179))]),
+    dict(name="reduce_sum_rows_special_values", cite="bafe/src/codegen.c:429-434",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[1]),
+         inputs=[("X", (64, 64), "float32", False, 0, SPECIAL(180))]),
+    dict(name="reduce_sum_i32", cite="bafe/src/codegen.c:419-423",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[0]),
+         inputs=[("X", (50, 30), "int32", False, 0, RINT(181))]),
+    dict(name="reduce_max_f64", cite="bafe/src/codegen.c:435-438",
+         build=lambda g, X: g.add("reduce_max", [X], axes=[1]),
+         inputs=[("X", (20, 33), "float64", False, 0, N01(182))]),
+    dict(name="reduce_sum_of_relu", cite="bafe/src/codegen.c:338-344,429-434",
+         build=lambda g, X: g.add("reduce_sum", [g.add("relu", [X])], axes=[1]),
+         inputs=[("X", (48, 70), "float32", False, 0, N01(183))]),
+    dict(name="reduce_sum_two_axes_zero_fill", cite="bafe/src/codegen.c:442-451 (generic reduce: zero fill)",
+         build=lambda g, X: g.add("reduce_sum", [X], axes=[0, 1]),
+         inputs=[("X", (4, 6), "float32", False, 0, N01(184))]),
+    dict(name="reduce_max_rank3_zero_fill", cite="bafe/src/codegen.c:442-451 (generic reduce: zero fill)",
+         build=lambda g, X: g.add("reduce_max", [X], axes=[2]),
+         inputs=[("X", (3, 4, 5), "float32", False, 0, N01(185))]),
     # ---- workload configs -----------------------------------------------------
     dict(name="cfg1_seed0", cite="benchmark configuration: relu(matmul(A,B)+C) 64x64x64",
          build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
