@@ -1004,7 +1004,15 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
             src = stage + stage_off[k];
         }
         cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], src, (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
-        if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e)); return 7; }
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            // copies already queued may still read the pinned staging buffer:
+            // let them finish before the next call can overwrite it
+            cudaStreamSynchronize(ds->stream);
+            cudaGetLastError();
+            set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
+            return 7;
+        }
     }
     std::vector<void*> dptrs(ds->in_stage);
     for (int k = 0; k < p.n_inputs; ++k)
@@ -1021,7 +1029,13 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
     if (p.out_bytes) {
         void* to = out_off >= 0 ? (void*)(stage + out_off) : ptrs[p.n_inputs];
         cudaError_t e = cudaMemcpyAsync(to, ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
-        if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e)); return 7; }
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            cudaStreamSynchronize(ds->stream);
+            cudaGetLastError();
+            set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e));
+            return 7;
+        }
     }
     // The device error word rides on the same stream into a pinned word.
     const int edev = ds->device;

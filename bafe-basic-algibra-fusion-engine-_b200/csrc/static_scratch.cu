@@ -2,13 +2,14 @@
 // memory is a fixed array inside this library, so the call allocates
 // nothing.
 //
-// Who needs this: callers that cannot call cudaMalloc -- code running while
-// a CUDA stream is being captured into a graph, code under a strict memory
-// budget or custom allocator that forbids hidden device allocations, and
-// code that must not hit the implicit synchronisation cudaMalloc/cudaFree
-// can cause.  The regular plans keep their scratch (the tf32 residuals of A
-// and B) in device buffers the library allocates on first use; this entry
-// point puts it in g_scratch instead.
+// Who needs this: callers that cannot call cudaMalloc -- code under a
+// strict memory budget or a custom allocator that forbids hidden device
+// allocations, and code that must not hit the implicit device-wide
+// synchronisation cudaMalloc/cudaFree can cause.  The regular plans keep
+// their scratch (the tf32 residuals of A and B) in device buffers the
+// library allocates on first use; this entry point puts it in g_scratch
+// instead.  The call is synchronous: it waits for its stream and reads the
+// status word back before returning.
 //
 // Limits and sharing:
 //   * capacity kStaticScratchBytes (64 MiB): 256 bytes of status, then
@@ -119,16 +120,19 @@ extern "C" __attribute__((visibility("default"))) int bafe_cuda_gemm_3xtf32_stat
     void* stream) {
     if (!A || !B || !out) return fail(8, "null operand");
     if (M < 1 || N < 1 || K < 1) return fail(8, "M, N and K must be >= 1");
+    // Element counts are compared with the capacity before any product is
+    // formed, so no size can wrap around (M, N, K are each >= 1 here).
+    const int64_t cap_floats = (int64_t)((kStaticScratchBytes - kStatusBytes - 256) / 4);
+    if (M > cap_floats / K || N > cap_floats / K || M * K + K * N > cap_floats)
+        return fail(15, "problem needs more scratch than the static scratch holds: " +
+                            std::to_string((unsigned long long)kStaticScratchBytes) +
+                            " bytes (M*K + K*N <= " + std::to_string((long long)cap_floats) + " floats)");
     const int64_t a_ld = a_col ? M : K, b_ld = b_col ? K : N;
     if ((a_ld * 4) % 16 || (b_ld * 4) % 16 || N % 4)
         return fail(8, "tensor-core GEMM needs 16-byte row strides (A, B) and N % 4 == 0");
     const size_t a_bytes = (size_t)(M * K) * 4, b_bytes = (size_t)(K * N) * 4;
     const size_t a_off = kStatusBytes, b_off = a_off + ((a_bytes + 255) & ~size_t(255));
-    if (b_off + b_bytes > kStaticScratchBytes)
-        return fail(15, "problem needs " + std::to_string((unsigned long long)(b_off + b_bytes)) +
-                            " bytes of scratch; the static scratch holds " +
-                            std::to_string((unsigned long long)kStaticScratchBytes) +
-                            " (M*K + K*N <= ~16.7M floats)");
+    if (b_off + b_bytes > kStaticScratchBytes) return fail(15, "static scratch too small for this problem");
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();

@@ -382,10 +382,11 @@ int bafe_cuda_selftest_wait_timeout(int timeout_us, unsigned *code_out, double *
 /* out = A . B (fp32, 3xTF32 tensor cores, M x N row-major out) without any
  * device allocation.  No counterpart in the reference.
  *
- * For callers that cannot call cudaMalloc: code running during stream
- * capture, code with a strict memory budget or its own allocator that
- * forbids hidden device allocations, and code that must avoid the implicit
- * synchronisation of cudaMalloc / cudaFree.  The planned entry points keep
+ * For callers that cannot call cudaMalloc: code with a strict memory budget
+ * or its own allocator that forbids hidden device allocations, and code
+ * that must avoid the implicit device-wide synchronisation of cudaMalloc /
+ * cudaFree.  The call itself is synchronous: it waits for its stream and
+ * reads a status word back before returning.  The planned entry points keep
  * GEMM scratch (the tf32 residuals of A and B) in device buffers allocated
  * on first use; this one uses a 64 MiB array compiled into the library
  * (present on every GPU that loads it, until exit), so M*K + K*N must stay

@@ -35,11 +35,13 @@ def available() -> bool:
 
 
 def build() -> bool:
-    """Build oracle/_ref/libbafe.so from the reference sources when they are present."""
-    src = os.environ.get("BAFE_REF_SRC", "/root/reference/bafe")
+    """Build oracle/_ref/libbafe.so from the reference sources named by
+    $BAFE_REF_SRC (the reference's bafe/ directory); False when neither the
+    library nor the variable is there."""
     if REF_LIB.exists():
         return True
-    if not Path(src, "src").exists():
+    src = os.environ.get("BAFE_REF_SRC")
+    if not src or not Path(src, "src").exists():
         return False
     subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_SRC={src}"], check=True)
     return REF_LIB.exists()

@@ -82,7 +82,7 @@ def run_case(ref: refbafe.Reference, case: dict, cache: dict) -> None:
 
 def main() -> None:
     if not refbafe.build():
-        raise SystemExit("reference sources not found: cannot generate golden fixtures here")
+        raise SystemExit("reference library not built and BAFE_REF_SRC (the reference's bafe/ directory) not set")
     want = set(sys.argv[1:])
     with tempfile.TemporaryDirectory() as d:
         ref = refbafe.Reference(cache_dir=d)

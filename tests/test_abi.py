@@ -131,3 +131,16 @@ def test_host_function_reaches_its_plan_without_a_gpu(n):
     xs = [np.ones(64, np.float32) for _ in range(n)]
     with pytest.raises(RuntimeError, match="no CUDA device"):
         k(*xs)
+
+
+@pytest.mark.parametrize("M,N,K", [(1 << 31, 1 << 31, 1 << 31), (1 << 40, 4, 1 << 24), (4, 1 << 62, 2),
+                                   (4096, 4096, 4096)])
+def test_static_scratch_rejects_oversize_before_touching_the_device(M, N, K):
+    """The allocation-free GEMM compares element counts with its fixed
+    scratch capacity before forming any byte count, so sizes whose products
+    would wrap a 64-bit integer are refused too; nothing reaches the device
+    (the pointers here are never dereferenced)."""
+    fake = ctypes.c_void_p(256)
+    rc = _binding.lib.bafe_cuda_gemm_3xtf32_static_scratch(fake, fake, fake, M, N, K, 0, 0, None)
+    assert rc == 15
+    assert "static scratch" in _binding.last_error()[1]

@@ -1,8 +1,9 @@
 """The GEMM entry point that allocates no device memory.
 
 bafe_cuda_gemm_3xtf32_static_scratch serves callers that cannot call
-cudaMalloc (stream capture, strict memory budgets or custom allocators,
-code that must avoid cudaMalloc's implicit synchronisation): its scratch --
+cudaMalloc (strict memory budgets or custom allocators that forbid hidden
+device allocations, code that must avoid cudaMalloc's implicit device-wide
+synchronisation): its scratch --
 the tf32 residuals of A and B -- lives in a fixed 64 MiB array inside the
 library instead of device buffers allocated on first use.  These tests call
 it through the C ABI and compare it with the planned entry point
