@@ -374,7 +374,7 @@ double stream_time(const Rates& r, double bytes) {
 double step_seconds(const Step& s, const Rates& r, int gemm_dtype) {
     switch (s.kind) {
         case StepKind::Ew: {
-            double b = (double)s.n * s.dst_esize;
+            double b = (double)s.n * s.dst_esize * (s.has_dst2 ? 2 : 1);
             for (size_t k = 0; k < s.srcs.size(); ++k)
                 b += (double)(s.src_row[k] ? s.ncols : s.n) * s.src_esize[k];
             return stream_time(r, b);

@@ -96,6 +96,8 @@ struct Step {
     std::string kernel;            // entry point (extern "C") in the plan's module
     std::string kernel_vec;        // Ew: vectorised entry point ("" if none); GemmTc: split-tail fixup
     BufRef dst;
+    BufRef dst2;                   // Ew: a second output, same element count (has_dst2)
+    bool has_dst2 = false;
     std::vector<BufRef> srcs;      // operands in kernel argument order
     int64_t dst_bytes = 0;
     // Ew / Zero
@@ -113,7 +115,7 @@ struct Step {
     bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
     int tc_elem = 0;               // GemmTc operands: 0 = f32 (tf32 MMAs), 1 = bf16 (kind::f16)
     bool tc_convert = false;       // GemmTc 3xTF32: residuals made in shared memory (no aux buffers)
-    std::vector<BufRef> aux;       // GemmTc 3xtf32: residual buffers of A and B
+    std::vector<BufRef> aux;       // GemmTc 3xtf32: A_lo, B_lo, B_hi (the operand parts the pre-passes write)
     // Row streaming of host calls (analyse_row_streaming): the step runs
     // once per row panel of the output (panel) or once per call; buffers
     // with a nonzero byte count per row are offset to the panel's first row.

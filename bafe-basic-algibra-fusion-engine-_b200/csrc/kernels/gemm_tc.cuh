@@ -29,13 +29,18 @@
 // error a random walk over chunks (~KC * K^0.5), inside the 3xTF32 bound.
 //
 // kind::tf32 reads the top 19 bits of each fp32 operand (the low 13
-// mantissa bits are ignored), so for 3xTF32 the raw operand is its own
-// "hi" part and only lo = x - trunc_tf32(x) is computed; each k-step issues
-//     A.B += A.B + A.B_lo + A_lo.B        (three MMAs, all on the tensor core)
-// By default a streaming pre-pass (bafe::tf32_residual) writes lo to
-// memory and TMA loads both halves.  With CONVERT the producer loads only
-// the raw operands and the accumulate threads write lo into the stage's
-// second half in shared memory (elementwise, so the swizzle needs no index
+// mantissa bits are ignored).  3xTF32 operands: A's raw values are its
+// "hi" part (truncated by the tensor core) and A_lo = rn_tf32(x -
+// trunc_tf32(x)); B is split to nearest, B_hi = rn_tf32(x), B_lo =
+// rn_tf32(x - B_hi), so the dropped A_lo.B_lo term has no systematic sign
+// (with both sides truncated it always had the product's sign and biased
+// sums toward zero: mean error -1.9e-9 at 16384^3, now ~0).  Each k-step
+//     acc += A.B_lo + A_lo.B_hi, then acc += A.B_hi   (three MMAs)
+// By default streaming pre-passes (tf32_residual for A, tf32_split for B)
+// write the parts to memory and TMA loads them.  With CONVERT the producer
+// loads only the raw operands and the accumulate threads write the parts
+// into the stage in shared memory (lo into the second half, B_hi over the
+// raw B; elementwise, so the swizzle needs no index
 // mapping), releasing each stage to the MMA issuer on LO(s): no pre-pass,
 // no scratch, half the operand bytes from L2 and HBM -- but 64 KB more
 // shared-memory traffic per k-block and CTA, which costs throughput on B200.
@@ -138,12 +143,38 @@ __device__ __forceinline__ void fadd2_rn(float& a0, float& a1, u32 b0, u32 b1) {
         : "+f"(a0), "+f"(a1) : "r"(b0), "r"(b1));
 }
 
-// Residual of the tf32 truncation: x - (x with the low 13 mantissa bits
-// cleared), exact in fp32; 0 for inf / NaN (whose hi part carries them).
+// x rounded to the nearest tf32 value (ties to even on the 10-bit
+// mantissa; the low 13 bits come out clear).  Rounding the bit pattern's
+// magnitude is symmetric in the sign.  A value whose rounding would
+// overflow is truncated instead (it stays finite; a residual carries the
+// rest); inf and NaN are returned unchanged.
+__device__ __forceinline__ float tf32_rn(float x) {
+    const u32 b = __float_as_uint(x);
+    if ((b & 0x7F800000u) == 0x7F800000u) return x;
+    const u32 r = (b + 0x0FFFu + ((b >> 13) & 1u)) & 0xFFFFE000u;
+    return __uint_as_float((r & 0x7F800000u) == 0x7F800000u ? (b & 0xFFFFE000u) : r);
+}
+
+// Residual of the tf32 truncation, x - (x with the low 13 mantissa bits
+// cleared) -- exact in fp32 -- rounded to the nearest tf32 value, so the
+// tensor core, which ignores those 13 bits, reads it rounded rather than
+// truncated.  0 for inf / NaN (the raw operand, the hi part, carries them).
+// Used where the raw operand itself is the hi part (kind::tf32 truncates
+// it); lo then has the sign of x.
 __device__ __forceinline__ float tf32_lo(float x) {
     const u32 bits = __float_as_uint(x);
     if ((bits & 0x7F800000u) == 0x7F800000u) return 0.0f;
-    return __fsub_rn(x, __uint_as_float(bits & 0xFFFFE000u));
+    return tf32_rn(__fsub_rn(x, __uint_as_float(bits & 0xFFFFE000u)));
+}
+
+// Round-to-nearest split x ~ hi + lo: hi = tf32_rn(x), lo = tf32_rn(x - hi)
+// (x - hi is exact in fp32).  |lo| <= 2^-11 |x| and its sign is independent
+// of x's, so the dropped lo_a * lo_b product of the 3xTF32 scheme no longer
+// has the sign of a * b (with a truncated hi on both sides it always did,
+// which biased every sum toward zero).
+__device__ __forceinline__ void tf32_split(float x, float& hi, float& lo) {
+    hi = tf32_rn(x);
+    lo = ((__float_as_uint(x) & 0x7F800000u) == 0x7F800000u) ? 0.0f : tf32_rn(__fsub_rn(x, hi));
 }
 
 namespace tc {
@@ -290,21 +321,41 @@ __device__ __forceinline__ void sts128(u32 addr, uint4 v) {
 // at (ct + i * NT) * 16 bytes) from `hi` to the same offsets at `lo`, four
 // chunks per round (four shared-memory loads in flight; the callers hold
 // 128 accumulators, so a wider round spills).
-template <int PER, int NT>
+// The first A_PER rounds cover the stage's A tile: the raw operand stays
+// the hi part and lo = tf32_lo(x).  The remaining rounds cover B: hi and lo
+// come from the round-to-nearest split (tf32_split) and hi is written back
+// over the raw operand -- the same operands the pre-pass gives the kernel.
+template <int PER, int NT, int A_PER>
 __device__ __forceinline__ void convert_stage(u32 hi, u32 lo, int ct) {
     constexpr int R = 4;
-    static_assert(PER % R == 0, "rounds of four chunks");
+    static_assert(PER % R == 0 && A_PER % R == 0, "rounds of four chunks");
 #pragma unroll
     for (int r = 0; r < PER; r += R) {
         uint4 v[R];
 #pragma unroll
         for (int j = 0; j < R; ++j) v[j] = lds128(hi + 16u * (u32)(ct + (r + j) * NT));
+        if (r < A_PER) {
 #pragma unroll
-        for (int j = 0; j < R; ++j) {
-            v[j].x = __float_as_uint(tf32_lo(__uint_as_float(v[j].x)));
-            v[j].y = __float_as_uint(tf32_lo(__uint_as_float(v[j].y)));
-            v[j].z = __float_as_uint(tf32_lo(__uint_as_float(v[j].z)));
-            v[j].w = __float_as_uint(tf32_lo(__uint_as_float(v[j].w)));
+            for (int j = 0; j < R; ++j) {
+                v[j].x = __float_as_uint(tf32_lo(__uint_as_float(v[j].x)));
+                v[j].y = __float_as_uint(tf32_lo(__uint_as_float(v[j].y)));
+                v[j].z = __float_as_uint(tf32_lo(__uint_as_float(v[j].z)));
+                v[j].w = __float_as_uint(tf32_lo(__uint_as_float(v[j].w)));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < R; ++j) {
+                float h[4], l[4];
+                tf32_split(__uint_as_float(v[j].x), h[0], l[0]);
+                tf32_split(__uint_as_float(v[j].y), h[1], l[1]);
+                tf32_split(__uint_as_float(v[j].z), h[2], l[2]);
+                tf32_split(__uint_as_float(v[j].w), h[3], l[3]);
+                sts128(hi + 16u * (u32)(ct + (r + j) * NT),
+                       make_uint4(__float_as_uint(h[0]), __float_as_uint(h[1]), __float_as_uint(h[2]),
+                                  __float_as_uint(h[3])));
+                v[j] = make_uint4(__float_as_uint(l[0]), __float_as_uint(l[1]), __float_as_uint(l[2]),
+                                  __float_as_uint(l[3]));
+            }
         }
 #pragma unroll
         for (int j = 0; j < R; ++j) sts128(lo + 16u * (u32)(ct + (r + j) * NT), v[j]);
@@ -786,22 +837,32 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                         const u32 b_hi = a_hi + A_BYTES;
                         const u32 a_lo = a_hi + A_BYTES + B_BYTES;
                         const u32 b_lo = a_lo + A_BYTES;
+                        // 3xTF32: the k-block's eight cross-term MMAs (hi.lo,
+                        // lo.hi) go first, then its four hi.hi MMAs, so the
+                        // small terms are summed while the accumulator is
+                        // small (its additions truncate: fewer full-size
+                        // truncations per chunk; measured rms error -25 %).
+                        // K-major: 32 B further along the row; MN-major:
+                        // the next 8 (tf32) / 16 (bf16) k-rows.
+                        if (SPLIT) {
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
+                                const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
+                                const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                                E::mma(d, smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt),
+                                       smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt), idesc, acc);
+                                E::mma(d, smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt),
+                                       smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt), idesc, 1u);
+                            }
+                        }
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
-                            // K-major: 32 B further along the row; MN-major:
-                            // the next 8 (tf32) / 16 (bf16) k-rows.
                             const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
                             const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
-                            const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
-                            const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
-                            const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
-                            E::mma(d, ah, bh, idesc, acc);
-                            if (SPLIT) {
-                                const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
-                                const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
-                                E::mma(d, ah, bl, idesc, 1u);
-                                E::mma(d, al, bh, idesc, 1u);
-                            }
+                            const u32 acc = (SPLIT || kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                            E::mma(d, smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt), smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt),
+                                   idesc, acc);
                         }
                         tc_commit(EMPTY(s));           // stage free once these MMAs finish
                         if (++s == STAGES) { s = 0; phase ^= 1u; }
@@ -841,7 +902,8 @@ __device__ __forceinline__ void gemm_tc(const TcArgs& g) {
                 while (conv < target) {
                     if (!wait(FULL(cs), cph, sh, g, 5u)) return false;
                     const u32 hi = base + cs * STAGE_BYTES;
-                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS>(hi, hi + A_BYTES + B_BYTES, at);
+                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS, A_BYTES / 16 / ACC_THREADS>(
+                        hi, hi + A_BYTES + B_BYTES, at);
                     fence_async_smem();                    // visible to the tensor core
                         mbar_arrive(LO(cs));
                     if (++cs == STAGES) { cs = 0; cph ^= 1u; }
@@ -1102,20 +1164,26 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                         const u32 b_hi = a_hi + A_BYTES;
                         const u32 a_lo = a_hi + A_BYTES + B_BYTES;
                         const u32 b_lo = a_lo + A_BYTES;
+                        // 3xTF32: cross terms first, then hi.hi (see gemm_tc)
+                        if (SPLIT) {
+#pragma unroll
+                            for (int kk = 0; kk < 4; ++kk) {
+                                const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
+                                const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
+                                const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                                E::mma_pair(d, smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt),
+                                            smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt), idesc, acc);
+                                E::mma_pair(d, smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt),
+                                            smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt), idesc, 1u);
+                            }
+                        }
 #pragma unroll
                         for (int kk = 0; kk < 4; ++kk) {
                             const u32 ao = g.a_mn ? kk * E::MN_KK : kk * 32u;
                             const u32 bo = g.b_mn ? kk * E::MN_KK : kk * 32u;
-                            const u64 ah = smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt);
-                            const u64 bh = smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt);
-                            const u32 acc = (kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
-                            E::mma_pair(d, ah, bh, idesc, acc);
-                            if (SPLIT) {
-                                const u64 al = smem_desc(a_lo + ao, a_lbo, a_sbo, a_lt);
-                                const u64 bl = smem_desc(b_lo + bo, b_lbo, b_sbo, b_lt);
-                                E::mma_pair(d, ah, bl, idesc, 1u);
-                                E::mma_pair(d, al, bh, idesc, 1u);
-                            }
+                            const u32 acc = (SPLIT || kb > c * KB_PER_CHUNK || kk > 0) ? 1u : 0u;
+                            E::mma_pair(d, smem_desc(a_hi + ao, a_lbo, a_sbo, a_lt),
+                                        smem_desc(b_hi + bo, b_lbo, b_sbo, b_lt), idesc, acc);
                         }
                         tc_commit_pair(EMPTY(s));      // both CTAs' stage s is free
                         if (++s == STAGES) { s = 0; phase ^= 1u; }
@@ -1154,7 +1222,8 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 while (conv < target) {
                     if (!wait(FULL(cs), cph, sh, g, 5u)) return false;
                     const u32 hi = base + cs * STAGE_BYTES;
-                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS>(hi, hi + A_BYTES + B_BYTES, at);
+                    convert_stage<(A_BYTES + B_BYTES) / 16 / ACC_THREADS, ACC_THREADS, A_BYTES / 16 / ACC_THREADS>(
+                        hi, hi + A_BYTES + B_BYTES, at);
                     fence_async_smem();                    // visible to the tensor core
                         if (cta == 0) mbar_arrive(LO(cs));
                         else mbar_arrive_cluster(LO(cs), 0u);

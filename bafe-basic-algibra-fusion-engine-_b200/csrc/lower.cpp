@@ -696,10 +696,14 @@ struct Lowerer {
             s.src_row.push_back(l.access == ROW);
         }
         if (s.kind == StepKind::GemmTc && s.tc_variant == 3 && !s.tc_convert) {
-            // 3xTF32 residual operands lo = x - trunc_tf32(x), written once
-            // per call by a streaming pre-pass into plan scratch.
+            // 3xTF32 operand parts, written once per call by streaming
+            // pre-passes into plan scratch: A_lo = rn_tf32(x - trunc_tf32(x))
+            // (A's raw values are its hi part); B split to nearest, B_lo and
+            // B_hi (bafe::tf32_split).
             s.aux.push_back(emit_residual(s.srcs[0], M * K * a_items, "A"));
-            s.aux.push_back(emit_residual(s.srcs[1], K * Nn * b_items, "B"));
+            BufRef b_hi;
+            s.aux.push_back(emit_residual(s.srcs[1], K * Nn * b_items, "B", &b_hi));
+            s.aux.push_back(b_hi);
         }
         if (s.kind == StepKind::GemmExact) {
             src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel
@@ -749,8 +753,11 @@ struct Lowerer {
     }
     static bool tc_available();
 
-    // Streaming pre-pass writing the tf32 residual of an f32 buffer.
-    BufRef emit_residual(const BufRef& from, int64_t n, const char* what) {
+    // Streaming pre-pass over an f32 buffer: writes its tf32 residual
+    // (bafe::tf32_lo: the raw values stay the hi part) or, when hi_out is
+    // given, its round-to-nearest split (bafe::tf32_split): lo to the step's
+    // output, hi to a second output.
+    BufRef emit_residual(const BufRef& from, int64_t n, const char* what, BufRef* hi_out = nullptr) {
         Step s;
         s.kind = StepKind::Ew;
         s.n = n;
@@ -758,25 +765,39 @@ struct Lowerer {
         s.dst = new_tmp(n * 4);
         s.dst_esize = 4;
         s.dst_bytes = n * 4;
+        if (hi_out) {
+            s.dst2 = new_tmp(n * 4);
+            s.has_dst2 = true;
+            *hi_out = s.dst2;
+        }
         s.srcs.push_back(from);
         s.src_esize.push_back(4);
         s.src_row.push_back(false);
-        s.kernel = kname("tf32_residual");
+        s.kernel = kname(hi_out ? "tf32_split" : "tf32_residual");
         s.kernel_vec = s.kernel + "_v4";
-        src << "\nstruct P_" << s.kernel << " { const float* __restrict__ in0; float* __restrict__ out; i64 n; i64 ncols; };\n"
+        // per element: hi (split only) and lo of x
+        auto body = [&](const std::string& x, const std::string& hi, const std::string& lo) -> std::string {
+            if (!hi_out) return lo + " = bafe::tf32_lo(" + x + ");";
+            return "{ float h_, l_; bafe::tf32_split(" + x + ", h_, l_); " + hi + " = h_; " + lo + " = l_; }";
+        };
+        src << "\nstruct P_" << s.kernel << " { const float* __restrict__ in0; float* __restrict__ out; i64 n; i64 ncols;"
+            << (hi_out ? " float* __restrict__ out2;" : "") << " };\n"
             << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel << "(const P_" << s.kernel << " p) {\n"
             << "  for (i64 i = (i64)blockIdx.x * blockDim.x + threadIdx.x; i < p.n; i += (i64)gridDim.x * blockDim.x)\n"
-            << "    p.out[i] = bafe::tf32_lo(p.in0[i]);\n}\n"
+            << "    " << body("p.in0[i]", "p.out2[i]", "p.out[i]") << "\n}\n"
             << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel_vec << "(const P_" << s.kernel << " p) {\n"
             << "  const i64 ng = p.n >> 2;\n"
             << "  for (i64 g = (i64)blockIdx.x * blockDim.x + threadIdx.x; g < ng; g += (i64)gridDim.x * blockDim.x) {\n"
-            << "    const auto v = bafe::ld4(p.in0 + 4 * g);\n    bafe::Vec4<float> r;\n"
-            << "#pragma unroll\n    for (int l = 0; l < 4; ++l) r.v[l] = bafe::tf32_lo(v.v[l]);\n"
-            << "    bafe::st4(p.out + 4 * g, r);\n  }\n"
+            << "    const auto v = bafe::ld4(p.in0 + 4 * g);\n    bafe::Vec4<float> r, rh;\n"
+            << "#pragma unroll\n    for (int l = 0; l < 4; ++l) " << body("v.v[l]", "rh.v[l]", "r.v[l]") << "\n"
+            << "    bafe::st4(p.out + 4 * g, r);\n"
+            << (hi_out ? "    bafe::st4(p.out2 + 4 * g, rh);\n" : "") << "  }\n"
             << "  const i64 t = (i64)blockIdx.x * blockDim.x + threadIdx.x;\n"
-            << "  if (t < 4 && (ng << 2) + t < p.n) p.out[(ng << 2) + t] = bafe::tf32_lo(p.in0[(ng << 2) + t]);\n}\n";
-        s.describe = std::string("ew n=") + std::to_string((long long)n) + " float tf32_residual(" + what + ") -> " +
-                     bufname(s.dst);
+            << "  if (t < 4 && (ng << 2) + t < p.n) "
+            << body("p.in0[(ng << 2) + t]", "p.out2[(ng << 2) + t]", "p.out[(ng << 2) + t]") << "\n}\n";
+        s.describe = std::string("ew n=") + std::to_string((long long)n) + " float " +
+                     (hi_out ? "tf32_split(" : "tf32_residual(") + what + ") -> " + bufname(s.dst) +
+                     (hi_out ? " (lo), " + bufname(s.dst2) + " (hi)" : "");
         P.steps.push_back(s);
         return s.dst;
     }

@@ -509,6 +509,11 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 args.push_back((uint64_t)(uintptr_t)dst);
                 args.push_back((uint64_t)n_run);
                 args.push_back((uint64_t)s.ncols);
+                if (s.has_dst2) {                            // second output: same rows as dst
+                    void* d2 = at_row(ptr_of(s.dst2), s.dst_rb);
+                    if ((uintptr_t)d2 % 16) vec = false;
+                    args.push_back((uint64_t)(uintptr_t)d2);
+                }
                 void* params[] = {args.data()};
                 int64_t units = vec ? n_run / 4 : n_run;
                 if (int rc = launch(vec ? ds->fn_vec[si] : ds->fn[si], grid_for(units, dev), 1, 1, 256, 1, 1, 0,
@@ -554,6 +559,8 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 const void* a_lo = s.aux.size() > 0 ? at_row(ptr_of(s.aux[0]), s.aux_rb.empty() ? 0 : s.aux_rb[0]) : nullptr;
                 const void* b_lo = s.aux.size() > 1 ? ptr_of(s.aux[1]) : nullptr;
                 const void* a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
+                // 3xTF32 reads B's round-to-nearest hi part, written by the split pre-pass
+                const void* b = s.aux.size() > 2 ? ptr_of(s.aux[2]) : ptr_of(s.srcs[1]);
                 if (ds->tc_cache.size() != p.steps.size()) ds->tc_cache.assign(p.steps.size(), DeviceState::TcCached());
                 DeviceState::TcCached& cached = ds->tc_cache[si];
                 Step panel;                                  // the step over this call's rows
@@ -582,13 +589,13 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                     if (cudaMalloc(&c, sizeof(unsigned)) == cudaSuccess) ds->tc_ctr = static_cast<unsigned*>(c);
                     else cudaGetLastError();                    // no alignment then
                 }
-                const void* key[15] = {a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, err_word};
+                const void* key[15] = {a, b, a_lo, b_lo, dst, err_word};
                 for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
                 key[14] = ds->tc_ws;
                 bool hit = cached.valid && cached.rows == m_run;
                 for (int k = 0; hit && k < 15; ++k) hit = cached.key[k] == key[k];
                 if (!hit) {
-                    int rc = tc_prepare(run, a, ptr_of(s.srcs[1]), a_lo, b_lo, dst, ep, sm_count(dev), err_word,
+                    int rc = tc_prepare(run, a, b, a_lo, b_lo, dst, ep, sm_count(dev), err_word,
                                         ds->fn_vec[si] ? ds->tc_ws : nullptr, ds->tc_ws_bytes, ds->tc_ctr, cached.L, err);
                     if (rc) {
                         cached.valid = false;

@@ -18,7 +18,9 @@
 //       - GEMM (batch 1, M = rows): A splits with K elements per row (A must
 //         be row-major so a panel is contiguous), B stays whole, epilogue
 //         operands split with N per row (full) or stay whole (row vector);
-//         the 3xTF32 residual of A splits like A, the one of B stays whole;
+//         the 3xTF32 residual of A splits like A, the parts of B (lo, hi)
+//         stay whole; an elementwise step with a second output writes it
+//         row for row with its first;
 //   * a step whose destination is whole runs once, before the panels, and
 //     needs every operand whole;
 //   * any other step kind with a split destination, or a buffer needed both
@@ -89,12 +91,14 @@ void analyse_row_streaming(Plan& P, const Shape& out_shape) {
         if (drb == 0) {   // runs once per call: every operand whole
             for (auto& b : s.srcs) need(b, 0);
             for (auto& b : s.aux) need(b, 0);
+            if (s.has_dst2) need(s.dst2, 0);
             continue;
         }
         s.panel = true;
         s.dst_rb = drb;
         switch (s.kind) {
             case StepKind::Ew: {
+                if (s.has_dst2) need(s.dst2, drb);   // written row for row with dst
                 if (s.n % R) { ok = false; break; }
                 const int64_t e = s.n / R;
                 if (e * s.dst_esize != drb) { ok = false; break; }
@@ -124,10 +128,11 @@ void analyse_row_streaming(Plan& P, const Shape& out_shape) {
                     s.src_rb[k] = s.src_row[k] ? 0 : s.N * s.src_esize[k];
                     need(s.srcs[k], s.src_rb[k]);
                 }
-                if (s.aux.size() == 2) {
+                if (s.aux.size() == 3) {               // A_lo splits like A; B_lo, B_hi stay whole
                     s.aux_rb[0] = s.K * 4;
                     need(s.aux[0], s.aux_rb[0]);
                     need(s.aux[1], 0);
+                    need(s.aux[2], 0);
                 } else if (!s.aux.empty()) {
                     ok = false;
                 }

@@ -75,7 +75,7 @@ def parse():
     p.add_argument("--precision", default=os.environ.get("BAFE_GEMM_PRECISION", "auto"))
     p.add_argument("--e2e-steps", type=int, default=3, help="0 skips the host-pointer measurement")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--only", choices=["gemm", "gemm_bf16", "ew", "transpose"], default=None,
+    p.add_argument("--only", choices=["gemm", "gemm_tf32", "gemm_bf16", "ew", "transpose"], default=None,
                    help="run one workload (profiling); prints its own line")
     p.add_argument("--gemm-size", type=int, default=GEMM_M, help="M=N=K (profiling smaller cases)")
     p.add_argument("--ew-elements", type=int, default=EW_N)
@@ -148,6 +148,25 @@ class Clocks:
 
 
 # ------------------------------------------------------------ workloads --
+
+def gemm_config(S: int) -> dict:
+    """The headline workload's `config`, identical in both arms."""
+    return {"workload": f"relu(matmul(A,B)+C) M=N=K={S} fp32, A row-major, B BLOCKED tag, "
+                        f"A, B, C i.i.d. N(0, 1/sqrt(K)) (std 1/{int(round(math.sqrt(S)))})",
+            "l2": "inputs larger than L2 (1 GiB each); no flush" if S >= 8192 else "inputs smaller than L2"}
+
+
+def roofline_basis(c, clocks: dict, div: float):
+    """(peak, basis name, burst peak, sustained peak) for a tensor-core
+    kernel whose rate is the bf16 peak / div.  A timed region whose median
+    SM clock stayed within 5 % of the maximum ran as a burst; one the power
+    cap held lower is measured against the sustained (power-capped) peak."""
+    burst, sustained = c.bf16_peak / div, c.bf16_sustained / div
+    med, mx = clocks.get("sm_mhz"), clocks.get("sm_max_mhz")
+    if med and mx and med >= 0.95 * mx:
+        return burst, "burst", burst, sustained
+    return sustained, "sustained", burst, sustained
+
 
 def gemm_graph(m_rows: int, size: int = GEMM_N):
     import bafe_b200 as bafe
@@ -253,30 +272,57 @@ def traffic_from_profiles(name: str):
 
 
 # ------------------------------------------------------- CPU baselines --
+# The reference's own generated C kernels, built and run through its public
+# C API (oracle/refgraph.py builds the graphs with the reference's graph
+# functions; oracle/refbafe.py optimizes, JITs and calls).  None of these
+# import the B200 backend.
+
+def _ref_kernel(build, cache: str | None = None):
+    """build(builder) -> root, with inputs named as the caller's arrays.
+    Returns (reference, kernel address, input names in call order, stack bytes)."""
+    import tempfile
+    from oracle import refbafe, refgraph
+    ref = refbafe.Reference(cache_dir=cache or tempfile.mkdtemp(prefix="bafe_ref_"))
+    b = refgraph.Builder(ref.lib)
+    b.output(build(b))
+    opt = ref.optimize(b.graph)
+    fn = ref.compile(opt)
+    nodes = refbafe.graph_nodes(opt)
+    names = [nodes[opt.inputs[i]]["name"] for i in range(opt.n_inputs)]
+    return ref, fn, names, refbafe.stack_bytes_for(nodes)
+
+
+def _ref_time(build, arrays: dict, out: np.ndarray, reps: int, cache: str | None = None) -> float:
+    """Seconds per call of the reference kernel (one warm call first)."""
+    ref, fn, names, stack = _ref_kernel(build, cache)
+    call = [arrays[n] for n in names]
+    ref.call_kernel(fn, call, out, stack_bytes=stack)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        ref.call_kernel(fn, call, out, stack_bytes=stack)
+    return (time.perf_counter() - t0) / reps
+
+
+def _build_gemm_relu_add(rows: int, S: int):
+    def build(b):
+        a = b.input("A", (rows, S))
+        bb = b.input("B", (S, S), layout=2)          # BLOCKED tag, row-major storage
+        c = b.input("C", (rows, S))
+        return b.add("relu", [b.add("add", [b.add("matmul", [a, bb]), c])])
+    return build
+
 
 def cpu_baseline_gemm(A_rows: np.ndarray, B: np.ndarray, C_rows: np.ndarray):
-    """The reference's generated kernel on a row panel (1 core)."""
+    """The reference's generated kernel on a row panel of the 16384^3
+    problem (1 core): 32 rows, one of the emitter's row tiles
+    (MATMUL_TILE, codegen.c:23), so B streams once per 32 rows as in the
+    full-size run."""
     from oracle import refbafe
     rows = A_rows.shape[0]
     flops = 2.0 * rows * GEMM_N * GEMM_K
+    out = np.zeros((rows, GEMM_N), np.float32)
     if refbafe.available():
-        from bafe_b200.graph import GraphBuilder
-        import tempfile
-        ref = refbafe.Reference(cache_dir=tempfile.mkdtemp(prefix="bafe_ref_"))
-        g = GraphBuilder()
-        a = g.add_input("A", A_rows.shape, 0, 0)
-        b = g.add_input("B", B.shape, 0, 2)
-        c = g.add_input("C", C_rows.shape, 0, 0)
-        g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
-        opt = ref.optimize(g.graph)
-        fn = ref.compile(opt)
-        nodes = refbafe.graph_nodes(opt)
-        byname = {"A": A_rows, "B": B, "C": C_rows}
-        call = [byname[nodes[opt.inputs[i]]["name"]] for i in range(opt.n_inputs)]
-        out = np.zeros((rows, GEMM_N), np.float32)
-        t0 = time.perf_counter()
-        ref.call_kernel(fn, call, out, stack_bytes=refbafe.stack_bytes_for(nodes))
-        dt = time.perf_counter() - t0
+        dt = _ref_time(_build_gemm_relu_add(rows, GEMM_N), {"A": A_rows, "B": B, "C": C_rows}, out, 1)
         kind = "reference"
     else:
         from oracle import oracle
@@ -289,28 +335,18 @@ def cpu_baseline_gemm(A_rows: np.ndarray, B: np.ndarray, C_rows: np.ndarray):
             "sample": f"{rows}-row panel of relu(matmul(A,B)+C) 16384^3 ({flops / 1e9:.1f} GFLOP, {dt:.2f} s)"}
 
 
+def _build_ew(n: int):
+    def build(b):
+        x, y, z = (b.input(nm, (n,)) for nm in "XYZ")
+        return b.add("relu", [b.add("add", [b.add("mul", [x, y]), z])])
+    return build
+
+
 def cpu_baseline_ew(x: np.ndarray, y: np.ndarray, z: np.ndarray):
     from oracle import refbafe
     n = x.size
     if refbafe.available():
-        from bafe_b200.graph import GraphBuilder
-        import tempfile
-        ref = refbafe.Reference(cache_dir=tempfile.mkdtemp(prefix="bafe_ref_"))
-        g = GraphBuilder()
-        ids = [g.add_input(nm, (n,), 0, 0) for nm in "XYZ"]
-        g.set_output(g.add("relu", [g.add("add", [g.add("mul", [ids[0], ids[1]]), ids[2]])]))
-        opt = ref.optimize(g.graph)
-        fn = ref.compile(opt)
-        nodes = refbafe.graph_nodes(opt)
-        byname = {"X": x, "Y": y, "Z": z}
-        call = [byname[nodes[opt.inputs[i]]["name"]] for i in range(opt.n_inputs)]
-        out = np.zeros(n, np.float32)
-        ref.call_kernel(fn, call, out, stack_bytes=refbafe.stack_bytes_for(nodes))   # warm
-        t0 = time.perf_counter()
-        reps = 3
-        for _ in range(reps):
-            ref.call_kernel(fn, call, out, stack_bytes=refbafe.stack_bytes_for(nodes))
-        dt = (time.perf_counter() - t0) / reps
+        dt = _ref_time(_build_ew(n), {"X": x, "Y": y, "Z": z}, np.zeros(n, np.float32), 3)
         kind = "reference"
     else:
         from oracle import oracle
@@ -321,6 +357,26 @@ def cpu_baseline_ew(x: np.ndarray, y: np.ndarray, z: np.ndarray):
         kind = "port"
     return {"value": 16.0 * n / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
             "sample": f"{n} elements of relu(add(mul(X,Y),Z)) ({dt * 1e3:.1f} ms per call)"}
+
+
+def cpu_baseline_transpose(x: np.ndarray):
+    """The reference's generated transpose kernel (codegen.c:360-369) on a
+    column panel: X[:, c0:c1] stored contiguously, transposed to rows."""
+    from oracle import refbafe
+    rows, cols = x.shape
+    if refbafe.available():
+        def build(b):
+            return b.add("transpose", [b.input("X", (rows, cols))], perm=[1, 0])
+        dt = _ref_time(build, {"X": x}, np.zeros((cols, rows), np.float32), 3)
+        kind = "reference"
+    else:
+        from oracle import oracle
+        t0 = time.perf_counter()
+        oracle.transpose2d(x, cols, rows)
+        dt = time.perf_counter() - t0
+        kind = "port"
+    return {"value": 8.0 * x.size / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
+            "sample": f"{rows}x{cols} column panel ({dt * 1e3:.1f} ms per call)"}
 
 
 # ------------------------------------------------------------ our arm --
@@ -403,27 +459,25 @@ def bench_gemm(c: Ctx) -> dict:
     kern_ms = statistics.mean(per)
     achieved = 2.0 * rows * S * S / (kern_ms * 1e-3) / 1e12
     tc3 = "3xtf32" in plan
-    # The timed region is a long back-to-back loop of GEMMs (the power cap
-    # holds the clock down), so the sustained bf16 figure is the basis; the
-    # burst-based fraction is reported beside it.
-    div = 2.0 * (3.0 if tc3 else 1.0)
-    peak = c.bf16_sustained / div
-    peak_burst = c.bf16_peak / div
+    # tf32 MMAs run at half the bf16 rate; 3xTF32 issues three per product
+    peak, basis, peak_burst, peak_sus = roofline_basis(c, clocks, 2.0 * (3.0 if tc3 else 1.0))
     res = {
         "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C))",
         "value": round(flops_total / (ms_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
         "ms_per_step": round(ms_step, 4),
         "dtype": "fp32 via 3xtf32" if tc3 else ("tf32" if "tc.tf32" in plan else "fp32"),
-        "config": {"workload": f"relu(matmul(A,B)+C) M=N=K={S} fp32, A row-major, B BLOCKED tag",
-                   "parallelism": f"M-row panels x{c.world}, B broadcast once (outside timed region)",
-                   "l2": "inputs larger than L2 (1 GiB each); no flush" if S >= 8192 else "inputs smaller than L2",
-                   "plan": plan, "precision_option": args.precision},
+        "config": gemm_config(S),
+        "run": {"parallelism": f"M-row panels x{c.world}, B broadcast once (outside the timed region)",
+                "plan": plan, "precision_option": args.precision},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 2), "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(f"gemm_{S}"),
-                     "peak_basis": f"{c.peak_src} sustained bf16 {c.bf16_sustained} TFLOP/s / 2 (tf32 rate)"
-                                   + (" / 3 (three products)" if tc3 else ""),
+                     "peak_basis": f"{c.peak_src} {basis} bf16 TFLOP/s / 2 (tf32 rate)"
+                                   + (" / 3 (three products)" if tc3 else "")
+                                   + f"; {basis} because the timed region's median SM clock was "
+                                   + f"{clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz",
                      "frac_of_burst": round(achieved / peak_burst, 4),
-                     "achieved_over": "CUDA events around each step of the plan (tf32 residual pre-passes + GEMM)"
+                     "frac_of_sustained": round(achieved / peak_sus, 4),
+                     "achieved_over": "CUDA events around each step of the plan (tf32 pre-passes + GEMM)"
                                       if tc3 else "CUDA events around each step of the plan"},
         "gpu_launches": launches, "clocks": clocks, "b_broadcast_ms": round(bcast_ms, 3),
         "compile_s": round(t_compile, 2),
@@ -448,10 +502,10 @@ def bench_gemm(c: Ctx) -> dict:
                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": float(4 * out.numel()) * c.world,
                       "ms_per_step": round(e2e_ms, 2), "path": path}
         if c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
-            res["cpu_baseline"] = cpu_baseline_gemm(hA[:8].numpy(), hB.numpy(), hC[:8].numpy())
+            res["cpu_baseline"] = cpu_baseline_gemm(hA[:32].numpy(), hB.numpy(), hC[:32].numpy())
         del hA, hB, hC, hO
     elif c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
-        res["cpu_baseline"] = cpu_baseline_gemm(A[:8].cpu().numpy(), B.cpu().numpy(), C[:8].cpu().numpy())
+        res["cpu_baseline"] = cpu_baseline_gemm(A[:32].cpu().numpy(), B.cpu().numpy(), C[:32].cpu().numpy())
     return res
 
 
@@ -484,17 +538,81 @@ def bench_gemm_bf16(c: Ctx) -> dict:
     total = c.max(total)
     ms = total / args.steps
     achieved = 2.0 * rows * S * S / (statistics.mean(per) * 1e-3) / 1e12
+    clocks = ck.summary()
+    peak, basis, burst, sus = roofline_basis(c, clocks, 1.0)
     return {
         "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C), bf16 operands and output)",
         "value": round(2.0 * S ** 3 / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
         "dtype": "bf16 (f32 accumulate)",
         "config": {"workload": f"relu(matmul(A,B)+C) M=N=K={S} bf16, A row-major, B BLOCKED tag",
-                   "parallelism": f"M-row panels x{c.world}, B broadcast once", "plan": k.describe().strip(),
                    "l2": "inputs larger than L2; no flush" if S >= 8192 else "inputs smaller than L2"},
-        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": c.bf16_sustained, "unit": "TFLOP/s",
-                     "frac": round(achieved / c.bf16_sustained, 4), "frac_of_burst": round(achieved / c.bf16_peak, 4),
-                     "traffic": None, "peak_basis": f"{c.peak_src} sustained bf16 (cuBLAS)"},
-        "gpu_launches": int(c.sum(launches)), "clocks": ck.summary(),
+        "run": {"parallelism": f"M-row panels x{c.world}, B broadcast once", "plan": k.describe().strip()},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "frac_of_burst": round(achieved / burst, 4),
+                     "frac_of_sustained": round(achieved / sus, 4), "traffic": None,
+                     "peak_basis": f"{c.peak_src} {basis} bf16 (cuBLAS); {basis} because the timed region's median "
+                                   f"SM clock was {clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz"},
+        "gpu_launches": int(c.sum(launches)), "clocks": clocks,
+    }
+
+
+def bench_gemm_tf32(c: Ctx) -> dict:
+    """The headline workload with gemm_precision=tf32 (one kind::tf32 MMA
+    per product): throughput against the TF32 peak, and its measured
+    relative error against fp64 on rank 0's first rows:
+    max |out - fp64| / (|A| |B|) elementwise (the bound the tests state is
+    2^-9: two operand truncations to tf32's 10-bit mantissa)."""
+    import bafe_b200 as bafe
+    torch, args = c.torch, c.args
+    from bafe_b200.parallel import broadcast_resident, row_panels
+    S = args.gemm_size
+    std = 1.0 / math.sqrt(S)
+    r0, r1 = row_panels(S, c.world)[c.rank]
+    rows = r1 - r0
+    A = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
+    C = torch.randn(rows, S, device=c.dev, generator=c.gen) * std
+    B = torch.randn(S, S, device=c.dev, generator=torch.Generator(device=c.dev).manual_seed(99)) * std
+    if c.dist is not None:
+        broadcast_resident(B, c.dist, src=0)
+    out = torch.empty(rows, S, device=c.dev)
+    old = bafe.get_option("gemm_precision")
+    bafe.set_option("gemm_precision", "tf32")
+    try:
+        k = bafe.compile_graph(gemm_graph(rows, S))
+    finally:
+        bafe.set_option("gemm_precision", old)
+    plan = k.describe().strip()
+    c.barrier()
+    with Clocks(c.local) as ck:
+        per, total, launches = time_steps(torch, k, [A, B, C], out, args.steps, args.warmup)
+    c.barrier()
+    total = c.max(total)
+    ms = total / args.steps
+    achieved = 2.0 * rows * S * S / (statistics.mean(per) * 1e-3) / 1e12
+    clocks = ck.summary()
+    peak, basis, burst, sus = roofline_basis(c, clocks, 2.0)
+    # accuracy on 16 rows: fp64 product on the device
+    Bd = B.double()
+    ref = torch.relu(A[:16].double() @ Bd + C[:16].double())
+    scale = A[:16].double().abs() @ Bd.abs()
+    err = (out[:16].double() - ref).abs()
+    rel = float((err / scale).max())
+    del Bd, scale
+    return {
+        "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C), 1xTF32)",
+        "value": round(2.0 * S ** 3 / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+        "dtype": "tf32 (f32 accumulate)",
+        "config": gemm_config(S),
+        "run": {"parallelism": f"M-row panels x{c.world}, B broadcast once", "plan": plan,
+                "precision_option": "tf32"},
+        "accuracy": {"max_abs_err_vs_fp64": float(err.max()), "max_rel_err_vs_fp64": rel,
+                     "rel_err": "max over 16 rows of |out - fp64| / (|A| |B|)", "rel_tolerance": 2.0 ** -9},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 4), "frac_of_burst": round(achieved / burst, 4),
+                     "frac_of_sustained": round(achieved / sus, 4), "traffic": None,
+                     "peak_basis": f"{c.peak_src} {basis} bf16 TFLOP/s / 2 (tf32 rate); {basis} because the timed "
+                                   f"region's median SM clock was {clocks.get('sm_mhz')} of {clocks.get('sm_max_mhz')} MHz"},
+        "gpu_launches": int(c.sum(launches)), "clocks": clocks,
     }
 
 
@@ -540,39 +658,6 @@ def bench_ew(c: Ctx) -> dict:
             m = min(1 << 24, n_local)
             res["cpu_baseline"] = cpu_baseline_ew(hX[:m].numpy(), hY[:m].numpy(), hZ[:m].numpy())
     return res
-
-
-def cpu_baseline_transpose(x: np.ndarray):
-    """The reference's generated transpose kernel (codegen.c:360-369) on a
-    column panel: X[:, c0:c1] stored contiguously, transposed to rows."""
-    from oracle import refbafe
-    rows, cols = x.shape
-    if refbafe.available():
-        import tempfile
-        from bafe_b200.graph import GraphBuilder
-        ref = refbafe.Reference(cache_dir=tempfile.mkdtemp(prefix="bafe_ref_"))
-        g = GraphBuilder()
-        xi = g.add_input("X", (rows, cols), 0, 0)
-        g.set_output(g.add("transpose", [xi], perm=[1, 0]))
-        opt = ref.optimize(g.graph)
-        fn = ref.compile(opt)
-        nodes = refbafe.graph_nodes(opt)
-        out = np.zeros((cols, rows), np.float32)
-        ref.call_kernel(fn, [x], out, stack_bytes=refbafe.stack_bytes_for(nodes))   # warm
-        t0 = time.perf_counter()
-        reps = 3
-        for _ in range(reps):
-            ref.call_kernel(fn, [x], out, stack_bytes=refbafe.stack_bytes_for(nodes))
-        dt = (time.perf_counter() - t0) / reps
-        kind = "reference"
-    else:
-        from oracle import oracle
-        t0 = time.perf_counter()
-        oracle.transpose2d(x, cols, rows)
-        dt = time.perf_counter() - t0
-        kind = "port"
-    return {"value": 8.0 * x.size / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": kind,
-            "sample": f"{rows}x{cols} column panel ({dt * 1e3:.1f} ms per call)"}
 
 
 def bench_transpose(c: Ctx) -> dict:
@@ -625,18 +710,21 @@ def bench_transpose(c: Ctx) -> dict:
     return res
 
 
-def bench_configs(c: Ctx) -> dict:
+def bench_configs(c: Ctx, cpu: bool = True) -> dict:
     """The other configurations of the reference's benchmark set, on one GPU
     (rank 0; they are too small to shard): relu(matmul(A,B)+C) at 64^3,
     matmul at 256^3 with B row- and column-major (launch-latency bound:
     microseconds per call, no roofline claim), and relu(add(matmul(A,B),
-    mul(C,D))) at 4096^3 (tensor-core bound)."""
+    mul(C,D))) at 4096^3 (tensor-core bound).  Each entry carries the
+    reference's generated C kernel timed on the same host (1 core, the same
+    inputs; 4096^3 on a 32-row panel, one of the emitter's row tiles,
+    scaled to the full problem by its row count)."""
     import bafe_b200 as bafe
     torch = c.torch
     g0 = torch.Generator(device=c.dev).manual_seed(5)
     out = {}
 
-    def run(name, g, shapes, steps, flops=None):
+    def run(name, g, ref_build, names, shapes, steps, flops, ref_rows=None):
         import ctypes
         from bafe_b200._binding import lib
         k = bafe.compile_graph(g)
@@ -660,32 +748,74 @@ def bench_configs(c: Ctx) -> dict:
         ms = total / steps
         r = {"plan": k.describe().strip(), "device_us_per_call": round(dev_ms.value * 1e3, 2),
              "python_loop_us_per_call": round(ms * 1e3, 2), "e2e_us_per_call": round(e2e_ms * 1e3, 1),
-             "e2e_pageable_us_per_call": round(e2e_np_ms * 1e3, 1)}
-        if flops:
-            achieved = flops / (statistics.mean(per) * 1e-3) / 1e12
-            basis = c.bf16_peak / 2.0 / (3.0 if "3xtf32" in r["plan"] else 1.0)
-            r.update({"value": round(flops / (ms * 1e-3) / 1e12, 1), "unit": "TFLOP/s",
-                      "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(basis, 1),
-                                   "unit": "TFLOP/s", "frac": round(achieved / basis, 4),
-                                   "peak_basis": f"{c.peak_src} burst bf16 / 2 (tf32 rate)"
-                                                 + (" / 3 (three products)" if "3xtf32" in r["plan"] else "")}})
+             "e2e_pageable_us_per_call": round(e2e_np_ms * 1e3, 1),
+             "tflops_device": round(flops / (dev_ms.value * 1e-3) / 1e12, 3),
+             "tflops_e2e": round(flops / (e2e_ms * 1e-3) / 1e12, 4)}
+        if "gemm.tc" in r["plan"]:
+            achieved = flops / (dev_ms.value * 1e-3) / 1e12
+            div = 2.0 * (3.0 if "3xtf32" in r["plan"] else 1.0)
+            r["roofline"] = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(c.bf16_peak / div, 1),
+                             "unit": "TFLOP/s", "frac": round(achieved / (c.bf16_peak / div), 4),
+                             "peak_basis": f"{c.peak_src} burst bf16 / 2 (tf32 rate)"
+                                           + (" / 3 (three products)" if "3xtf32" in r["plan"] else "")
+                                           + " (back-to-back calls of a few ms run at the burst clock)"}
+        from oracle import refbafe
+        if cpu and refbafe.available():
+            arrays = dict(zip(names, nins))
+            if ref_rows:
+                full_rows = shapes[0][0]
+                arrays = {n: (np.ascontiguousarray(a[:ref_rows]) if n in ("A", "C", "D") else a)
+                          for n, a in arrays.items()}
+                ref_out = np.zeros((ref_rows, k.out_shape[1]), np.float32)
+                dt = _ref_time(ref_build(ref_rows), arrays, ref_out, 1) * full_rows / ref_rows
+                sample = f"{ref_rows}-row panel, scaled by {full_rows // ref_rows} to the full problem"
+            else:
+                ref_out = np.zeros(tuple(k.out_shape), np.float32)
+                reps = max(3, min(50, int(0.5 / max(flops / 2e9, 1e-4))))
+                dt = _ref_time(ref_build(None), arrays, ref_out, reps)
+                sample = f"the full problem, mean of {reps} calls"
+            r["cpu_baseline"] = {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s",
+                                 "us_per_call": round(dt * 1e6, 1), "cores": 1, "kind": "reference",
+                                 "sample": sample}
         out[name] = r
 
     g = bafe.GraphBuilder()
     a, b, cc = (g.add_input(n, (64, 64), 0, 0) for n in "ABC")
     g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), cc])]))
-    run("cfg1 relu(matmul(A,B)+C) 64^3", g, [(64, 64)] * 3, 200)
+
+    def ref_cfg1(_rows):
+        def build(rb):
+            x, y, z = (rb.input(n, (64, 64)) for n in "ABC")
+            return rb.add("relu", [rb.add("add", [rb.add("matmul", [x, y]), z])])
+        return build
+    run("cfg1 relu(matmul(A,B)+C) 64^3", g, ref_cfg1, "ABC", [(64, 64)] * 3, 200, 2.0 * 64 ** 3)
     for col in (0, 1):
         g = bafe.GraphBuilder()
         a = g.add_input("A", (256, 256), 0, 0)
         b = g.add_input("B", (256, 256), 0, col)
         g.set_output(g.add("matmul", [a, b]))
-        run(f"cfg2 matmul 256^3 B {'col' if col else 'row'}-major", g, [(256, 256)] * 2, 200)
+
+        def ref_cfg2(_rows, col=col):
+            def build(rb):
+                return rb.add("matmul", [rb.input("A", (256, 256)), rb.input("B", (256, 256), layout=col)])
+            return build
+        run(f"cfg2 matmul 256^3 B {'col' if col else 'row'}-major", g, ref_cfg2, "AB", [(256, 256)] * 2, 200,
+            2.0 * 256 ** 3)
     n = 4096
     g = bafe.GraphBuilder()
     a, b, cc, dd = (g.add_input(x, (n, n), 0, 0) for x in "ABCD")
     g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), g.add("mul", [cc, dd])])]))
-    run("cfg3 relu(add(matmul(A,B),mul(C,D))) 4096^3", g, [(n, n)] * 4, 20, flops=2.0 * n ** 3)
+
+    def ref_cfg3(rows):
+        def build(rb):
+            x = rb.input("A", (rows, n))
+            y = rb.input("B", (n, n))
+            z = rb.input("C", (rows, n))
+            w = rb.input("D", (rows, n))
+            return rb.add("relu", [rb.add("add", [rb.add("matmul", [x, y]), rb.add("mul", [z, w])])])
+        return build
+    run("cfg3 relu(add(matmul(A,B),mul(C,D))) 4096^3", g, ref_cfg3, "ABCD", [(n, n)] * 4, 20, 2.0 * n ** 3,
+        ref_rows=32)
     return out
 
 
@@ -701,14 +831,17 @@ def run_ours(args):
         line["scaling"] = "strong"
     elif args.only == "gemm_bf16":
         line = dict(common, **bench_gemm_bf16(c))
+    elif args.only == "gemm_tf32":
+        line = dict(common, **bench_gemm_tf32(c))
     else:
         line = dict(common, **bench_gemm(c))
         if args.only is None:
+            line["gemm_tf32"] = bench_gemm_tf32(c)
             line["gemm_bf16"] = bench_gemm_bf16(c)
             line["ew"] = bench_ew(c)
             line["transpose"] = bench_transpose(c)
             if c.rank == 0:
-                line["configs"] = bench_configs(c)
+                line["configs"] = bench_configs(c, cpu=not args.no_cpu_baseline)
     if c.rank == 0:
         print(json.dumps(line), flush=True)
     if c.dist is not None:
@@ -719,40 +852,23 @@ def run_ours(args):
 # ------------------------------------------------------ reference arm --
 
 def _ref_worker(job):
-    """One host process: the reference's generated kernel on its own row panel."""
+    """One host process: the reference's generated kernel on its own 32-row
+    panel of the 16384^3 problem, built and run through the reference's
+    own C API (this process never loads the B200 backend)."""
     import numpy as np
     from multiprocessing import shared_memory
-    sys.path.insert(0, str(PKG))
     sys.path.insert(0, str(ROOT))
     from oracle import refbafe
-    from bafe_b200.graph import GraphBuilder
-    kind, shm_name, shape, rows, steps, cache = job
+    shm_name, shape, rows, steps, cache = job
     shm = shared_memory.SharedMemory(name=shm_name)
     try:
-        big = np.ndarray(shape, np.float32, buffer=shm.buf)
-        ref = refbafe.Reference(cache_dir=cache)
-        g = GraphBuilder()
+        B = np.ndarray(shape, np.float32, buffer=shm.buf)
         rng = np.random.default_rng(os.getpid())
-        if kind == "gemm":
-            A = (rng.standard_normal((rows, GEMM_K), dtype=np.float32) * np.float32(STD))
-            C = (rng.standard_normal((rows, GEMM_N), dtype=np.float32) * np.float32(STD))
-            a = g.add_input("A", A.shape, 0, 0)
-            b = g.add_input("B", big.shape, 0, 2)
-            c = g.add_input("C", C.shape, 0, 0)
-            g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
-            byname = {"A": A, "B": big, "C": C}
-            out = np.zeros((rows, GEMM_N), np.float32)
-        else:
-            X, Y, Z = (rng.uniform(-1, 1, rows).astype(np.float32) for _ in range(3))
-            ids = [g.add_input(nm, (rows,), 0, 0) for nm in "XYZ"]
-            g.set_output(g.add("relu", [g.add("add", [g.add("mul", [ids[0], ids[1]]), ids[2]])]))
-            byname = {"X": X, "Y": Y, "Z": Z}
-            out = np.zeros(rows, np.float32)
-        opt = ref.optimize(g.graph)
-        fn = ref.compile(opt)
-        nodes = refbafe.graph_nodes(opt)
-        call = [byname[nodes[opt.inputs[i]]["name"]] for i in range(opt.n_inputs)]
-        stack = refbafe.stack_bytes_for(nodes)
+        A = rng.standard_normal((rows, GEMM_K), dtype=np.float32) * np.float32(STD)
+        C = rng.standard_normal((rows, GEMM_N), dtype=np.float32) * np.float32(STD)
+        out = np.zeros((rows, GEMM_N), np.float32)
+        ref, fn, names, stack = _ref_kernel(_build_gemm_relu_add(rows, GEMM_N), cache)
+        call = [{"A": A, "B": B, "C": C}[n] for n in names]
         times = []
         for _ in range(steps):
             t0 = time.perf_counter()
@@ -764,6 +880,13 @@ def _ref_worker(job):
 
 
 def run_reference(args):
+    """The reference's own CPU implementation of the headline workload on
+    every host core: one process per core, each computing a 32-row panel
+    (one of the emitter's row tiles, MATMUL_TILE = 32, codegen.c:23) of
+    relu(matmul(A,B)+C) at 16384^3 per step with the reference's
+    generated, single-threaded kernel (codegen.c:13-14); a step takes as
+    long as its slowest process.  Only oracle/_ref/libbafe.so (the
+    reference compiled from its own sources) is loaded."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -774,7 +897,6 @@ def run_reference(args):
     from oracle import refbafe
     if not refbafe.available():
         refbafe.build()
-    kind_label = "reference" if refbafe.available() else "port"
     if not refbafe.available():
         print(json.dumps({"impl": "reference", "unavailable": "reference library oracle/_ref/libbafe.so not built"}))
         return
@@ -782,35 +904,34 @@ def run_reference(args):
     procs = max(1, min(cores, 64))
     steps = args.warmup + args.steps
     cache = tempfile.mkdtemp(prefix="bafe_ref_cache_")
-    # warm the reference's on-disk JIT cache once (so workers only dlopen)
-    rows = 2
+    rows = 32
     shm = shared_memory.SharedMemory(create=True, size=4 * GEMM_K * GEMM_N)
     try:
         B = np.ndarray((GEMM_K, GEMM_N), np.float32, buffer=shm.buf)
         B[:] = np.random.default_rng(99).standard_normal((GEMM_K, GEMM_N), dtype=np.float32) * np.float32(STD)
-        _ref_worker(("gemm", shm.name, (GEMM_K, GEMM_N), rows, 1, cache))
+        # build the kernel once here, so the workers find it in the reference's on-disk JIT cache
+        _ref_kernel(_build_gemm_relu_add(rows, GEMM_N), cache)
         ctx = mp.get_context("spawn")
         with ctx.Pool(procs) as pool:
-            res = pool.map(_ref_worker, [("gemm", shm.name, (GEMM_K, GEMM_N), rows, steps, cache)] * procs)
+            res = pool.map(_ref_worker, [(shm.name, (GEMM_K, GEMM_N), rows, steps, cache)] * procs)
     finally:
         shm.close()
         shm.unlink()
-    # step i: every process computes its panel concurrently; the step takes
-    # the slowest process's time
     step_times = [max(r[i] for r in res) for i in range(args.warmup, steps)]
     ms = statistics.mean(step_times) * 1e3
     flops = 2.0 * rows * procs * GEMM_N * GEMM_K
     value = flops / (ms * 1e-3) / 1e12
+    sample = (f"{procs} processes x one {rows}-row panel of relu(matmul(A,B)+C) 16384^3 per step "
+              f"({flops / 1e9:.0f} GFLOP per step; the reference kernel is single-threaded)")
     line = {
         "metric": "TFLOP/s (fused GEMM relu(matmul(A,B)+C))", "value": value, "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic N(0,1/sqrt(K)) fp32",
-        "config": {"workload": "relu(matmul(A,B)+C) M=N=K=16384 fp32, A row-major, B BLOCKED tag",
-                   "sample": f"{procs} processes x {rows}-row panels per step (the reference kernel is single-threaded)"},
+        "data": "synthetic, generated on the host",
+        "config": gemm_config(GEMM_M),
+        "run": {"sample": sample, "library": "oracle/_ref/libbafe.so (the reference built from its own sources)"},
         "impl": "reference",
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": procs, "kind": kind_label,
-                         "sample": f"{procs} x {rows}-row panels of 16384^3 per step"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": procs, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -6,9 +6,11 @@ API through ctypes exactly as the reference's own callers do
 (bafe/python/bafe/__init__.py:440-544, scripts/test_smoke.c:31-60):
 bafe_optimize -> bafe_jit_get_or_compile (which emits C, runs `cc -O3
 -march=native` and dlopens it) -> call the generated kernel with host
-pointers.  Graph structs are built with bafe_b200's GraphBuilder, whose
-struct layout is the reference's ABI; the library only compares op names
-with strcmp, so the builder's interned strings are valid input.
+pointers.  Graph structs are built with oracle/refgraph.py (the
+reference's own graph API on a struct-only mirror of its ABI) or, in the
+golden-fixture generator, with the backend's GraphBuilder, whose struct
+layout is the same ABI; graph arguments are passed by address, so either
+struct works.  This module itself never imports the backend.
 
 The generated kernels keep one stack array per node (codegen.c:188), so
 large problems must run on a thread with a big stack: `call_kernel` does.
@@ -21,7 +23,7 @@ import ctypes
 import os
 import subprocess
 import threading
-from ctypes import POINTER, c_char_p, c_int, c_size_t, c_void_p
+from ctypes import c_char_p, c_int, c_size_t, c_void_p
 from pathlib import Path
 
 import numpy as np
@@ -49,12 +51,12 @@ def build() -> bool:
 
 class Reference:
     def __init__(self, cache_dir: str | None = None):
-        from bafe_b200._binding import BafeGraph, BafeJitStats   # struct mirrors (the ABI)
-        self.BafeGraph = BafeGraph
+        from oracle.refgraph import Graph   # struct-only mirror of the graph ABI
+        self.BafeGraph = Graph
         if not REF_LIB.exists():
-            raise FileNotFoundError(f"{REF_LIB} missing (make -C oracle ref)")
+            raise FileNotFoundError(f"{REF_LIB} missing (make -C oracle ref REF_SRC=...)")
         self.lib = ctypes.CDLL(str(REF_LIB))
-        G = POINTER(BafeGraph)
+        G = c_void_p                        # graphs by address: any struct with the ABI's layout
         self.lib.bafe_optimize.argtypes = [G, G, c_char_p, c_size_t]
         self.lib.bafe_optimize.restype = c_int
         self.lib.bafe_jit_get_or_compile.argtypes = [G, c_char_p, c_size_t]
@@ -71,7 +73,7 @@ class Reference:
         """bafe_optimize (bafe.c:250-258): the graph the backend receives."""
         out = self.BafeGraph()
         err = ctypes.create_string_buffer(512)
-        rc = self.lib.bafe_optimize(ctypes.byref(graph), ctypes.byref(out), err, len(err))
+        rc = self.lib.bafe_optimize(ctypes.addressof(graph), ctypes.addressof(out), err, len(err))
         if rc != 0:
             raise RuntimeError(f"bafe_optimize failed ({rc}): {err.value.decode()}")
         return out
@@ -79,14 +81,14 @@ class Reference:
     def compile(self, graph) -> int:
         """bafe_jit_get_or_compile (jit.c:204-328) -> generated-kernel address."""
         err = ctypes.create_string_buffer(2048)
-        fn = self.lib.bafe_jit_get_or_compile(ctypes.byref(graph), err, len(err))
+        fn = self.lib.bafe_jit_get_or_compile(ctypes.addressof(graph), err, len(err))
         if not fn:
             raise RuntimeError(f"reference JIT failed: {err.value.decode()}")
         return fn
 
     def hash(self, graph) -> str:
         buf = ctypes.create_string_buffer(65)
-        self.lib.bafe_jit_hash_graph(ctypes.byref(graph), buf, 65)
+        self.lib.bafe_jit_hash_graph(ctypes.addressof(graph), buf, 65)
         return buf.value.decode()
 
     @staticmethod

@@ -241,6 +241,12 @@ CASES = [
                  ("B", (16384, 16384), "float32", False, 3, N01(41, 0.0078125)),
                  ("C", (16384, 16384), "float32", False, 0, N01(42, 0.0078125))],
          panel=(8190, 8194), panel_inputs=("A", "C"), store_inputs=False),
+    dict(name="cfg5_panel_bottom", cite="benchmark configuration: relu(matmul(A,B)+C) 16384^3, B BLOCKED, rows 16380:16384",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (16384, 16384), "float32", False, 0, N01(40, 0.0078125)),
+                 ("B", (16384, 16384), "float32", False, 2, N01(41, 0.0078125)),
+                 ("C", (16384, 16384), "float32", False, 0, N01(42, 0.0078125))],
+         panel=(16380, 16384), panel_inputs=("A", "C"), store_inputs=False),
 ]
 
 CASE_BY_NAME = {c["name"]: c for c in CASES}

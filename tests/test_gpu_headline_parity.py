@@ -1,0 +1,149 @@
+"""Parity of the benchmarked fused GEMMs at their full sizes, with a bound
+that scales with the operands.
+
+The 3xTF32 bound 1e-4*sqrt(K/64) is stated for unit-variance operands.  A
+product's error scales with sigma_A * sigma_B, so the bound applied here is
+
+    1e-4 * sqrt(K/64) * sigma_A * sigma_B
+
+which for relu(matmul(A,B)+C) at 16384^3 with std 1/sqrt(K) = 1/128
+operands is 9.8e-8 (outputs are ~1e-2; the reference's own fp32 rows are
+3.4e-8 from fp64).  For each configuration (16384^3 relu(matmul(A,B)+C);
+4096^3 relu(add(matmul(A,B), mul(C,D)))), on the seeded inputs the
+reference's golden row panels were made from:
+
+  * the exact CUDA-core plan reproduces the reference's rows bit for bit
+    (top, middle and bottom panels);
+  * the benchmarked plan (`auto` = 3xTF32 tensor cores) is within the
+    scaled bound of the reference's rows AND, over the WHOLE output, of the
+    exact plan -- which covers every tile, the split-tail tiles of the last
+    wave and the last M tiles;
+  * 1xTF32 forced on the same inputs FAILS the scaled bound (so the bound
+    tells an fp32-faithful kernel from a tf32 one) and meets its own
+    relative tolerance: |out - fp64| <= 2^-9 * (|A| |B|) elementwise (two
+    operand truncations to tf32's 10-bit mantissa, 2^-10 each).
+"""
+import math
+
+import numpy as np
+import pytest
+
+import bafe_b200 as bafe
+import cases
+
+pytestmark = pytest.mark.gpu
+
+TF32_REL_TOL = 2.0 ** -9
+
+CONFIGS = {
+    "cfg5": dict(panels=["cfg5_panel_top", "cfg5_panel_mid", "cfg5_panel_bottom"]),
+    "cfg3": dict(panels=["cfg3_panel_top", "cfg3_panel_bottom"]),
+}
+
+
+def scaled_bound(K: int, sigma_a: float, sigma_b: float) -> float:
+    return 1e-4 * math.sqrt(K / 64) * sigma_a * sigma_b
+
+
+def _build(case):
+    g = bafe.GraphBuilder()
+    ids = [g.add_input(s[0], s[1], 0, s[4]) for s in case["inputs"]]
+    g.set_output(case["build"](g, *ids))
+    return g
+
+
+def _run(torch, case, dev, precision):
+    bafe.set_option("gemm_precision", precision)
+    try:
+        k = bafe.compile_graph(_build(case))
+        M, N = case["inputs"][0][1][0], case["inputs"][1][1][1]
+        out = torch.full((M, N), float("nan"), device="cuda")
+        k.run_torch(dev, out)
+        bafe.synchronize()
+    finally:
+        bafe.set_option("gemm_precision", "auto")
+    return k.describe().strip(), out
+
+
+@pytest.fixture(scope="module", params=list(CONFIGS))
+def config(request, cuda):
+    """Full-size inputs of one configuration, generated from the golden
+    seeds, on the device; the exact and benchmarked plans' outputs."""
+    torch = cuda
+    panels = CONFIGS[request.param]["panels"]
+    case = cases.CASE_BY_NAME[panels[0]]
+    dev = []
+    for spec in case["inputs"]:
+        dev.append(torch.from_numpy(cases.make_input(spec)).cuda())
+    sig = [float(s[5].get("std", 1.0)) for s in case["inputs"]]
+    K = case["inputs"][0][1][1]
+    plan_exact, exact = _run(torch, case, dev, "exact")
+    plan_auto, auto = _run(torch, case, dev, "auto")
+    goldens = {name: cases.load(name) for name in panels}
+    yield dict(name=request.param, case=case, dev=dev, K=K, sigma_a=sig[0], sigma_b=sig[1],
+               exact=exact, auto=auto, plan_exact=plan_exact, plan_auto=plan_auto, goldens=goldens)
+    del dev, exact, auto
+    torch.cuda.empty_cache()
+
+
+def test_exact_plan_reproduces_reference_rows(config):
+    assert "gemm.exact" in config["plan_exact"], config["plan_exact"]
+    for name, (meta, _, golden) in config["goldens"].items():
+        r0, r1 = meta["panel"]
+        got = config["exact"][r0:r1].cpu().numpy()
+        assert got.tobytes() == np.ascontiguousarray(golden).tobytes(), name
+
+
+def test_benchmarked_plan_within_scaled_bound_of_reference_rows(config):
+    assert "gemm.tc.3xtf32" in config["plan_auto"], config["plan_auto"]
+    bound = scaled_bound(config["K"], config["sigma_a"], config["sigma_b"])
+    for name, (meta, _, golden) in config["goldens"].items():
+        r0, r1 = meta["panel"]
+        got = config["auto"][r0:r1].cpu().numpy().astype(np.float64)
+        err = float(np.max(np.abs(got - golden.astype(np.float64))))
+        print(f"{name}: 3xTF32 vs the reference's rows max |err| {err:.3e} (scaled bound {bound:.3e})")
+        assert err <= bound, name
+
+
+def test_benchmarked_plan_whole_output_within_scaled_bound_of_exact_plan(config):
+    """Every element of the 3xTF32 output against the exact plan (the
+    reference's arithmetic), compared on the device."""
+    bound = scaled_bound(config["K"], config["sigma_a"], config["sigma_b"])
+    diff = (config["auto"] - config["exact"]).abs()
+    err = float(diff.max())
+    worst = int(diff.argmax())
+    N = config["auto"].shape[1]
+    print(f"{config['name']}: whole output, 3xTF32 vs exact max |err| {err:.3e} at row {worst // N}, "
+          f"column {worst % N} (scaled bound {bound:.3e}); NaN: {bool(config['auto'].isnan().any())}")
+    assert not bool(config["auto"].isnan().any())
+    assert err <= bound
+
+
+def test_tf32_fails_the_scaled_bound_and_meets_its_relative_tolerance(config, cuda):
+    torch = cuda
+    case = config["case"]
+    plan, out = _run(torch, case, config["dev"], "tf32")
+    assert "gemm.tc.tf32" in plan, plan
+    bound = scaled_bound(config["K"], config["sigma_a"], config["sigma_b"])
+    err_exact = float((out - config["exact"]).abs().max())
+    print(f"{config['name']}: 1xTF32 vs exact max |err| {err_exact:.3e} (3xTF32 scaled bound {bound:.3e})")
+    assert err_exact > bound, "the scaled bound does not tell 1xTF32 from 3xTF32"
+    # relative tolerance on the golden panels' rows, against fp64
+    A, B = config["dev"][0], config["dev"][1]
+    Bd = B.double()
+    Babs = Bd.abs()
+    worst = 0.0
+    for name, (meta, _, _) in config["goldens"].items():
+        r0, r1 = meta["panel"]
+        Ad = A[r0:r1].double()
+        ref = Ad @ Bd
+        scale = Ad.abs() @ Babs
+        if len(config["dev"]) == 3:        # relu(acc + C)
+            ref = torch.relu(ref + config["dev"][2][r0:r1].double())
+        else:                              # relu(acc + C*D)
+            ref = torch.relu(ref + (config["dev"][2][r0:r1] * config["dev"][3][r0:r1]).double())
+        rel = float(((out[r0:r1].double() - ref).abs() / scale).max())
+        worst = max(worst, rel)
+    del Bd, Babs
+    print(f"{config['name']}: 1xTF32 max |out - fp64| / (|A||B|) = {worst:.3e} (tolerance {TF32_REL_TOL:.3e})")
+    assert worst <= TF32_REL_TOL

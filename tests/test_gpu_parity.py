@@ -89,6 +89,44 @@ def test_exact_precision_is_bit_exact(name, cuda):
         f"{name}: {int(np.sum(got != want))} elements differ; plan:\n{k.describe()}")
 
 
+def _rms(a) -> float:
+    a = np.asarray(a, np.float64)
+    return float(np.sqrt(np.mean(a * a))) if a.size else 0.0
+
+
+@pytest.mark.parametrize("precision", ["auto", "3xtf32"])
+@pytest.mark.parametrize("name", SMALL)
+def test_tensor_core_precisions_match_reference(name, precision, cuda):
+    """Every small golden case in the default precision (`auto`: tensor
+    cores from 256^3 on, so the 256^3 configurations run their benchmarked
+    3xTF32 plan) and with 3xTF32 forced wherever the shape allows it.  A
+    plan that stays on the CUDA cores must be bit-exact; a tensor-core plan
+    must be within 1e-4*sqrt(K/64)*rms(A)*rms(B) (north star's bound scaled
+    to the operands) of the reference's output."""
+    bafe.set_option("gemm_precision", precision)
+    meta, stored, golden = cases.load(name)
+    arrays = _inputs(meta, stored, False)
+    k, out = _run(meta, arrays)
+    plan = k.describe()
+    got = np.ascontiguousarray(out).reshape(-1)
+    want = np.ascontiguousarray(golden).reshape(-1)
+    if "gemm.tc" not in plan:
+        if name in TRANSCENDENTAL:
+            return   # covered by test_exact_precision_is_bit_exact
+        assert got.view(np.uint8).tobytes() == want.view(np.uint8).tobytes(), plan
+        return
+    nodes = meta["nodes"]
+    mm = [n for n in nodes if n["op"] in ("matmul", "fused_matmul_relu", "fused_matmul_bias", "fused_matmul_bias_relu")]
+    assert len(mm) == 1, plan
+    a_node, b_node = (nodes[c] for c in mm[0]["children"][:2])
+    A, B = arrays[a_node["name"]], arrays[b_node["name"]]
+    K = A.shape[-1]
+    bound = 1e-4 * np.sqrt(K / 64) * _rms(A) * _rms(B)
+    err = float(np.max(np.abs(got.astype(np.float64) - want.astype(np.float64)))) if got.size else 0.0
+    print(f"{name} [{precision}]: tensor-core plan vs the reference max |err| {err:.3e} (scaled bound {bound:.3e})")
+    assert err <= bound, plan
+
+
 @pytest.mark.parametrize("name", PANELS)
 def test_full_size_rows_match_reference_panels_exact(name, cuda):
     """Full-size 4096^3 / 16384^3 problems, exact precision: the rows the
