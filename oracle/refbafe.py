@@ -63,6 +63,8 @@ class Reference:
         self.lib.bafe_jit_get_or_compile.restype = c_void_p
         self.lib.bafe_jit_hash_graph.argtypes = [G, c_char_p, c_size_t]
         self.lib.bafe_jit_hash_graph.restype = c_int
+        self.lib.bafe_fuse_concat.argtypes = [G, G, G, c_char_p, c_size_t]
+        self.lib.bafe_fuse_concat.restype = c_int
         self.lib.bafe_jit_set_cache_dir.argtypes = [c_char_p]
         self.lib.bafe_jit_clear.argtypes = []
         if cache_dir:
@@ -76,6 +78,17 @@ class Reference:
         rc = self.lib.bafe_optimize(ctypes.addressof(graph), ctypes.addressof(out), err, len(err))
         if rc != 0:
             raise RuntimeError(f"bafe_optimize failed ({rc}): {err.value.decode()}")
+        return out
+
+    def fuse_concat(self, graph_a, graph_b) -> object:
+        """bafe_fuse_concat (fuse.c:12-106): graph_a's output feeds graph_b's
+        first input; the inputs are graph_a's then graph_b's inputs[1:]."""
+        out = self.BafeGraph()
+        err = ctypes.create_string_buffer(256)
+        rc = self.lib.bafe_fuse_concat(ctypes.addressof(graph_a), ctypes.addressof(graph_b),
+                                       ctypes.addressof(out), err, len(err))
+        if rc != 0:
+            raise RuntimeError(f"bafe_fuse_concat failed ({rc}): {err.value.decode()}")
         return out
 
     def compile(self, graph) -> int:

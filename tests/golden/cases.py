@@ -116,6 +116,67 @@ CASES = [
     dict(name="i64_add", cite="bafe/tests/test_dtypes.py:213",
          build=lambda g, A, B: g.add("add", [A, B]),
          inputs=[("A", (8, 8), "int64", False, 0, RINT(150)), ("B", (8, 8), "int64", False, 0, RINT(151))]),
+    # ---- BF16 through the C API: inputs are raw bf16 words, the kernel
+    # widens them exactly and rounds its result back to nearest-even with the
+    # emitter's bias trick (codegen.c:113-127, 157-169) ----------------------
+    dict(name="bf16_matmul", cite="bafe/src/codegen.c:113-127,191-293 (bf16 in, bf16 out)",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (8, 8), "bfloat16", False, 0, N01(186)), ("B", (8, 8), "bfloat16", False, 0, N01(187))]),
+    dict(name="bf16_relu", cite="bafe/src/codegen.c:113-127,338-344",
+         build=lambda g, X: g.add("relu", [X]),
+         inputs=[("X", (16, 16), "bfloat16", False, 0, N01(188, 2.0))]),
+    dict(name="bf16_add", cite="bafe/src/codegen.c:113-127,294-326",
+         build=lambda g, A, B: g.add("add", [A, B]),
+         inputs=[("A", (16, 16), "bfloat16", False, 0, N01(189)), ("B", (16, 16), "bfloat16", False, 0, N01(190))]),
+    dict(name="bf16_matmul_relu", cite="bafe/src/codegen.c:113-127,467-486 (fused at 8x8)",
+         build=lambda g, A, B: g.add("relu", [g.add("matmul", [A, B])]),
+         inputs=[("A", (8, 8), "bfloat16", False, 0, N01(191)), ("B", (8, 8), "bfloat16", False, 0, N01(192))]),
+    dict(name="bf16_matmul_bias_relu", cite="bafe/src/codegen.c:113-127,502-517",
+         build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
+         inputs=[("A", (8, 8), "bfloat16", False, 0, N01(193)), ("B", (8, 8), "bfloat16", False, 0, N01(194)),
+                 ("bias", (8,), "bfloat16", False, 0, N01(195))]),
+    dict(name="bf16_special_values", cite="bafe/src/codegen.c:113-127,294-344 (NaN / -0 / inf through bf16)",
+         build=_ew3,
+         inputs=[("X", (4096,), "bfloat16", False, 0, SPECIAL(196)), ("Y", (4096,), "bfloat16", False, 0, SPECIAL(197)),
+                 ("Z", (4096,), "bfloat16", False, 0, SPECIAL(198))]),
+    dict(name="bf16_relu_matmul_plus_c_256", cite="bafe/src/codegen.c:113-127,191-293,294-344 (tensor-core size)",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (256, 256), "bfloat16", False, 0, N01(199)), ("B", (256, 256), "bfloat16", False, 0, N01(200)),
+                 ("C", (256, 256), "bfloat16", False, 0, N01(201))],
+         store_inputs=False),
+    dict(name="bf16_matmul_col_b_320x384x512", cite="bafe/src/codegen.c:113-127,206-213 (B Fortran order)",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (320, 512), "bfloat16", False, 0, N01(202)), ("B", (512, 384), "bfloat16", True, 1, N01(203))],
+         store_inputs=False),
+    # ---- bafe.fuse(f, g): the graph FusedFunction compiles (f and g optimized
+    # apart, bafe_fuse_concat, optimized again; __init__.py:844-885,
+    # fuse.c:12-125).  fuse = (f, g) names the jitted functions the tests
+    # rebuild; na = f's argument count ---------------------------------------
+    dict(name="fuse_two_matmuls", cite="bafe/tests/test_fuse.py:14", fuse=("matmul", "matmul"), na=2,
+         build_a=lambda g, A, B: g.add("matmul", [A, B]),
+         build_b=lambda g, X, C: g.add("matmul", [X, C]),
+         inputs=[("A", (8, 16), "float32", False, 0, N01(204)), ("B", (16, 32), "float32", False, 0, N01(205)),
+                 ("C", (32, 24), "float32", False, 0, N01(206))]),
+    dict(name="fuse_matmul_then_relu", cite="bafe/tests/test_fuse.py:35", fuse=("matmul", "relu"), na=2,
+         build_a=lambda g, A, B: g.add("matmul", [A, B]),
+         build_b=lambda g, X: g.add("relu", [X]),
+         inputs=[("A", (16, 32), "float32", False, 0, N01(207)), ("B", (32, 24), "float32", False, 0, N01(208))]),
+    dict(name="fuse_matmul_then_add_bias", cite="bafe/tests/test_fuse.py:54", fuse=("matmul", "relu_add"), na=2,
+         build_a=lambda g, A, B: g.add("matmul", [A, B]),
+         build_b=lambda g, X, b: g.add("relu", [g.add("add", [X, b])]),
+         inputs=[("A", (32, 32), "float32", False, 0, N01(209)), ("B", (32, 32), "float32", False, 0, N01(210)),
+                 ("bias", (32,), "float32", False, 0, N01(211))]),
+    dict(name="fuse_matmul_then_relu_64x64", cite="bafe/tests/test_fuse.py:113 (largest shape)", fuse=("matmul", "relu"),
+         na=2, build_a=lambda g, A, B: g.add("matmul", [A, B]),
+         build_b=lambda g, X: g.add("relu", [X]),
+         inputs=[("A", (64, 64), "float32", False, 0, N01(212)), ("B", (64, 64), "float32", False, 0, N01(213))]),
+    dict(name="fuse_gemm_then_relu_add_c_256", cite="bafe/tests/test_fuse.py:243 (fused == sequential), tensor-core size",
+         fuse=("matmul", "relu_add"), na=2,
+         build_a=lambda g, A, B: g.add("matmul", [A, B]),
+         build_b=lambda g, X, C: g.add("relu", [g.add("add", [X, C])]),
+         inputs=[("A", (256, 320), "float32", False, 0, N01(214)), ("B", (320, 192), "float32", False, 0, N01(215)),
+                 ("C", (256, 192), "float32", False, 0, N01(216))],
+         store_inputs=False),
     # ---- scripts/test_smoke.c (deterministic pattern) ----------------------
     dict(name="smoke_c_pattern", cite="scripts/test_smoke.c:11-24,54-56",
          build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
@@ -261,9 +322,28 @@ def make_input(name_shape_spec, full: bool = True) -> np.ndarray:
         n = int(np.prod(shape))
         a = ((np.arange(n) % spec["mod"]).astype(np.float32) * np.float32(spec["scale"])).reshape(shape)
         return a.astype(dtype)
+    if dtype == "bfloat16":
+        # drawn in fp32, then rounded to bf16 words (nearest-even)
+        base = (name, shape, "float32", fortran, layout, spec)
+        return f32_to_bf16_bits(make_input(base))
     if kind == "special":
         return special_values(int(np.prod(shape)), spec["seed"]).reshape(shape).astype(dtype)
     return generate(spec, shape, dtype, fortran)
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 words, round to nearest-even by adding 0x7FFF plus the
+    kept lsb (the emitter's own rounding, codegen.c:119-125); keeps the
+    array's memory order."""
+    bits = np.asarray(a, np.float32).view(np.uint32).astype(np.uint64)
+    bits = (bits + 0x7FFF + ((bits >> 16) & 1)) & 0xFFFFFFFF
+    out = (bits >> 16).astype(np.uint16)
+    return np.asfortranarray(out) if np.isfortran(a) else np.ascontiguousarray(out)
+
+
+def bf16_bits_to_f64(a: np.ndarray) -> np.ndarray:
+    """bf16 words -> their exact values (as float64)."""
+    return (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
 
 
 def load(name: str):

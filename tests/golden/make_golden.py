@@ -35,7 +35,7 @@ from cases import CASES, make_input  # noqa: E402
 from bafe_b200.graph import GraphBuilder  # noqa: E402
 from oracle import refbafe  # noqa: E402
 
-DT = {"float32": 0, "float64": 1, "int32": 2, "int64": 3, "float16": 4}
+DT = {"float32": 0, "float64": 1, "int32": 2, "int64": 3, "float16": 4, "bfloat16": 5}
 NPDT = {0: np.float32, 1: np.float64, 2: np.int32, 3: np.int64, 4: np.float16, 5: np.uint16}
 
 
@@ -52,11 +52,14 @@ def run_case(ref: refbafe.Reference, case: dict, cache: dict) -> None:
         if panel and spec[0] in case.get("panel_inputs", ()):
             a = np.ascontiguousarray(a[panel[0]:panel[1]])
         arrays[spec[0]] = a
-    g = GraphBuilder()
-    ids = [g.add_input(s[0], arrays[s[0]].shape, DT[s[2]], s[4]) for s in case["inputs"]]
-    root = case["build"](g, *ids)
-    g.set_output(root)
-    opt = ref.optimize(g.graph)
+    if case.get("fuse"):
+        opt = fused_graph(ref, case, arrays)
+    else:
+        g = GraphBuilder()
+        ids = [g.add_input(s[0], arrays[s[0]].shape, DT[s[2]], s[4]) for s in case["inputs"]]
+        root = case["build"](g, *ids)
+        g.set_output(root)
+        opt = ref.optimize(g.graph)
     nodes = refbafe.graph_nodes(opt)
     input_ids = [opt.inputs[i] for i in range(opt.n_inputs)]
     oroot = opt.outputs[0]
@@ -69,6 +72,7 @@ def run_case(ref: refbafe.Reference, case: dict, cache: dict) -> None:
         "name": case["name"], "cite": case["cite"], "nodes": nodes, "input_ids": input_ids, "root": oroot,
         "inputs": [{"name": s[0], "shape": list(s[1]), "dtype": s[2], "fortran": s[3], "layout": s[4],
                     "spec": s[5]} for s in case["inputs"]],
+        "fuse": list(case["fuse"]) if case.get("fuse") else None, "fuse_na": case.get("na"),
         "panel": list(panel) if panel else None, "panel_inputs": list(case.get("panel_inputs", ())),
         "reference_graph_hash": ref.hash(opt), "ops": [n["op"] for n in nodes if not n["is_input"]],
     }
@@ -78,6 +82,24 @@ def run_case(ref: refbafe.Reference, case: dict, cache: dict) -> None:
             save[f"in_{k}"] = v
     np.savez_compressed(HERE / f"{case['name']}.npz", **save)
     print(f"{case['name']:28s} ops={meta['ops']} out={out.shape} {time.time() - t0:.1f}s", flush=True)
+
+
+def fused_graph(ref: refbafe.Reference, case: dict, arrays: dict):
+    """The graph the reference's FusedFunction compiles (__init__.py:844-885):
+    f and g each optimized on their own (g traced on an input shaped like
+    f's output), concatenated by bafe_fuse_concat, optimized again."""
+    specs = case["inputs"]
+    na = case["na"]
+    ga = GraphBuilder()
+    ids_a = [ga.add_input(s[0], arrays[s[0]].shape, DT[s[2]], s[4]) for s in specs[:na]]
+    root_a = case["build_a"](ga, *ids_a)
+    ga.set_output(root_a)
+    gb = GraphBuilder()
+    x = gb.add_input("X", ga.shape(root_a), ga.dtype(root_a), 0)
+    ids_b = [gb.add_input(s[0], arrays[s[0]].shape, DT[s[2]], s[4]) for s in specs[na:]]
+    gb.set_output(case["build_b"](gb, x, *ids_b))
+    cat = ref.fuse_concat(ref.optimize(ga.graph), ref.optimize(gb.graph))
+    return ref.optimize(cat)
 
 
 def main() -> None:

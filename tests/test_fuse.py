@@ -104,3 +104,76 @@ def test_fused_large_gemm_epilogue_matches_unfused(cuda):
     ref = np.maximum(A.astype(np.float64) @ B.astype(np.float64) + C, 0)
     bound = 1e-4 * np.sqrt(K / 64)
     assert np.abs(fused - ref).max() <= bound and np.abs(seq - ref).max() <= bound
+
+
+# ---- pinned to the reference: tests/golden/fuse_*.npz hold the output of
+# the reference's own fused kernel (f and g optimized apart,
+# bafe_fuse_concat, optimized again, its JIT) on seeded inputs ------------
+
+@bafe.jit
+def mm_x(X, C):
+    return bafe.matmul(X, C)
+
+
+@bafe.jit
+def relu_x(X):
+    return bafe.relu(X)
+
+
+@bafe.jit
+def relu_add_x(X, C):
+    return bafe.relu(X + C)
+
+
+FNS = {"matmul": (mm, mm_x), "relu": (None, relu_x), "relu_add": (None, relu_add_x)}
+
+
+def _fuse_case_args(name):
+    import cases
+    meta, stored, golden = cases.load(name)
+    args = []
+    for spec in meta["inputs"]:
+        if spec["name"] in stored:
+            args.append(stored[spec["name"]])
+        else:
+            t = (spec["name"], tuple(spec["shape"]), spec["dtype"], spec["fortran"], spec["layout"], spec["spec"])
+            args.append(cases.make_input(t))
+    f_name, g_name = meta["fuse"]
+    return bafe.fuse(FNS[f_name][0], FNS[g_name][1]), args, golden
+
+
+FUSE_CASES = ["fuse_two_matmuls", "fuse_matmul_then_relu", "fuse_matmul_then_add_bias",
+              "fuse_matmul_then_relu_64x64", "fuse_gemm_then_relu_add_c_256"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", FUSE_CASES)
+def test_fused_call_is_bit_exact_to_reference_fuse(cuda, name):
+    """h = bafe.fuse(f, g) called with numpy arrays, `exact` GEMM precision:
+    the device-resident fused plan reproduces the reference's fused kernel
+    bit for bit."""
+    bafe.set_option("gemm_precision", "exact")
+    try:
+        h, args, golden = _fuse_case_args(name)
+        out = h(*args)
+    finally:
+        bafe.set_option("gemm_precision", "auto")
+    assert out.shape == golden.shape
+    assert out.tobytes() == np.ascontiguousarray(golden).tobytes(), h.kernel_for(*args).describe()
+
+
+@pytest.mark.gpu
+def test_fused_tensor_core_plan_matches_reference_fuse(cuda):
+    """The 256 x 320 x 192 fused case in the default precision runs one
+    3xTF32 tensor-core kernel with the epilogue fused; it stays within
+    1e-4 * sqrt(K/64) * rms(A) * rms(B) of the reference's fused output."""
+    h, args, golden = _fuse_case_args("fuse_gemm_then_relu_add_c_256")
+    k = h.kernel_for(*args)
+    steps = k.describe().strip().splitlines()
+    assert "gemm.tc.3xtf32" in steps[-1] and "epi=relu(add(acc,C))" in steps[-1], k.describe()
+    out = h(*args)
+    A, B = (a.astype(np.float64) for a in args[:2])
+    bound = 1e-4 * np.sqrt(A.shape[1] / 64) * np.sqrt(np.mean(A * A)) * np.sqrt(np.mean(B * B))
+    err = float(np.abs(out.astype(np.float64) - golden).max())
+    print(f"fused 3xTF32 vs the reference's fused kernel: max |err| {err:.3e} (bound {bound:.3e})")
+    assert err <= bound

@@ -1,5 +1,9 @@
 """bf16 GEMMs on the tensor cores (kind::f16), against the exact kernel.
 
+(The exact kernel and the tensor-core plan are also pinned to the
+reference's own bf16 outputs: tests/golden/bf16_*.npz, checked in
+test_gpu_parity.py bit for bit and within the bound below.)
+
 The reference converts bf16 operands to f32 exactly, multiplies in f32
 (exact for bf16 x bf16) and sums in f32 in 32-wide chunks, then rounds the
 epilogue result to bf16 (codegen.c:85-127, 191-293).  The tensor-core path
