@@ -78,6 +78,9 @@ def parse():
     p.add_argument("--only", choices=["gemm", "gemm_tf32", "gemm_bf16", "ew", "transpose"], default=None,
                    help="run one workload (profiling); prints its own line")
     p.add_argument("--gemm-size", type=int, default=GEMM_M, help="M=N=K (profiling smaller cases)")
+    p.add_argument("--gemm-epilogue", choices=["c", "mul_cd"], default="c",
+                   help="c: relu(matmul(A,B)+C) (the headline); mul_cd: relu(add(matmul(A,B), mul(C,D))), "
+                        "the 4096^3 configuration's epilogue, for profiling it at any size")
     p.add_argument("--ew-elements", type=int, default=EW_N)
     p.add_argument("--transpose-size", type=int, default=TR_N, help="transpose of an S x S fp32 matrix")
     return p.parse_args()
@@ -168,13 +171,17 @@ def roofline_basis(c, clocks: dict, div: float):
     return sustained, "sustained", burst, sustained
 
 
-def gemm_graph(m_rows: int, size: int = GEMM_N):
+def gemm_graph(m_rows: int, size: int = GEMM_N, epilogue: str = "c"):
     import bafe_b200 as bafe
     g = bafe.GraphBuilder()
     a = g.add_input("A", (m_rows, size), 0, 0)
     b = g.add_input("B", (size, size), 0, 2)      # BLOCKED tag, row-major storage
     c = g.add_input("C", (m_rows, size), 0, 0)
-    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
+    if epilogue == "mul_cd":
+        d = g.add_input("D", (m_rows, size), 0, 0)
+        g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), g.add("mul", [c, d])])]))
+    else:
+        g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
     return g
 
 
@@ -443,13 +450,17 @@ def bench_gemm(c: Ctx) -> dict:
         torch.cuda.synchronize()
         bcast_ms = c.max(e0.elapsed_time(e1))
     out = torch.empty(rows, S, device=c.dev)
+    epi = args.gemm_epilogue
+    ins = [A, B, C]
+    if epi == "mul_cd":
+        ins.append(torch.randn(rows, S, device=c.dev, generator=c.gen))
     t_compile = time.perf_counter()
-    k = bafe.compile_graph(gemm_graph(rows, S))
+    k = bafe.compile_graph(gemm_graph(rows, S, epi))
     t_compile = time.perf_counter() - t_compile
     plan = k.describe().strip()
     c.barrier()
     with Clocks(c.local) as ck:
-        per, total_ms, launches = time_steps(torch, k, [A, B, C], out, args.steps, args.warmup)
+        per, total_ms, launches = time_steps(torch, k, ins, out, args.steps, args.warmup)
     c.barrier()
     clocks = ck.summary()
     total_ms = c.max(total_ms)
@@ -466,11 +477,12 @@ def bench_gemm(c: Ctx) -> dict:
         "value": round(flops_total / (ms_step * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
         "ms_per_step": round(ms_step, 4),
         "dtype": "fp32 via 3xtf32" if tc3 else ("tf32" if "tc.tf32" in plan else "fp32"),
-        "config": gemm_config(S),
+        "config": gemm_config(S) if epi == "c" else
+                  {"workload": f"relu(add(matmul(A,B), mul(C,D))) M=N=K={S} fp32, A, C, D row-major, B BLOCKED tag"},
         "run": {"parallelism": f"M-row panels x{c.world}, B broadcast once (outside the timed region)",
                 "plan": plan, "precision_option": args.precision},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 2), "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(f"gemm_{S}"),
+                     "frac": round(achieved / peak, 4), "traffic": traffic_from_profiles(f"gemm_{S}" if epi == "c" else f"gemm_mul_cd_{S}"),
                      "peak_basis": f"{c.peak_src} {basis} bf16 TFLOP/s / 2 (tf32 rate)"
                                    + (" / 3 (three products)" if tc3 else "")
                                    + f"; {basis} because the timed region's median SM clock was "
@@ -482,7 +494,7 @@ def bench_gemm(c: Ctx) -> dict:
         "gpu_launches": launches, "clocks": clocks, "b_broadcast_ms": round(bcast_ms, 3),
         "compile_s": round(t_compile, 2),
     }
-    if args.e2e_steps > 0:
+    if args.e2e_steps > 0 and epi == "c":
         hA, hB, hC = A.cpu().pin_memory(), B.cpu().pin_memory(), C.cpu().pin_memory()
         hO = torch.empty(rows, S).pin_memory()
         c.barrier()
@@ -504,7 +516,7 @@ def bench_gemm(c: Ctx) -> dict:
         if c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
             res["cpu_baseline"] = cpu_baseline_gemm(hA[:32].numpy(), hB.numpy(), hC[:32].numpy())
         del hA, hB, hC, hO
-    elif c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M:
+    elif c.rank == 0 and not args.no_cpu_baseline and S == GEMM_M and epi == "c":
         res["cpu_baseline"] = cpu_baseline_gemm(A[:32].cpu().numpy(), B.cpu().numpy(), C[:32].cpu().numpy())
     return res
 

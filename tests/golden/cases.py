@@ -174,8 +174,8 @@ CASES = [
          fuse=("matmul", "relu_add"), na=2,
          build_a=lambda g, A, B: g.add("matmul", [A, B]),
          build_b=lambda g, X, C: g.add("relu", [g.add("add", [X, C])]),
-         inputs=[("A", (256, 320), "float32", False, 0, N01(214)), ("B", (320, 192), "float32", False, 0, N01(215)),
-                 ("C", (256, 192), "float32", False, 0, N01(216))],
+         inputs=[("A", (256, 320), "float32", False, 0, N01(214)), ("B", (320, 256), "float32", False, 0, N01(215)),
+                 ("C", (256, 256), "float32", False, 0, N01(216))],
          store_inputs=False),
     # ---- scripts/test_smoke.c (deterministic pattern) ----------------------
     dict(name="smoke_c_pattern", cite="scripts/test_smoke.c:11-24,54-56",

@@ -164,7 +164,7 @@ def test_fused_call_is_bit_exact_to_reference_fuse(cuda, name):
 
 @pytest.mark.gpu
 def test_fused_tensor_core_plan_matches_reference_fuse(cuda):
-    """The 256 x 320 x 192 fused case in the default precision runs one
+    """The 256 x 320 x 256 fused case in the default precision runs one
     3xTF32 tensor-core kernel with the epilogue fused; it stays within
     1e-4 * sqrt(K/64) * rms(A) * rms(B) of the reference's fused output."""
     h, args, golden = _fuse_case_args("fuse_gemm_then_relu_add_c_256")
