@@ -346,6 +346,33 @@ def bf16_bits_to_f64(a: np.ndarray) -> np.ndarray:
     return (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32).astype(np.float64)
 
 
+DTYPE_CODE = {"float32": 0, "float64": 1, "int32": 2, "int64": 3, "float16": 4, "bfloat16": 5}
+
+
+def traced_graph(case: dict):
+    """The case's graph as the front end traces it, at its declared (full)
+    shapes and layout tags; for a fuse case, f's and g's traced graphs
+    concatenated as bafe.fuse does (fuse.c:12-106: f's output feeds g's
+    first input)."""
+    from bafe_b200.graph import GraphBuilder
+    specs = case["inputs"]
+    if not case.get("fuse"):
+        g = GraphBuilder()
+        ids = [g.add_input(s[0], s[1], DTYPE_CODE[s[2]], s[4]) for s in specs]
+        g.set_output(case["build"](g, *ids))
+        return g
+    na = case["na"]
+    ga = GraphBuilder()
+    ids_a = [ga.add_input(s[0], s[1], DTYPE_CODE[s[2]], s[4]) for s in specs[:na]]
+    ra = case["build_a"](ga, *ids_a)
+    ga.set_output(ra)
+    gb = GraphBuilder()
+    x = gb.add_input("X", ga.shape(ra), ga.dtype(ra), 0)
+    ids_b = [gb.add_input(s[0], s[1], DTYPE_CODE[s[2]], s[4]) for s in specs[na:]]
+    gb.set_output(case["build_b"](gb, x, *ids_b))
+    return GraphBuilder.concat(ga, gb)
+
+
 def load(name: str):
     """-> (meta dict, {input name: array or None}, golden output)."""
     z = np.load(GOLDEN_DIR / f"{name}.npz", allow_pickle=False)

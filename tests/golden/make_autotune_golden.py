@@ -35,6 +35,7 @@ sys.path.insert(0, str(HERE))
 sys.path.insert(0, str(ROOT / "bafe-basic-algibra-fusion-engine-_b200"))
 sys.path.insert(0, str(ROOT))
 
+import cases  # noqa: E402
 from cases import CASES, graph_from_nodes, load  # noqa: E402
 from bafe_b200 import _binding  # noqa: E402
 from bafe_b200.graph import GraphBuilder  # noqa: E402
@@ -68,11 +69,8 @@ def feats(lib, g) -> list:
 
 
 def traced_graph(case) -> GraphBuilder:
-    """The case's graph as traced, at its declared (full) shapes and layout tags."""
-    g = GraphBuilder()
-    ids = [g.add_input(s[0], s[1], DT[s[2]], s[4]) for s in case["inputs"]]
-    g.set_output(case["build"](g, *ids))
-    return g
+    """The case's graph as traced (cases.traced_graph)."""
+    return cases.traced_graph(case)
 
 
 def refit_logs():

@@ -38,11 +38,7 @@ def _features(g) -> list:
 
 
 def _traced(case) -> GraphBuilder:
-    DT = {"float32": 0, "float64": 1, "int32": 2, "int64": 3, "float16": 4, "bfloat16": 5}
-    g = GraphBuilder()
-    ids = [g.add_input(s[0], s[1], DT[s[2]], s[4]) for s in case["inputs"]]
-    g.set_output(case["build"](g, *ids))
-    return g
+    return cases.traced_graph(case)
 
 
 # ------------------------------------------------------------ vs reference --
