@@ -180,6 +180,29 @@ class Kernel:
         s = stream if stream is not None else torch.cuda.current_stream()
         self.run_device([t.data_ptr() for t in inputs] + [out.data_ptr()], s.cuda_stream)
 
+    @property
+    def k_slice_align(self) -> int:
+        """Multiple of K that K-slice bounds must be; 0: the plan cannot run in K slices."""
+        return int(lib.bafe_cuda_plan_k_slice_align(self.plan))
+
+    def run_torch_ksliced(self, inputs: Sequence, out, k_bounds: Sequence[int], ready=None, stream=None) -> None:
+        """bafe_cuda_run_device_ksliced on torch CUDA tensors: the GEMM over
+        K slices [k_bounds[j], k_bounds[j+1]), slice j waiting on ready[j]
+        (torch.cuda.Event, raw cudaEvent_t or None)."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        ptrs = [t.data_ptr() for t in inputs] + [out.data_ptr()]
+        arr = (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+        n = len(k_bounds) - 1
+        kb = (ctypes.c_int64 * len(k_bounds))(*[int(k) for k in k_bounds])
+        evs = None
+        if ready is not None:
+            if len(ready) != n:
+                raise TypeError(f"{n} K slices but {len(ready)} events")
+            evs = (ctypes.c_void_p * n)(*[ctypes.c_void_p(getattr(e, "cuda_event", e) or 0) for e in ready])
+        check(lib.bafe_cuda_run_device_ksliced(self.plan, arr, len(ptrs), ctypes.c_void_p(int(s.cuda_stream)), n, kb,
+                                               evs), "run_device_ksliced")
+
 
 def compile_graph(builder: GraphBuilder) -> Kernel:
     """bafe_cuda_jit_get_or_compile on a built graph."""

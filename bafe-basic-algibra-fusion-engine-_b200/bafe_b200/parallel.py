@@ -9,9 +9,21 @@
   only its slab of B over its own host link and an all-gather over NVLink
   completes B on every rank.  The output stays sharded; `gather_rows` all-gathers it
   when a single copy is needed.
+* When B changes from call to call, it can cross NVLink inside the call:
+  `broadcast_slabs` broadcasts it from the root in K slabs (contiguous row
+  ranges of a row-major B) on a communication stream, one event per slab,
+  and the plan runs in K slices (Kernel.run_torch_ksliced), slice j's
+  launches waiting only for slab j -- so the GEMM over the first slabs
+  overlaps the broadcast of the later ones.  The slices carry the fp32
+  sums through the output in the same chunk order as one launch: the
+  result is the same bit for bit.
 * Elementwise graphs shard by contiguous element ranges with no collective
   (range starts are multiples of 4 elements so every shard keeps 16-byte
   vector access).
+* A rank-2 transpose shards by output row blocks (`transpose_blocks`):
+  rank r writes rows [c0, c1) of the (cols x rows) output, which are
+  columns [c0, c1) of the input -- a column panel it reads in place with
+  the input's row stride; no collective.
 Panel boundaries are multiples of 128 rows (the tensor-core tile height)
 where the size allows, so no rank carries a partial tile in the middle.
 
@@ -42,6 +54,71 @@ def row_panels(M: int, world: int, align: int = 128) -> List[Tuple[int, int]]:
 def element_ranges(n: int, world: int, align: int = 4) -> List[Tuple[int, int]]:
     """Contiguous element ranges covering [0, n), starts multiples of `align`."""
     return row_panels(n, world, align)
+
+
+def transpose_blocks(cols: int, world: int, align: int = 64) -> List[Tuple[int, int]]:
+    """Output row blocks of a transpose of a (rows x cols) matrix, one per
+    rank: rank r writes output rows [c0, c1) = input columns [c0, c1);
+    boundaries are multiples of `align` (the transpose kernel's tile) when
+    the size allows."""
+    return row_panels(cols, world, align)
+
+
+def k_slices(K: int, align: int, first: int = 0, growth: float = 2.0, max_slices: int = 6) -> List[int]:
+    """Bounds [0, k1, ..., K] of the K slabs a B broadcast is cut into:
+    interior bounds are multiples of `align`; the first slab is small (its
+    broadcast is the only one nothing overlaps), each next one `growth`
+    times the previous (the GEMM over a slab outlasts the broadcast of the
+    next, so the later, larger slabs stay hidden), at most `max_slices`
+    slabs.  first = 0 picks K / 16."""
+    if align <= 0 or K <= align:
+        return [0, K]
+    want = first if first > 0 else K // 16
+    size = max(align, (want + align - 1) // align * align)
+    bounds = [0]
+    while len(bounds) < max_slices and bounds[-1] + size < K:
+        bounds.append(bounds[-1] + size)
+        size = max(align, int(size * growth) // align * align)
+    bounds.append(K)
+    # a last slab under half the one before joins it (a launch with little
+    # work costs its pipeline fill and one more store and reload of the sums)
+    if len(bounds) > 3 and 2 * (bounds[-1] - bounds[-2]) < bounds[-2] - bounds[-3]:
+        del bounds[-2]
+    return bounds
+
+
+def broadcast_slabs(B, bounds: Sequence[int], dist, src: int = 0, stream=None):
+    """Broadcast the rows [bounds[j], bounds[j+1]) of B (row-major, shape
+    (K, ...)) from `src`, slab by slab, in place.  On CUDA the broadcasts
+    are issued on `stream` (a side stream) and a list of events is returned,
+    event j recorded once slab j is in this rank's B; on the CPU (gloo) the
+    calls complete in order and the list holds None."""
+    import torch
+    world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+    events = []
+    on_gpu = B.is_cuda
+    ctx = torch.cuda.stream(stream) if (on_gpu and stream is not None) else _null()
+    with ctx:
+        for j in range(len(bounds) - 1):
+            slab = B[bounds[j]:bounds[j + 1]]
+            if world > 1:
+                w = dist.broadcast(slab, src=src, async_op=True)
+                w.wait()                     # the issuing stream waits for the collective
+            if on_gpu:
+                ev = torch.cuda.Event()
+                ev.record()
+                events.append(ev)
+            else:
+                events.append(None)
+    return events
+
+
+class _null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
 
 
 def broadcast_resident(tensor, dist, src: int = 0):

@@ -26,6 +26,7 @@ Options& options() {
         if (const char* t = getenv("BAFE_TC_PAIR")) o.tc_pair = atoi(t) != 0;
         if (const char* h = getenv("BAFE_HOST_PANELS")) o.host_panels = strcmp(h, "auto") == 0 ? -1 : atoi(h);
         if (const char* c = getenv("BAFE_TC_CONVERT")) o.tc_convert = strcmp(c, "auto") == 0 ? -1 : (atoi(c) != 0);
+        if (const char* f = getenv("BAFE_KSLICE_FREE_SMS")) o.kslice_free_sms = atoi(f) > 0 ? atoi(f) : 0;
     }
     return o;
 }
@@ -332,6 +333,21 @@ BAFE_API int bafe_cuda_run_device(int plan, void* const* ptrs, int n_ptrs, void*
     return run_plan_device(*p, ptrs, n_ptrs, stream);
 }
 
+BAFE_API int bafe_cuda_plan_k_slice_align(int plan) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return -1; }
+    return plan_k_slice_align(*p);
+}
+
+BAFE_API int bafe_cuda_run_device_ksliced(int plan, void* const* ptrs, int n_ptrs, void* stream, int n_slices,
+                                          const int64_t* k_bounds, void* const* ready) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
+    return run_plan_device_ksliced(*p, ptrs, n_ptrs, stream, n_slices, k_bounds, ready);
+}
+
 BAFE_API int bafe_cuda_run_host(int plan, void* const* ptrs, int n_ptrs) {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     Plan* p = plan_ptr(plan);
@@ -376,6 +392,13 @@ BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
         o.tc_convert = v == "auto" ? -1 : (v == "1");
         return 0;
     }
+    if (k == "kslice_free_sms") {
+        char* end = nullptr;
+        long n = strtol(value, &end, 10);
+        if (!end || *end || n < 0 || n > 1024) return -1;
+        o.kslice_free_sms = (int)n;
+        return 0;
+    }
     if (k == "host_panels") {
         if (v == "auto") { o.host_panels = -1; return 0; }
         char* end = nullptr;
@@ -404,6 +427,7 @@ BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
     else if (k == "tc_pair") v = o.tc_pair ? "1" : "0";
     else if (k == "tc_convert") v = o.tc_convert < 0 ? "auto" : (o.tc_convert ? "1" : "0");
     else if (k == "host_panels") v = o.host_panels < 0 ? "auto" : std::to_string(o.host_panels);
+    else if (k == "kslice_free_sms") v = std::to_string(o.kslice_free_sms);
     else return -1;
     if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());
     return 0;

@@ -79,6 +79,7 @@ struct Options {
     bool tc_pair = true;                    // tensor-core GEMM on CTA pairs (cta_group::2)
     int host_panels = -1;                   // host calls: -1 auto, 0/1 off, n: n row panels
     int tc_convert = -1;                    // 3xTF32 residuals inside the kernel: 1 yes, 0 no, -1 auto (small GEMMs)
+    int kslice_free_sms = 0;                // K-sliced runs: SMs every slice but the last leaves to other streams
 };
 Options& options();
 
@@ -186,6 +187,13 @@ std::string sha256_hex(const void* data, size_t len);
 
 // Runtime (runtime.cpp).
 int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
+// The plan (tf32 pre-passes + one CTA-pair GEMM) over K slices
+// [k_bounds[j], k_bounds[j+1]); slice j's launches wait for ready[j] (a
+// cudaEvent_t, or null).  plan_k_slice_align: the multiple of K slice
+// bounds must be, 0 if the plan cannot be sliced.
+int run_plan_device_ksliced(Plan& p, void* const* ptrs, int n_ptrs, void* stream, int n_slices,
+                            const int64_t* k_bounds, void* const* ready);
+int plan_k_slice_align(const Plan& p);
 // resident: per input, nonzero = ptrs[k] is already a device buffer (or null: none);
 // ready: cudaEvent_t the kernels wait for before reading them (or null)
 int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident = nullptr,

@@ -87,6 +87,15 @@ struct TcArgs {
     int split_first;               // first split tile: tiles [split_first, num_tiles) are split
     int num_units;                 // split_first + (num_tiles - split_first) * split
     unsigned* wave_ctr;            // wave alignment counter (zero at launch), or null
+    // K slices (CTA-pair kernel): this launch covers k-blocks [kb_first,
+    // kb_last), kb_first a multiple of the promotion chunk, so every output
+    // still sums the same chunk partials in the same order.  acc_in: each
+    // tile's sums start from the fp32 values in `out` (the previous slice's);
+    // acc_raw: the sums are stored to `out` as they are, without the
+    // epilogue (a later slice continues them).  A whole-K launch has
+    // kb_first 0, kb_last 0 (all k-blocks) and both flags 0.
+    int kb_first, kb_last;
+    int acc_in, acc_raw;
 };
 static_assert(sizeof(TcArgs) == 1024, "TcArgs layout (mirrored by the host)");
 
@@ -483,6 +492,8 @@ __device__ __forceinline__ void tile_coords(const TcArgs& g, int t, int& mb, int
 // Measured on a 256^3 tf32 pair tile: relu(acc + C) 41k -> 12k cycles,
 // plain stores 9.3k -> 4.5k.  Results of at most 4 bytes are kept, as
 // bits, in the accumulator registers between the passes.
+template <class T> struct tc_is_f32 { static constexpr bool value = false; };
+template <> struct tc_is_f32<float> { static constexpr bool value = true; };
 constexpr u32 EPI_OFFSET = 1024;                 // staging: after the ring's mbarriers and Shared words
 constexpr u32 EPI_WARP_BYTES = 4096;             // 32 rows x 128 bytes per accumulate warp
 __device__ __forceinline__ float tc_pack_bits(float x) { return x; }
@@ -615,6 +626,38 @@ __device__ __forceinline__ void tc_epilogue(float (&acc)[128], const TcArgs& g, 
 // the warp's bulk stores have completed.
 __device__ __forceinline__ void tc_epilogue_flush(int lane) {
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// K slices: lane r's row i0 + r, columns n0 .. n0+127, of the fp32 sums a
+// previous slice left in `out` (16-byte loads; N % 4 == 0 keeps the rows
+// 16-byte aligned), rows >= M and columns >= N read as 0.
+__device__ __forceinline__ void tc_load_sums(float (&acc)[128], const TcArgs& g, i64 bi, i64 i0, i64 n0, int lane) {
+    const i64 i = i0 + lane;
+    if (i >= g.M) return;
+    const float* row = reinterpret_cast<const float*>(g.out) + bi * g.o_bstride + i * g.N + n0;
+#pragma unroll
+    for (int v = 0; v < 128; v += 4) {
+        if (n0 + v < g.N) {
+            const float4 x = *reinterpret_cast<const float4*>(row + v);
+            acc[v] = x.x; acc[v + 1] = x.y; acc[v + 2] = x.z; acc[v + 3] = x.w;
+        }
+    }
+}
+// ... and the sums stored back unchanged (no epilogue) for the next slice:
+// through the output's TMA map (kept in L2: the next slice reads them), or
+// plain 16-byte stores.
+__device__ __forceinline__ void tc_store_sums(const float (&acc)[128], const TcArgs& g, i64 bi, i64 i0, i64 n0,
+                                              u32 stg, int lane) {
+    if (g.out_tma) {
+        tc_store_rows<float, false>(acc, &g.tmap_out, n0, i0, bi, g.N, stg, lane);
+        return;
+    }
+    const i64 i = i0 + lane;
+    if (i >= g.M) return;
+    float* row = reinterpret_cast<float*>(g.out) + bi * g.o_bstride + i * g.N + n0;
+#pragma unroll
+    for (int v = 0; v < 128; v += 4)
+        if (n0 + v < g.N) *reinterpret_cast<float4*>(row + v) = make_float4(acc[v], acc[v + 1], acc[v + 2], acc[v + 3]);
 }
 
 // Split tail tiles: out = epi(sum of the K-range partials in ws, in part
@@ -1039,7 +1082,15 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
     tc_fence_after();
     const u32 tmem = sh->tmem_base;
     const int k_blocks = (int)((g.K + BKE - 1) / BKE);
-    const int n_chunks = (k_blocks + KB_PER_CHUNK - 1) / KB_PER_CHUNK;
+    // this launch's K slice: k-blocks [kb_first, kb_hi), chunks from c_first
+    const int kb_hi = g.kb_last > 0 && g.kb_last < k_blocks ? g.kb_last : k_blocks;   // 0: all
+    const int c_first = g.kb_first / KB_PER_CHUNK;
+    const int n_chunks = (kb_hi + KB_PER_CHUNK - 1) / KB_PER_CHUNK - c_first;
+    auto unit_chunks = [&](int u, int& t, int& c0, int& c1, int& part) {
+        unit_range(g, u, n_chunks, t, c0, c1, part);
+        c0 += c_first;
+        c1 += c_first;
+    };
 
     if (warp == 0) {
         // ---------------------------------------- TMA producer (both CTAs) --
@@ -1052,11 +1103,11 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             bool align_on = true;
             for (int u = pair; ok && u < g.num_units; u += num_pairs) {
                 int t, c0, c1, part;
-                unit_range(g, u, n_chunks, t, c0, c1, part);
+                unit_chunks(u, t, c0, c1, part);
                 int mb, nb, bi;
                 tile_coords(g, t, mb, nb, bi);
                 const int m0 = mb * 2 * BM + (int)cta * BM, n0 = nb * BN + (int)cta * (BN / 2);
-                const int kb_stop = c1 * KB_PER_CHUNK < k_blocks ? c1 * KB_PER_CHUNK : k_blocks;
+                const int kb_stop = c1 * KB_PER_CHUNK < kb_hi ? c1 * KB_PER_CHUNK : kb_hi;
                 const int za = g.a_batched ? bi : 0, zb = g.b_batched ? bi : 0;
                 // Wave alignment (advisory): the leader's producer starts the
                 // loads of wave w once every pair has issued all of wave
@@ -1148,14 +1199,14 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             bool ok = true;
             for (int u = pair; ok && u < g.num_units; u += num_pairs) {
                 int t, c0, c1, part;
-                unit_range(g, u, n_chunks, t, c0, c1, part);
+                unit_chunks(u, t, c0, c1, part);
                 for (int c = c0; ok && c < c1; ++c, ++chunk) {
                     const int buf = (int)(chunk & 1u);
                     const u32 use = (chunk >> 1) & 1u;
                     if (!wait(TEMPTY(buf), use ^ 1u, sh, g, 2u)) { ok = false; break; }
                     tc_fence_after();
                     const u32 d = tmem + (u32)(buf * BN);
-                    const int kb_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                    const int kb_end = (c + 1) * KB_PER_CHUNK < kb_hi ? (c + 1) * KB_PER_CHUNK : kb_hi;
                     for (int kb = c * KB_PER_CHUNK; kb < kb_end; ++kb) {
                         const bool ready = CONV ? wait_cluster(LO(s), phase, sh, g, 3u) : wait(FULL(s), phase, sh, g, 3u);
                         if (!ready) { ok = false; break; }
@@ -1235,18 +1286,28 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
         };
         for (int u = pair; ok && u < g.num_units; u += num_pairs) {
             int t, c0, c1, part;
-            unit_range(g, u, n_chunks, t, c0, c1, part);
+            unit_chunks(u, t, c0, c1, part);
             // k-blocks this CTA still has after the current tile, capped
-            // (with converted residuals the tiles are never split: u == t)
+            // (with converted residuals the tiles are never split: u == t,
+            // and never sliced: the launch covers all k-blocks)
             const long long after = (long long)(g.num_units - 1 - u) / num_pairs * k_blocks;
             const int limit = k_blocks + (after < KB_PER_CHUNK ? (int)after : KB_PER_CHUNK);
             float acc[128];
 #pragma unroll
             for (int e = 0; e < 128; ++e) acc[e] = 0.0f;
+            // a K slice after the first continues the sums the previous one
+            // stored (the first K range of a split tile carries them)
+            if constexpr (tc_is_f32<typename Spec::Out>::value) {
+                if (g.acc_in && part <= 0) {
+                    int mb, nb, bi;
+                    tile_coords(g, t, mb, nb, bi);
+                    tc_load_sums(acc, g, bi, (i64)mb * 2 * BM + (i64)cta * BM + q * 32, (i64)nb * BN + half * 128, lane);
+                }
+            }
             for (int c = c0; c < c1; ++c, ++chunk) {
                 const int buf = (int)(chunk & 1u);
                 const u32 use = (chunk >> 1) & 1u;
-                const int c_end = (c + 1) * KB_PER_CHUNK < k_blocks ? (c + 1) * KB_PER_CHUNK : k_blocks;
+                const int c_end = (c + 1) * KB_PER_CHUNK < kb_hi ? (c + 1) * KB_PER_CHUNK : kb_hi;
                 const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
                 const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
                 if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
@@ -1273,7 +1334,10 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
             tile_coords(g, t, mb, nb, bi);
             const i64 i0 = (i64)mb * 2 * BM + (i64)cta * BM + q * 32;
             const i64 n0 = (i64)nb * BN + half * 128;
-            if (part < 0) tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
+            bool raw = false;
+            if constexpr (tc_is_f32<typename Spec::Out>::value) raw = g.acc_raw != 0;
+            if (part < 0 && raw) tc_store_sums(acc, g, bi, i0, n0, stg, lane);
+            else if (part < 0) tc_epilogue<Spec>(acc, g, bi, i0, n0, out, stg, lane);
             else tc_store_rows<float, false>(acc, &g.tmap_ws, half * 128,
                                              ((i64)(t - g.split_first) * g.split + part) * 2 * BM + cta * BM + q * 32, 0, 256,
                                              stg, lane);

@@ -461,10 +461,33 @@ int ensure_tmps(Plan& p, DeviceState* ds) {
 // Which steps one pass of run_steps launches: all of them over the whole
 // problem, only the once-per-call steps, or the per-panel steps over output
 // rows [r0, r0 + rows).
+// KPrep / KSlice: a plan of tf32 pre-passes and one CTA-pair GEMM run over
+// K slices (run_plan_device_ksliced): KPrep runs A's residual pre-pass over
+// all of A; KSlice runs B's split pre-pass over rows [k0, k1) of B and the
+// GEMM over K range [k0, k1), continuing (first false) and leaving (last
+// false) its sums in the output.
 struct Pass {
-    enum Kind { All, Once, Panel } kind = All;
+    enum Kind { All, Once, Panel, KPrep, KSlice } kind = All;
     int64_t r0 = 0, rows = 0;
+    int64_t k0 = 0, k1 = 0;
+    bool first = true, last = true;
 };
+
+bool same_buf(const BufRef& a, const BufRef& b) { return a.kind == b.kind && a.idx == b.idx; }
+
+// Role of step si in a K-sliced plan: 0 the GEMM (last step), 1 A's
+// residual pre-pass (writes aux[0]), 2 B's split pre-pass (writes aux[1]
+// and aux[2]), -1 anything else (the plan cannot be sliced).
+int k_slice_role(const Plan& p, size_t si) {
+    const Step& G = p.steps.back();
+    const Step& s = p.steps[si];
+    if (si + 1 == p.steps.size()) return 0;
+    if (s.kind != StepKind::Ew || G.aux.size() < 3 || s.srcs.size() != 1) return -1;
+    if (!s.has_dst2 && same_buf(s.dst, G.aux[0]) && same_buf(s.srcs[0], G.srcs[0])) return 1;
+    if (s.has_dst2 && same_buf(s.dst, G.aux[1]) && same_buf(s.dst2, G.aux[2]) && same_buf(s.srcs[0], G.srcs[1]))
+        return 2;
+    return -1;
+}
 
 int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t stream, const Pass& pass) {
     auto ptr_of = [&](const BufRef& b) -> void* {
@@ -479,10 +502,31 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
     auto at_row = [&](void* base, int64_t row_bytes) -> void* {
         return cut && row_bytes ? static_cast<void*>(static_cast<char*>(base) + pass.r0 * row_bytes) : base;
     };
+    const bool ksl = pass.kind == Pass::KPrep || pass.kind == Pass::KSlice;
     for (size_t si = 0; si < p.steps.size(); ++si) {
         Step& s = p.steps[si];
         if (pass.kind == Pass::Once && s.panel) continue;
         if (pass.kind == Pass::Panel && !s.panel) continue;
+        // K slices: A's residual once (KPrep); B's split over the slice's
+        // rows of B and the GEMM over its K range (KSlice)
+        const int role = ksl ? k_slice_role(p, si) : -1;
+        if (ksl && (pass.kind == Pass::KPrep) != (role == 1)) continue;
+        if (ksl && role == 2) {
+            const int64_t off = pass.k0 * p.steps.back().N;            // B row-major: rows are contiguous
+            const int64_t cnt = (pass.k1 - pass.k0) * p.steps.back().N;
+            if (cnt == 0) continue;
+            char* bsrc = static_cast<char*>(ptr_of(s.srcs[0])) + off * s.src_esize[0];
+            char* lo = static_cast<char*>(ptr_of(s.dst)) + off * 4;
+            char* hi = static_cast<char*>(ptr_of(s.dst2)) + off * 4;
+            const bool vec = ds->fn_vec[si] != nullptr && ((uintptr_t)bsrc | (uintptr_t)lo | (uintptr_t)hi) % 16 == 0;
+            uint64_t args[5] = {(uint64_t)(uintptr_t)bsrc, (uint64_t)(uintptr_t)lo, (uint64_t)cnt, (uint64_t)s.ncols,
+                                (uint64_t)(uintptr_t)hi};
+            void* params[] = {args};
+            if (int rc = launch(vec ? ds->fn_vec[si] : ds->fn[si], grid_for(vec ? cnt / 4 : cnt, dev), 1, 1, 256, 1, 1, 0,
+                                stream, params))
+                return rc;
+            continue;
+        }
         void* dst = at_row(ptr_of(s.dst), s.dst_rb);
         const int64_t n_run = cut ? pass.rows * s.row_elems : s.n;
         const int64_t m_run = cut ? pass.rows : s.M;
@@ -592,7 +636,23 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 const void* key[15] = {a, b, a_lo, b_lo, dst, err_word};
                 for (int k = 0; k < s.n_epi && k < 8; ++k) key[6 + k] = ep[k];
                 key[14] = ds->tc_ws;
-                bool hit = cached.valid && cached.rows == m_run;
+                TcLaunch sliced;                             // K slice: no split tail, not cached
+                if (pass.kind == Pass::KSlice) {
+                    if (int rc = tc_prepare(run, a, b, a_lo, b_lo, dst, ep, sm_count(dev), err_word, nullptr, 0,
+                                            ds->tc_ctr, sliced, err)) {
+                        set_error(rc, err);
+                        return rc;
+                    }
+                    tc_set_k_slice(sliced, pass.k0, pass.k1, s.K, !pass.first, !pass.last, s.tc_elem == 1);
+                    // every slice but the last may leave SMs to the streams that
+                    // bring the next slabs in (a kernel queued there cannot start
+                    // on an SM this persistent kernel fills)
+                    const int free_pairs = (options().kslice_free_sms + 1) / 2;
+                    const int pairs = sm_count(dev) / 2;
+                    if (!pass.last && free_pairs > 0 && sliced.cluster == 2 && (int)sliced.grid / 2 > pairs - free_pairs)
+                        sliced.grid = (unsigned)(2 * std::max(1, pairs - free_pairs));
+                }
+                bool hit = pass.kind == Pass::KSlice || (cached.valid && cached.rows == m_run);
                 for (int k = 0; hit && k < 15; ++k) hit = cached.key[k] == key[k];
                 if (!hit) {
                     int rc = tc_prepare(run, a, b, a_lo, b_lo, dst, ep, sm_count(dev), err_word,
@@ -606,7 +666,7 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                     cached.rows = m_run;
                     cached.valid = true;
                 }
-                TcLaunch& L = cached.L;
+                TcLaunch& L = pass.kind == Pass::KSlice ? sliced : cached.L;
                 if (L.wave_sync) {
                     cudaError_t e = cudaMemsetAsync(ds->tc_ctr, 0, sizeof(unsigned), stream);
                     if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("cudaMemsetAsync: ") + cudaGetErrorString(e)); return 7; }
@@ -706,6 +766,70 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
 }
 
 }  // namespace
+
+int run_plan_device_ksliced(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v, int n_slices,
+                            const int64_t* k_bounds, void* const* ready) {
+    if (n_ptrs != p.n_inputs + 1) {
+        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
+        return 8;
+    }
+    const int64_t align = p.steps.empty() ? 0 : tc_k_slice_align(p.steps.back());
+    if (!align) {
+        set_error(8, "K slices need a plan whose last step is a CTA-pair tensor-core GEMM with an fp32 output, "
+                     "unbatched, B row-major");
+        return 8;
+    }
+    for (size_t si = 0; si + 1 < p.steps.size(); ++si)
+        if (k_slice_role(p, si) < 0) {
+            set_error(8, "K slices: the plan has steps other than the GEMM's tf32 pre-passes");
+            return 8;
+        }
+    const int64_t K = p.steps.back().K;
+    if (n_slices < 1 || !k_bounds || k_bounds[0] != 0 || k_bounds[n_slices] != K) {
+        set_error(8, "K slices: bounds must run from 0 to K = " + std::to_string(K));
+        return 8;
+    }
+    for (int j = 0; j < n_slices; ++j)
+        if (k_bounds[j + 1] <= k_bounds[j] || (j + 1 < n_slices && k_bounds[j + 1] % align)) {
+            set_error(8, "K slices: bounds must increase and be multiples of " + std::to_string(align));
+            return 8;
+        }
+    int dev = 0;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, std::string("no CUDA device available (") + cudaGetErrorString(ce) + ")");
+        return 4;
+    }
+    DeviceState* ds = nullptr;
+    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+    if (int rc = ensure_tmps(p, ds)) return rc;
+    cudaStream_t st = (cudaStream_t)stream_v;
+    Pass prep;
+    prep.kind = Pass::KPrep;
+    if (int rc = run_steps(p, ds, dev, ptrs, st, prep)) return rc;
+    for (int j = 0; j < n_slices; ++j) {
+        if (ready && ready[j]) {
+            cudaError_t e = cudaStreamWaitEvent(st, (cudaEvent_t)ready[j], 0);
+            if (e != cudaSuccess) { cudaGetLastError(); set_error(7, std::string("cudaStreamWaitEvent: ") + cudaGetErrorString(e)); return 7; }
+        }
+        Pass sl;
+        sl.kind = Pass::KSlice;
+        sl.k0 = k_bounds[j];
+        sl.k1 = k_bounds[j + 1];
+        sl.first = j == 0;
+        sl.last = j + 1 == n_slices;
+        if (int rc = run_steps(p, ds, dev, ptrs, st, sl)) return rc;
+    }
+    return 0;
+}
+
+int plan_k_slice_align(const Plan& p) {
+    if (p.steps.empty()) return 0;
+    for (size_t si = 0; si + 1 < p.steps.size(); ++si)
+        if (k_slice_role(p, si) < 0) return 0;
+    return tc_k_slice_align(p.steps.back());
+}
 
 int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v) {
     if (n_ptrs != p.n_inputs + 1) {

@@ -38,6 +38,8 @@ struct alignas(64) TcArgsHost {
     float* ws;
     int32_t split, split_first, num_units;
     unsigned* wave_ctr;
+    int32_t kb_first, kb_last;     // K slice in k-blocks (kb_last 0: all)
+    int32_t acc_in, acc_raw;       // continue / leave the sums in the output
 };
 static_assert(sizeof(CUtensorMap) == 128, "CUtensorMap size");
 static_assert(sizeof(TcArgsHost) == 1024, "TcArgs layout");
@@ -254,6 +256,23 @@ int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, co
     L.block = (unsigned)threads_of(s.tc_variant);
     L.smem = (unsigned)tc_smem_bytes(s.tc_variant, s.tc_pair);
     return 0;
+}
+
+int tc_k_slice_align(const Step& s) {
+    if (s.kind != StepKind::GemmTc || !s.tc_pair || s.tc_convert || s.dst_esize != 4 || s.batch > 1 || s.b_col)
+        return 0;
+    return chunk_kblocks(s) * (s.tc_elem == 1 ? 64 : 32);
+}
+
+void tc_set_k_slice(TcLaunch& L, int64_t k0, int64_t k1, int64_t K, bool acc_in, bool acc_raw, bool elem_bf16) {
+    TcArgsHost h;
+    memcpy(&h, L.args, sizeof(h));
+    const int64_t bke = elem_bf16 ? 64 : 32;
+    h.kb_first = (int32_t)(k0 / bke);
+    h.kb_last = k1 >= K ? 0 : (int32_t)(k1 / bke);
+    h.acc_in = acc_in ? 1 : 0;
+    h.acc_raw = acc_raw ? 1 : 0;
+    memcpy(L.args, &h, sizeof(h));
 }
 
 }  // namespace bafe_cuda

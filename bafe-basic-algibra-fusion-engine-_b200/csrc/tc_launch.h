@@ -30,6 +30,15 @@ int tc_smem_bytes(int variant, bool pair = false);
 int tc_prepare(const Step& s, const void* a, const void* b, const void* a_lo, const void* b_lo, void* out,
                const std::vector<const void*>& ep, int sm_count, unsigned* err_word, void* ws, size_t ws_bytes,
                unsigned* wave_ctr, TcLaunch& L, std::string& err);
+// K slices of a CTA-pair GEMM whose output is fp32 (its sums are carried
+// through the output between slices): the multiple of K, in elements, that
+// slice boundaries must be (one promotion chunk, so that the summation
+// order is the whole launch's), or 0 when the step cannot be sliced
+// (single-CTA or converting kernel, batched, col-major B, other output type).
+int tc_k_slice_align(const Step& s);
+// Makes a prepared launch (no split tail: ws null) cover K range [k0, k1):
+// acc_in continues the sums in the output, acc_raw leaves them there.
+void tc_set_k_slice(TcLaunch& L, int64_t k0, int64_t k1, int64_t K, bool acc_in, bool acc_raw, bool elem_bf16);
 // elem: 0 = u8, 1 = f32, 2 = bf16; swizzle: 0 none, 1 = 128B, 2 = 128B with 32-byte atoms
 int tc_encode_tensor_map(void* map, int elem, int rank, void* gaddr, const uint64_t* dims,
                          const uint64_t* strides_bytes, const uint32_t* box, int swizzle, std::string& err);

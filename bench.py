@@ -220,6 +220,45 @@ def time_steps(torch, kernel, ins, out, steps, warmup):
     return per, ev[0].elapsed_time(ev[steps]), launches
 
 
+def time_bcast_steps(c, kernel, ins, out, bounds, free_sms, steps, warmup):
+    """Steps whose B arrives inside the step: rank 0's B is broadcast slab by
+    slab (rows [bounds[j], bounds[j+1])) over NCCL on a side stream, and the
+    plan runs in K slices, slice j waiting for slab j
+    (Kernel.run_torch_ksliced); bounds [0, K] is the broadcast followed by
+    the whole GEMM.  Every step's broadcast starts after the previous step's
+    work (an event on the launching stream).  -> (max-over-ranks ms of the
+    timed region, GEMM launches counted)."""
+    import bafe_b200 as bafe
+    from bafe_b200.parallel import broadcast_slabs
+    torch = c.torch
+    cur = torch.cuda.current_stream()
+    comm = torch.cuda.Stream()
+    bafe.set_option("kslice_free_sms", str(free_sms))
+
+    def step(start):
+        start.record(cur)
+        comm.wait_event(start)
+        evs = broadcast_slabs(ins[1], bounds, c.dist, 0, comm)
+        kernel.run_torch_ksliced(ins, out, bounds, ready=evs, stream=cur)
+
+    try:
+        for _ in range(warmup):
+            step(torch.cuda.Event())
+        torch.cuda.synchronize()
+        c.barrier()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+        launches0 = bafe.launch_count()
+        for i in range(steps):
+            step(ev[i])
+        ev[steps].record(cur)
+        torch.cuda.synchronize()
+        launches = bafe.launch_count() - launches0
+    finally:
+        bafe.set_option("kslice_free_sms", "0")
+    c.barrier()
+    return c.max(ev[0].elapsed_time(ev[steps])), launches
+
+
 class _NpPtr:
     """A numpy array seen through time_e2e's data_ptr() (pageable host memory)."""
 
@@ -494,6 +533,25 @@ def bench_gemm(c: Ctx) -> dict:
         "gpu_launches": launches, "clocks": clocks, "b_broadcast_ms": round(bcast_ms, 3),
         "compile_s": round(t_compile, 2),
     }
+    if c.world > 1 and epi == "c":
+        # B crosses NVLink inside every step (the same workload when B changes
+        # from call to call): broadcast, then the GEMM; and broadcast in K
+        # slabs overlapped with the GEMM's K slices
+        from bafe_b200.parallel import k_slices
+        variants = {"b_broadcast_in_step": ([0, S], 0)}
+        if k.k_slice_align:
+            free = int(os.environ.get("BENCH_KSLICE_FREE_SMS", "16"))
+            variants["b_broadcast_overlapped"] = (k_slices(S, k.k_slice_align), free)
+        for name, (bounds, free) in variants.items():
+            ms_total, n_launch = time_bcast_steps(c, k, ins, out, bounds, free, args.steps, args.warmup)
+            ms = ms_total / args.steps
+            res[name] = {"value": round(flops_total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+                         "ms_per_step": round(ms, 4), "k_slabs": bounds, "free_sms_while_slabs_arrive": free,
+                         "gpu_launches": int(c.sum(n_launch)),
+                         "how": "rank 0's B broadcast over NCCL inside each timed step ("
+                                + ("one piece, then the GEMM" if len(bounds) == 2 else
+                                   f"{len(bounds) - 1} K slabs on a side stream; GEMM K slice j waits for slab j")
+                                + "); max over ranks"}
     if args.e2e_steps > 0 and epi == "c":
         hA, hB, hC = A.cpu().pin_memory(), B.cpu().pin_memory(), C.cpu().pin_memory()
         hO = torch.empty(rows, S).pin_memory()

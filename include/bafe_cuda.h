@@ -235,6 +235,28 @@ int bafe_cuda_plan_row_split(int plan, int64_t *rows, int64_t *in_row_bytes, int
  * nonzero code with the message available from bafe_cuda_last_error. */
 int bafe_cuda_run_device(int plan, void *const *ptrs, int n_ptrs, void *stream);
 
+/* K-sliced device run, for a multi-GPU caller whose B arrives over NVLink
+ * in slabs of rows while the GEMM runs.  The plan must be one CTA-pair
+ * tensor-core GEMM (with its tf32 pre-passes) with an fp32 output,
+ * unbatched, B row-major (any row-major layout tag).  Slice j covers K
+ * range [k_bounds[j], k_bounds[j+1]) (k_bounds[0] = 0, k_bounds[n_slices] =
+ * K, interior bounds multiples of bafe_cuda_plan_k_slice_align(plan)): its
+ * launches -- B's tf32 split over rows [k_j, k_{j+1}) of B, then the GEMM
+ * over that K range -- wait on ready[j] (a cudaEvent_t recorded after the
+ * slab's copy; NULL array or entry: no wait).  The sums are carried
+ * through the output between slices, in the same chunk order as one
+ * launch, and the epilogue runs on the last slice, so the result equals
+ * bafe_cuda_run_device's bit for bit.  Asynchronous, like
+ * bafe_cuda_run_device.  Extension (multi-GPU B broadcast overlapped with
+ * compute): the reference is single-threaded.  Returns 0 or a nonzero code. */
+int bafe_cuda_run_device_ksliced(int plan, void *const *ptrs, int n_ptrs, void *stream, int n_slices,
+                                 const int64_t *k_bounds, void *const *ready);
+/* The multiple of K that interior slice bounds of
+ * bafe_cuda_run_device_ksliced must be (the GEMM's promotion chunk in
+ * elements), 0 when the plan cannot run in K slices, -1 for an unknown
+ * plan. */
+int bafe_cuda_plan_k_slice_align(int plan);
+
 /* Same as calling the plan's function: host pointers, synchronous.
  * Returns 0 or a nonzero code. */
 int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);
@@ -286,6 +308,11 @@ void bafe_cuda_clear_error(void);
  *                     with the kernels; auto = one panel per 96 MiB of
  *                     row-split bytes, 8 to 32, once they exceed 64 MiB;
  *                     0 or 1 = one piece (read at each call)
+ *   "kslice_free_sms": "0" (default) | n: bafe_cuda_run_device_ksliced
+ *                     launches every slice but the last on all SMs but n
+ *                     (rounded up to CTA pairs), so that kernels queued on
+ *                     other streams -- the collective bringing the next
+ *                     slab -- can run beside it (read at each call)
  *   "device":         CUDA device ordinal used by host-pointer calls
  *                     (default: the current device)
  * Environment variables BAFE_GEMM_PRECISION, BAFE_TC_PAIR, BAFE_TC_CONVERT,

@@ -215,3 +215,80 @@ def test_shared_input_assembled_from_slabs(world):
     while not q.empty():
         out.append(q.get())
     assert out == [("ok", True)] * world, out
+
+
+def test_k_slices_are_chunk_aligned_and_grow():
+    from bafe_b200.parallel import k_slices
+    for K, align in [(16384, 64), (16384, 1024), (16384, 2048), (4096, 64), (2048, 64), (64, 64), (1000, 64)]:
+        b = k_slices(K, align)
+        assert b[0] == 0 and b[-1] == K
+        assert all(b[i] < b[i + 1] for i in range(len(b) - 1))
+        assert all(x % align == 0 for x in b[1:-1])
+        sizes = [b[i + 1] - b[i] for i in range(len(b) - 1)]
+        # geometric growth up to the last slab, which is never under half of the one before
+        assert all(sizes[i + 1] >= sizes[i] for i in range(len(sizes) - 2))
+        if len(sizes) > 2:
+            assert 2 * sizes[-1] >= sizes[-2]
+    assert k_slices(16384, 64) == [0, 1024, 3072, 7168, 16384]
+
+
+def test_transpose_blocks_cover_the_output_rows():
+    """Each rank writes rows [c0, c1) of transpose(X) = columns [c0, c1) of
+    X; together the blocks are the whole transpose."""
+    from bafe_b200.parallel import transpose_blocks
+    rng = np.random.default_rng(2)
+    for rows, cols, world in [(300, 1000, 8), (64, 130, 3), (5, 7, 2), (16384 // 64, 16384, 8)]:
+        X = rng.standard_normal((rows, cols)).astype(np.float32)
+        blocks = transpose_blocks(cols, world)
+        assert blocks[0][0] == 0 and blocks[-1][1] == cols
+        assert all(blocks[i][1] == blocks[i + 1][0] for i in range(world - 1))
+        if cols >= 64 * world:
+            assert all(a % 64 == 0 for a, _ in blocks)
+        parts = [np.ascontiguousarray(X[:, a:b].T) for a, b in blocks]   # each rank's own output rows
+        assert np.concatenate(parts, axis=0).tobytes() == np.ascontiguousarray(X.T).tobytes()
+
+
+def _slab_worker(rank, world, port, q):
+    for p in PATHS:
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from bafe_b200.parallel import broadcast_slabs, k_slices
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    try:
+        K, N = 1000, 24
+        want = torch.arange(K * N, dtype=torch.float32).reshape(K, N) * 0.5 - 3
+        B = want.clone() if rank == 0 else torch.full((K, N), float("nan"))
+        bounds = k_slices(K, 64)
+        evs = broadcast_slabs(B, bounds, dist, src=0)
+        q.put(("ok", bool(torch.equal(B, want)) and len(evs) == len(bounds) - 1 and len(bounds) > 2))
+    except Exception as e:
+        q.put(("error", f"rank {rank}: {type(e).__name__}: {e}"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_b_broadcast_in_k_slabs(world):
+    """B crosses from the root slab by slab (contiguous row ranges); every
+    rank ends with the root's B."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_slab_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    out = []
+    while not q.empty():
+        out.append(q.get())
+    assert out == [("ok", True)] * world, out
