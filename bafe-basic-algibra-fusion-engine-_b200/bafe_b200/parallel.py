@@ -87,6 +87,41 @@ def k_slices(K: int, align: int, first: int = 0, growth: float = 2.0, max_slices
     return bounds
 
 
+def k_slab_schedule(K: int, align: int, t_gemm_ms: float, t_bcast_ms: float, boundary_ms: float,
+                    keep: float = 1.0, max_slices: int = 6) -> List[int]:
+    """K slab bounds for a GEMM over a B that is broadcast in the same step.
+
+    t_gemm_ms / t_bcast_ms: the GEMM over all of K and the broadcast of all
+    of B, measured; keep: the fraction of the SMs the GEMM slices keep while
+    a slab is in flight; boundary_ms: the cost of one more slice (its sums
+    stored and reloaded).  Slab j+1 is R = t_gemm / (keep * t_bcast) times
+    slab j, so its broadcast ends as slice j's GEMM does; with n slabs the
+    step costs the first slab's broadcast (nothing overlaps it), the slower
+    slices 0..n-2 and n-1 boundaries.  Returns the bounds of the n in
+    [2, max_slices] with the least cost ([0, K] when slicing cannot help)."""
+    if align <= 0 or K < 2 * align or t_bcast_ms <= 0:
+        return [0, K]
+    R = max(1.0, t_gemm_ms / (keep * t_bcast_ms))
+    best, best_cost = [0, K], t_bcast_ms             # no slicing: the whole broadcast is exposed
+    for n in range(2, max_slices + 1):
+        w = [R ** j for j in range(n)]
+        tot = sum(w)
+        bounds, acc = [0], 0.0
+        for j in range(n - 1):
+            acc += K * w[j] / tot
+            b = int(round(acc / align)) * align
+            if b <= bounds[-1] or b >= K:
+                break
+            bounds.append(b)
+        else:
+            bounds.append(K)
+            first, last = bounds[1] / K, (K - bounds[-2]) / K
+            cost = t_bcast_ms * first + t_gemm_ms * (1.0 / keep - 1.0) * (1.0 - last) + (n - 1) * boundary_ms
+            if cost < best_cost:
+                best, best_cost = bounds, cost
+    return best
+
+
 def broadcast_slabs(B, bounds: Sequence[int], dist, src: int = 0, stream=None):
     """Broadcast the rows [bounds[j], bounds[j+1]) of B (row-major, shape
     (K, ...)) from `src`, slab by slab, in place.  On CUDA the broadcasts

@@ -537,14 +537,24 @@ def bench_gemm(c: Ctx) -> dict:
         # B crosses NVLink inside every step (the same workload when B changes
         # from call to call): broadcast, then the GEMM; and broadcast in K
         # slabs overlapped with the GEMM's K slices
-        from bafe_b200.parallel import k_slices
+        from bafe_b200.parallel import k_slab_schedule
         variants = {"b_broadcast_in_step": ([0, S], 0)}
         if k.k_slice_align:
-            free = int(os.environ.get("BENCH_KSLICE_FREE_SMS", "16"))
-            variants["b_broadcast_overlapped"] = (k_slices(S, k.k_slice_align), free)
+            variants["b_broadcast_overlapped"] = (None, int(os.environ.get("BENCH_KSLICE_FREE_SMS", "16")))
+        ms_plain = None
         for name, (bounds, free) in variants.items():
+            if bounds is None:
+                # slabs sized from the two times just measured (the GEMM with B
+                # resident, the broadcast = the plain variant's excess): each
+                # slab's broadcast hides behind the previous slab's GEMM slice
+                sms = torch.cuda.get_device_properties(c.dev).multi_processor_count
+                boundary_ms = 2.0 * out.numel() * 4 / (c.hbm_peak * 1e9) * 1e3   # sums stored + reloaded
+                bounds = k_slab_schedule(S, k.k_slice_align, ms_step, max(ms_plain - ms_step, 1e-3), boundary_ms,
+                                         keep=(sms - free) / sms)
             ms_total, n_launch = time_bcast_steps(c, k, ins, out, bounds, free, args.steps, args.warmup)
             ms = ms_total / args.steps
+            if ms_plain is None:
+                ms_plain = ms
             res[name] = {"value": round(flops_total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
                          "ms_per_step": round(ms, 4), "k_slabs": bounds, "free_sms_while_slabs_arrive": free,
                          "gpu_launches": int(c.sum(n_launch)),

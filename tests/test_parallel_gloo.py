@@ -292,3 +292,20 @@ def test_b_broadcast_in_k_slabs(world):
     while not q.empty():
         out.append(q.get())
     assert out == [("ok", True)] * world, out
+
+
+def test_k_slab_schedule_follows_the_measured_times():
+    from bafe_b200.parallel import k_slab_schedule
+    K, align = 16384, 64
+    for t_gemm, t_bcast, bd in [(18.4, 1.6, 0.16), (9.2, 1.7, 0.08), (4.6, 1.8, 0.04), (4.6, 0.2, 0.04)]:
+        b = k_slab_schedule(K, align, t_gemm, t_bcast, bd, keep=132 / 148)
+        assert b[0] == 0 and b[-1] == K and len(b) >= 3
+        assert all(x % align == 0 for x in b[1:-1]) and all(b[i] < b[i + 1] for i in range(len(b) - 1))
+        sizes = [b[i + 1] - b[i] for i in range(len(b) - 1)]
+        assert sizes[0] <= K // 8                          # little of B waits for nothing to overlap it
+        assert all(sizes[i + 1] > sizes[i] for i in range(len(sizes) - 1))
+    # slower broadcast relative to the GEMM: more, more gradual slabs
+    assert len(k_slab_schedule(K, align, 4.6, 1.8, 0.04, keep=0.9)) > len(k_slab_schedule(K, align, 18.4, 1.6, 0.16, keep=0.9))
+    # a broadcast cheaper than a slice boundary is not worth slicing
+    assert k_slab_schedule(K, align, 18.4, 0.05, 0.16, keep=0.9) == [0, K]
+    assert k_slab_schedule(100, 64, 1.0, 1.0, 0.01) == [0, 100]
