@@ -746,9 +746,9 @@ def bench_transpose(c: Ctx) -> dict:
     (r1 - r0) panel; no collective."""
     import bafe_b200 as bafe
     torch, args = c.torch, c.args
-    from bafe_b200.parallel import row_panels
+    from bafe_b200.parallel import transpose_blocks
     S = args.transpose_size
-    r0, r1 = row_panels(S, c.world, align=32)[c.rank]
+    r0, r1 = transpose_blocks(S, c.world)[c.rank]
     cols = r1 - r0
     X = torch.rand(S, cols, device=c.dev, generator=c.gen)
     O = torch.empty(cols, S, device=c.dev)
