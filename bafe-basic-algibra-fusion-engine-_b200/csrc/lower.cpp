@@ -594,19 +594,26 @@ struct Lowerer {
                              a.dtype == BAFE_DTYPE_F32 && b.dtype == BAFE_DTYPE_F32;
         const bool bf16_ops = T == BAFE_DTYPE_F32 && a.dtype == BAFE_DTYPE_BF16 && b.dtype == BAFE_DTYPE_BF16;
         if ((f32_ops || bf16_ops) && tc_shape_ok(s, f32_ops ? 4 : 2) && prec != "exact") {
-            bool big = (double)M * (double)Nn * (double)K >= 16777216.0;   // 256^3
+            // auto: tensor cores from 256^3 multiply-adds on for bf16 (one
+            // product per k-step), above 256^3 for f32 (three): a 256^3 f32
+            // GEMM is one CTA-pair tile, latency-bound, and the bit-exact
+            // CUDA-core kernel is as fast there (measured on B200: 24.7 us,
+            // against 24.8 us for 3xTF32 with its pre-passes; 512^3: 47.2
+            // against 32.8 us)
+            const double macs = (double)M * (double)Nn * (double)K;
+            const bool big = bf16_ops ? macs >= 16777216.0 : macs > 16777216.0;   // 256^3
             if (prec == "tf32" || prec == "3xtf32" || big) {
                 s.kind = StepKind::GemmTc;
                 s.tc_variant = (bf16_ops || prec == "tf32") ? 1 : 3;
                 s.tc_elem = bf16_ops ? 1 : 0;
                 // 3xTF32 residuals: a pre-pass into plan scratch (default), or
-                // made in shared memory by the kernel (tc_convert: no scratch,
-                // half the operand traffic, more shared-memory traffic)
-                // auto: in the kernel below 2 x 256^3 multiply-adds, where the
-                // two pre-pass launches cost more than the conversion (measured
-                // on B200: 256^3 24.6 -> 20.5 us; even at 512^3, slower above)
-                const bool small = (double)M * (double)Nn * (double)K * (double)batch < 2.0 * 16777216.0;
-                s.tc_convert = s.tc_variant == 3 && (opt.tc_convert > 0 || (opt.tc_convert < 0 && small));
+                // made in shared memory by the kernel (tc_convert=1: no
+                // scratch, half the operand traffic, more shared-memory
+                // traffic).  With B split to nearest the in-kernel conversion
+                // costs more than the two pre-pass launches even at 256^3
+                // (32.9 against 24.8 us on B200; equal at 512^3, slower above),
+                // so auto keeps the pre-pass.
+                s.tc_convert = s.tc_variant == 3 && opt.tc_convert > 0;
                 s.tc_pair = opt.tc_pair;
             }
         }

@@ -290,18 +290,19 @@ int bafe_cuda_last_error(char *buf, size_t buf_size);
 void bafe_cuda_clear_error(void);
 
 /* Backend options (strings, process-wide):
- *   "gemm_precision": "auto" (default) | "3xtf32" | "tf32" | "exact"
- *                     (read when a plan is built)
+ *   "gemm_precision": "auto" (default) | "3xtf32" | "tf32" | "exact";
+ *                     auto: 3xTF32 tensor cores for f32 GEMMs above 256^3
+ *                     multiply-adds, bf16 tensor cores from 256^3, the
+ *                     bit-exact CUDA-core kernel otherwise (read when a
+ *                     plan is built)
  *   "tc_pair":        "1" (default): tensor-core GEMMs run on CTA pairs
  *                     (256x256 tiles over two SMs); "0": one CTA per tile
  *                     (read when a plan is built)
  *   "tc_convert":     "auto" (default) | "0" | "1": "0": 3xTF32 residuals
  *                     come from a pre-pass into plan scratch; "1": the GEMM
  *                     kernel makes them in shared memory (no scratch, half
- *                     the operand traffic, lower throughput on B200 at
- *                     large sizes); auto = "1" below 2 x 256^3
- *                     multiply-adds (one launch instead of three), else "0"
- *                     (read when a plan is built)
+ *                     the operand traffic, lower throughput on B200 at every
+ *                     size measured); auto = "0" (read when a plan is built)
  *   "host_panels":    "auto" (default) | "0" | n: host-pointer calls of a
  *                     row-separable plan copy, compute and copy back in n
  *                     row panels on three streams, overlapping the copies

@@ -154,15 +154,20 @@ def test_tc_convert_option_drops_the_residual_pre_pass():
     try:
         conv = bafe.compile_graph(g).describe().strip().splitlines()
         bafe.set_option("tc_convert", "auto")
-        g2 = GraphBuilder()                  # 256^3: auto makes the residuals in the kernel
+        g2 = GraphBuilder()                  # 256^3: auto keeps the pre-pass too
         a2 = g2.add_input("A", (256, 256), 0, 0)
         b2 = g2.add_input("B", (256, 256), 0, 0)
         g2.set_output(g2.add("matmul", [a2, b2]))
         small = bafe.compile_graph(g2).describe().strip().splitlines()
+        bafe.set_option("gemm_precision", "auto")
+        dflt = bafe.compile_graph(g2).describe().strip().splitlines()
     finally:
         bafe.set_option("tc_convert", "auto")
+        bafe.set_option("gemm_precision", "auto")
     assert len(conv) == 1 and conv[0].startswith("gemm.tc.3xtf32")
-    assert len(small) == 1 and small[0].startswith("gemm.tc.3xtf32")
+    assert len(small) == 3 and small[2].startswith("gemm.tc.3xtf32")
+    # default precision: an f32 GEMM of 256^3 multiply-adds runs the exact kernel
+    assert len(dflt) == 1 and dflt[0].startswith("gemm.exact"), dflt
 
 
 def _sum_chain(n, tree=False):
