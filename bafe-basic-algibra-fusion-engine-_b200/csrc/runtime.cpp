@@ -265,7 +265,10 @@ struct DeviceState {
     CUmodule module = nullptr;
     std::vector<CUfunction> fn, fn_vec;
     std::vector<void*> tmp;
-    std::vector<void*> in_stage;
+    std::vector<void*> in_stage;        // inputs' device copies: in_block + in_off[k]
+    void* in_block = nullptr;           // one allocation for all of them
+    std::vector<int64_t> in_off;        // 256-byte aligned offsets in in_block
+    int64_t in_block_bytes = 0;
     void* out_stage = nullptr;
     cudaStream_t stream = nullptr;      // host calls: kernels
     cudaStream_t h2d = nullptr;         // host calls: input copies (row streaming)
@@ -302,6 +305,9 @@ struct DeviceState {
 // with a fixed cost that dominates small calls; from pinned memory the
 // copies queue behind one another and run asynchronously.
 constexpr int64_t kPackedCallBytes = int64_t(1) << 20;
+// ... and move all their inputs in one copy, pinned ones included, up to
+// this many input bytes.
+constexpr int64_t kPackPinnedBytes = int64_t(128) << 10;
 
 // Timing events (pairs: before / after kernels) of a host call.
 static int ensure_timing_events(DeviceState* ds, size_t n) {
@@ -1088,61 +1094,106 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
         }
     }
     if (ds->in_stage.size() != (size_t)p.n_inputs) {
+        // one device block for the inputs, at the offsets a small call's
+        // packed host buffer uses too (one copy moves all of them)
+        ds->in_off.assign(p.n_inputs, 0);
+        int64_t total = 0;
+        for (int k = 0; k < p.n_inputs; ++k) {
+            ds->in_off[k] = total;
+            total += (p.in_bytes[k] + 255) / 256 * 256;
+        }
+        if (int rc = alloc(&ds->in_block, total)) return rc;
+        ds->in_block_bytes = total;
         ds->in_stage.assign(p.n_inputs, nullptr);
         for (int k = 0; k < p.n_inputs; ++k)
-            if (int rc = alloc(&ds->in_stage[k], p.in_bytes[k])) return rc;
+            ds->in_stage[k] = p.in_bytes[k] ? static_cast<char*>(ds->in_block) + ds->in_off[k] : nullptr;
         if (int rc = alloc(&ds->out_stage, p.out_bytes)) return rc;
     }
     if (int rc = ensure_tmps(p, ds)) return rc;
     const int panels = host_panel_count(p);
     if (panels > 1) return run_plan_host_streamed(p, ds, ptrs, panels, resident, ready);
     if (ready) cudaStreamWaitEvent(ds->stream, (cudaEvent_t)ready, 0);   // resident inputs filled
-    // Small calls: the operands in pageable host memory pass through the
-    // pinned buffer, each at a 256-byte offset (one CPU copy per operand);
-    // pinned host and device pointers are copied from directly, as before.
+    // Small calls (inputs and output within the pinned buffer, no resident
+    // input): every input is copied on the CPU into the pinned buffer at
+    // its offset in the device input block, and ONE host-to-device copy
+    // moves them all (each copy on the stream costs ~5 us on B200, more
+    // than the CPU copy of up to 1 MiB); the output comes back in one copy,
+    // through the buffer when the caller's is pageable.  Otherwise operands
+    // in pageable memory pass through the pinned buffer one copy each and
+    // pinned host or device pointers are copied from directly.
     std::vector<int64_t> stage_off(p.n_inputs + 1, -1);
+    bool any_resident = false;
+    for (int k = 0; k < p.n_inputs; ++k) any_resident = any_resident || (resident && resident[k]);
+    auto pageable = [](const void* q) {
+        cudaPointerAttributes a;
+        if (cudaPointerGetAttributes(&a, q) != cudaSuccess) { cudaGetLastError(); return false; }
+        return a.type == cudaMemoryTypeUnregistered;
+    };
+    const int64_t out_round = (p.out_bytes + 255) / 256 * 256;
+    bool pack_all = !any_resident && ds->in_block_bytes > 0 && ds->in_block_bytes + out_round <= kPackedCallBytes;
+    // pinned inputs are packed only while the extra CPU copy is cheap (a
+    // few microseconds); pageable ones go through the buffer anyway
+    if (pack_all && ds->in_block_bytes > kPackPinnedBytes)
+        for (int k = 0; k < p.n_inputs && pack_all; ++k)
+            if (p.in_bytes[k] && !pageable(ptrs[k])) pack_all = false;
     {
-        auto pageable = [](const void* q) {
-            cudaPointerAttributes a;
-            if (cudaPointerGetAttributes(&a, q) != cudaSuccess) { cudaGetLastError(); return false; }
-            return a.type == cudaMemoryTypeUnregistered;
-        };
         int64_t total = 0;
-        for (int k = 0; k <= p.n_inputs; ++k) {
-            const int64_t b = k < p.n_inputs ? ((resident && resident[k]) ? 0 : p.in_bytes[k]) : p.out_bytes;
-            if (b == 0 || !pageable(ptrs[k])) continue;
-            stage_off[k] = total;
-            total += (b + 255) / 256 * 256;
+        if (pack_all) {
+            // no pointer queries: every input is copied on the CPU, and the
+            // output comes back through the buffer too (one small CPU copy)
+            for (int k = 0; k < p.n_inputs; ++k) if (p.in_bytes[k]) stage_off[k] = ds->in_off[k];
+            total = ds->in_block_bytes;
+            if (p.out_bytes) stage_off[p.n_inputs] = total;
+            total += out_round;
+        } else {
+            for (int k = 0; k <= p.n_inputs; ++k) {
+                const int64_t b = k < p.n_inputs ? ((resident && resident[k]) ? 0 : p.in_bytes[k]) : p.out_bytes;
+                if (b == 0 || !pageable(ptrs[k])) continue;
+                stage_off[k] = total;
+                total += (b + 255) / 256 * 256;
+            }
         }
-        bool packed = total > 0 && total <= kPackedCallBytes;
-        if (packed && !ds->host_stage) {
+        bool staged = total > 0 && total <= kPackedCallBytes;
+        if (staged && !ds->host_stage) {
             if (cudaHostAlloc(&ds->host_stage, (size_t)kPackedCallBytes, cudaHostAllocDefault) == cudaSuccess) {
                 ds->host_stage_bytes = (size_t)kPackedCallBytes;
             } else {
                 cudaGetLastError();
                 ds->host_stage = nullptr;
-                packed = false;   // direct copies instead
+                staged = false;   // direct copies instead
             }
         }
-        if (!packed) stage_off.assign(p.n_inputs + 1, -1);
+        if (!staged) {
+            stage_off.assign(p.n_inputs + 1, -1);
+            pack_all = false;
+        }
     }
     char* const stage = (char*)ds->host_stage;
-    for (int k = 0; k < p.n_inputs; ++k) {
-        if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
-        const void* src = ptrs[k];
-        if (stage_off[k] >= 0) {
-            memcpy(stage + stage_off[k], ptrs[k], (size_t)p.in_bytes[k]);
-            src = stage + stage_off[k];
-        }
-        cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], src, (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            // copies already queued may still read the pinned staging buffer:
-            // let them finish before the next call can overwrite it
-            cudaStreamSynchronize(ds->stream);
-            cudaGetLastError();
-            set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
-            return 7;
+    auto h2d_failed = [&](cudaError_t e) {
+        cudaGetLastError();
+        // copies already queued may still read the pinned staging buffer:
+        // let them finish before the next call can overwrite it
+        cudaStreamSynchronize(ds->stream);
+        cudaGetLastError();
+        set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
+        return 7;
+    };
+    if (pack_all) {
+        for (int k = 0; k < p.n_inputs; ++k)
+            if (p.in_bytes[k]) memcpy(stage + stage_off[k], ptrs[k], (size_t)p.in_bytes[k]);
+        cudaError_t e = cudaMemcpyAsync(ds->in_block, stage, (size_t)ds->in_block_bytes, cudaMemcpyHostToDevice,
+                                        ds->stream);
+        if (e != cudaSuccess) return h2d_failed(e);
+    } else {
+        for (int k = 0; k < p.n_inputs; ++k) {
+            if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
+            const void* src = ptrs[k];
+            if (stage_off[k] >= 0) {
+                memcpy(stage + stage_off[k], ptrs[k], (size_t)p.in_bytes[k]);
+                src = stage + stage_off[k];
+            }
+            cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], src, (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
+            if (e != cudaSuccess) return h2d_failed(e);
         }
     }
     std::vector<void*> dptrs(ds->in_stage);
@@ -1168,10 +1219,15 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
             return 7;
         }
     }
-    // The device error word rides on the same stream into a pinned word.
+    // The device error word rides on the same stream into a pinned word --
+    // for plans with a tensor-core step, the only kernels whose bounded
+    // waits can set it (a word left by an earlier device-resident run is
+    // reported by bafe_cuda_synchronize or the next such call).
     const int edev = ds->device;
+    bool has_tc = false;
+    for (const Step& st : p.steps) has_tc = has_tc || st.kind == StepKind::GemmTc;
     bool err_async = false;
-    if (edev >= 0 && edev < 64 && g_err_word[edev]) {
+    if (has_tc && edev >= 0 && edev < 64 && g_err_word[edev]) {
         if (!ds->err_host && cudaHostAlloc((void**)&ds->err_host, 4, cudaHostAllocDefault) != cudaSuccess) {
             cudaGetLastError();
             ds->err_host = nullptr;
@@ -1190,6 +1246,7 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
     }
     if (p.out_bytes && out_off >= 0) memcpy(ptrs[p.n_inputs], stage + out_off, (size_t)p.out_bytes);
     p.last_device_ms = timed_ms(ds, 1);
+    if (!has_tc) return 0;
     return err_async ? report_error_word(edev, *ds->err_host) : check_device_error_word(edev);
 }
 
@@ -1240,7 +1297,7 @@ void release_plan_device_state(Plan& p) {
         cudaSetDevice(s->device);
         if (s->stream) cudaStreamSynchronize(s->stream);
         for (void* t : s->tmp) if (t) cudaFree(t);
-        for (void* t : s->in_stage) if (t) cudaFree(t);
+        if (s->in_block) cudaFree(s->in_block);
         if (s->out_stage) cudaFree(s->out_stage);
         if (s->tc_ws) cudaFree(s->tc_ws);
         if (s->tc_ctr) cudaFree(s->tc_ctr);
