@@ -42,17 +42,22 @@ def _planned(torch, A, B, a_col, b_col):
 
 
 def _static(torch, A, B, a_col, b_col):
+    """One call; returns (output, device bytes free before the call minus
+    after it), the operands and the output allocated before measuring."""
     M, K = A.shape
     N = B.shape[1]
     a_store = A.t().contiguous() if a_col else A
     b_store = B.t().contiguous() if b_col else B
     out = torch.full((M, N), float("nan"), device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
     rc = _binding.lib.bafe_cuda_gemm_3xtf32_static_scratch(
         ctypes.c_void_p(a_store.data_ptr()), ctypes.c_void_p(b_store.data_ptr()), ctypes.c_void_p(out.data_ptr()),
         M, N, K, a_col, b_col, ctypes.c_void_p(stream))
     assert rc == 0, _binding.last_error()
-    return out
+    torch.cuda.synchronize()
+    return out, free0 - torch.cuda.mem_get_info()[0]
 
 
 @pytest.mark.parametrize("shape,a_col,b_col", [((1024, 768, 512), 0, 0), ((640, 520, 1000), 1, 1)])
@@ -65,7 +70,12 @@ def test_static_scratch_matches_planned_entry_two_calls(cuda, shape, a_col, b_co
         A = torch.randn(M, K, device="cuda", generator=gen)
         B = torch.randn(K, N, device="cuda", generator=gen)
         want = _planned(torch, A, B, a_col, b_col)
-        got = _static(torch, A, B, a_col, b_col)
+        got, taken = _static(torch, A, B, a_col, b_col)
+        if call > 0:
+            # the device's free memory is the same after the call as before
+            # it: no allocation on the caller's behalf (the first call of the
+            # process may load the library's kernels)
+            assert taken == 0, f"call {call}: {taken} bytes of device memory taken"
         err = float((got - want).abs().max())
         assert err <= bound, f"call {call}: max |static - planned| = {err}"
         ref = A.double() @ B.double()
