@@ -101,6 +101,12 @@ __device__ __forceinline__ u16 f32_to_bf16(float f) {
     return (u16)(bits >> 16);
 }
 
+// An L2 prefetch hint of the 128-byte line holding p (no register result,
+// nothing to wait for).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
 // ---------------------------------------------------------------------------
 // Streaming loads / stores.  Generated elementwise kernels move every
 // operand once, so loads bypass L1 allocation and stores are marked

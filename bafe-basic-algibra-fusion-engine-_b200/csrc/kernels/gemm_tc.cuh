@@ -1309,6 +1309,14 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                 const u32 use = (chunk >> 1) & 1u;
                 const int c_end = (c + 1) * KB_PER_CHUNK < kb_hi ? (c + 1) * KB_PER_CHUNK : kb_hi;
                 const bool conv_ok = convert_until(c_end + KB_PER_CHUNK < limit ? c_end + KB_PER_CHUNK : limit);
+                // two chunks before a whole tile's epilogue: its operand rows
+                // into L2 (the epilogue's loads would otherwise stall these
+                // threads, which also drain TMEM for the MMA issuer)
+                if (part < 0 && !g.acc_raw && c == (c1 - 2 > c0 ? c1 - 2 : c0)) {
+                    int mb, nb, bi;
+                    tile_coords(g, t, mb, nb, bi);
+                    Spec::prefetch(g, bi, (i64)mb * 2 * BM + (i64)cta * BM + q * 32 + lane, (i64)nb * BN + half * 128);
+                }
                 const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
                 if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
                 tc_fence_after();

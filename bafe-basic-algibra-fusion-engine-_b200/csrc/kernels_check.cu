@@ -24,6 +24,13 @@ struct CheckSpec {
 #pragma unroll
         for (int e = 0; e < 4; ++e) o4.v[e] = bafe::relu(bafe::add(acc4[e], v0.v[e]));
     }
+    template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0) {
+        if (i >= g.M) return;
+        for (int l = 0; l < 4; ++l) {
+            const i64 j = j0 + l * 32;
+            if (j < g.N) bafe::prefetch_l2(reinterpret_cast<const char*>(g.ep[0]) + (b * g.o_bstride + i * g.N + j) * 4);
+        }
+    }
 };
 
 extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
@@ -61,6 +68,7 @@ struct CheckSpecBf16 {
 #pragma unroll
         for (int e = 0; e < 4; ++e) o4.v[e] = bafe::f32_to_bf16(bafe::relu(acc4[e]));
     }
+    template <class G> static __device__ __forceinline__ void prefetch(const G&, i64, i64, i64) {}
 };
 extern "C" __global__ void __launch_bounds__(bafe::TcPairCfg<1>::THREADS, 1) check_gemm_bf16_pair(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc_pair<CheckSpecBf16, 1, bafe::ElemBf16>(g);

@@ -693,6 +693,25 @@ struct Lowerer {
         };
         emit_apply(false);
         emit_apply(true);
+        // prefetch(g, b, i, j0): row i, columns j0 .. j0+127 of every
+        // full-size epilogue operand into L2 (bounds-checked, a hint), so
+        // the epilogue's loads after the tile's last chunk find them there
+        // (row-vector operands are small and stay cached anyway).
+        src << "  template <class G> static __device__ __forceinline__ void prefetch(const G& g, i64 b, i64 i, i64 j0) {\n"
+            << "    if (i >= g.M) return;\n    (void)b; (void)j0;\n";
+        if (R) {
+            const int leaf_base = (g.op == Op::FusedMatmulBias || g.op == Op::FusedMatmulBiasRelu) ? 1 : 0;
+            for (size_t k = 0; k < R->leaves.size(); ++k) {
+                if (R->leaves[k].access == ROW) continue;
+                const int es = dtype_size(buf_dtype[R->leaves[k].node]);
+                const int per_line = 128 / es;
+                src << "    for (int l = 0; l < " << (128 + per_line - 1) / per_line << "; ++l) {\n"
+                    << "      const i64 j = j0 + l * " << per_line << ";\n"
+                    << "      if (j < g.N) bafe::prefetch_l2(reinterpret_cast<const char*>(g.ep[" << leaf_base + (int)k
+                    << "]) + (b * g.o_bstride + i * g.N + j) * " << es << ");\n    }\n";
+            }
+        }
+        src << "  }\n";
         src << "};\n";
         for (auto& l : leaves) s.srcs.push_back(buf[l.node]);
         s.n_epi = (int)leaves.size();
