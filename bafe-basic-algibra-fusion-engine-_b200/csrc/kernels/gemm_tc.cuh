@@ -136,13 +136,17 @@ template <int VARIANT> struct TcPairCfg;
 template <> struct TcPairCfg<1> {
     static constexpr int STAGES = 6, THREADS = 320, KB_PER_CHUNK = 32;
 };
-// 3xTF32 pair: 64-deep chunks.  The MMA issuer then waits on a TMEM
-// buffer still being drained ~27 % of its time, and 96-deep chunks remove
-// most of that (+11.7 % per clock, within the error bound) -- but under the
-// 1 kW power cap the denser MMA stream drew the clock from 1.49 to 1.19 GHz
-// on real data (same box, A/B): -11 % net, so the 64-deep form stays.
+// 3xTF32 pair: 96-deep chunks.  With 64-deep ones the MMA issuer waited
+// on a TMEM buffer still being drained for part of its time; 96-deep
+// chunks run 4.4-4.6 % faster on two B200s under the power cap (A/B on the
+// same box, the SM clock no lower), 128-deep ones 5.3 %, for an error that
+// grows with the chunk: max |err| at 4096^3 1.87e-4 (64), 2.63e-4 (96),
+// 3.40e-4 (128) against the bound 8e-4.  96 keeps most of the gain and
+// fits the converting form's look-ahead (KB_PER_CHUNK <= STAGES).  (An
+// older form of this kernel lost 11 % net with 96-deep chunks on a box
+// whose power cap then pulled the clock from 1.49 to 1.19 GHz.)
 template <> struct TcPairCfg<3> {
-    static constexpr int STAGES = 3, THREADS = 320, KB_PER_CHUNK = 2;
+    static constexpr int STAGES = 3, THREADS = 320, KB_PER_CHUNK = 3;
 };
 
 // Two IEEE round-to-nearest fp32 additions in one instruction (Blackwell

@@ -47,10 +47,10 @@ static_assert(sizeof(TcArgsHost) <= sizeof(TcLaunch::args), "TcArgs fits the lau
 
 int threads_of(int) { return 320; }
 // k-blocks (one 128-byte row of K) per TMEM promotion chunk, as the kernels
-// have it: bf16 32; tf32 pair 32 (1x) / 2 (3x), single 4 / 2
+// have it: bf16 32; tf32 pair 32 (1x) / 3 (3x), single 4 / 2
 int chunk_kblocks(const Step& s) {
     if (s.tc_elem == 1) return 32;
-    if (s.tc_variant == 3) return 2;
+    if (s.tc_variant == 3) return s.tc_pair ? 3 : 2;
     return s.tc_pair ? 32 : 4;
 }
 int stages_of(int variant, bool pair) { return pair ? (variant == 3 ? 3 : 6) : (variant == 3 ? 2 : 4); }

@@ -57,12 +57,12 @@ def _whole(torch, k, ins, M, N, split):
     return out
 
 
-@pytest.mark.parametrize("precision,shape,bounds", [
-    ("3xtf32", (512, 1024, 4096), [0, 320, 1024, 2112, 4096]),
-    ("3xtf32", (768, 512, 2048), [0, 64, 2048]),
-    ("tf32", (512, 1024, 4096), [0, 1024, 3072, 4096]),
+@pytest.mark.parametrize("precision,shape,chunks", [
+    ("3xtf32", (512, 1024, 4096), [3, 11, 22]),       # interior bounds, in promotion chunks
+    ("3xtf32", (768, 512, 2048), [1]),
+    ("tf32", (512, 1024, 4096), [1, 3]),
 ])
-def test_k_slices_equal_one_launch(cuda, precision, shape, bounds):
+def test_k_slices_equal_one_launch(cuda, precision, shape, chunks):
     torch = cuda
     M, N, K = shape
     bafe.set_option("gemm_precision", precision)
@@ -72,7 +72,8 @@ def test_k_slices_equal_one_launch(cuda, precision, shape, bounds):
         bafe.set_option("gemm_precision", "auto")
     assert "gemm.tc" in k.describe() and ".pair" in k.describe(), k.describe()
     align = k.k_slice_align
-    assert align == (64 if precision == "3xtf32" else 1024)
+    assert align == (96 if precision == "3xtf32" else 1024)   # one promotion chunk
+    bounds = [0] + [c * align for c in chunks] + [K]
     ins = _operands(torch, M, N, K, M + K)
     want = _whole(torch, k, ins, M, N, split=False)
     # slabs "arrive" on a side stream: each slice waits for its event
@@ -132,7 +133,8 @@ def test_k_slices_without_epilogue(cuda):
     ins = _operands(torch, M, N, K, 5, epi=False)
     want = _whole(torch, k, ins, M, N, split=False)
     out = torch.empty(M, N, device="cuda")
-    k.run_torch_ksliced(ins, out, [0, 128, 512, 1024])
+    a = k.k_slice_align
+    k.run_torch_ksliced(ins, out, [0, 2 * a, 6 * a, 1024])
     torch.cuda.synchronize()
     bafe.synchronize()
     assert torch.equal(out, want)
@@ -152,11 +154,12 @@ def test_k_slices_refused_where_they_do_not_apply(cuda):
     with pytest.raises(RuntimeError):
         kx.run_torch_ksliced(ins, out, [0, 512, 1024])
     k = bafe.compile_graph(_graph(M, N, K))
-    for bad in ([0, 100, 1024], [0, 512, 512, 1024], [64, 1024], [0, 512]):
+    a = k.k_slice_align
+    for bad in ([0, a + 4, 1024], [0, 5 * a, 5 * a, 1024], [a, 1024], [0, 5 * a]):
         with pytest.raises(RuntimeError):
             k.run_torch_ksliced(ins, out, bad)
     # the context stays usable
-    k.run_torch_ksliced(ins, out, [0, 512, 1024])
+    k.run_torch_ksliced(ins, out, [0, 5 * a, 1024])
     torch.cuda.synchronize()
     bafe.synchronize()
     assert torch.equal(out, _whole(torch, k, ins, M, N, split=False))
