@@ -27,6 +27,7 @@ Options& options() {
         if (const char* h = getenv("BAFE_HOST_PANELS")) o.host_panels = strcmp(h, "auto") == 0 ? -1 : atoi(h);
         if (const char* c = getenv("BAFE_TC_CONVERT")) o.tc_convert = strcmp(c, "auto") == 0 ? -1 : (atoi(c) != 0);
         if (const char* f = getenv("BAFE_KSLICE_FREE_SMS")) o.kslice_free_sms = atoi(f) > 0 ? atoi(f) : 0;
+        if (const char* hg = getenv("BAFE_HOST_GRAPHS")) o.host_graphs = atoi(hg) != 0;
     }
     return o;
 }
@@ -392,6 +393,11 @@ BAFE_API int bafe_cuda_set_option(const char* key, const char* value) {
         o.tc_convert = v == "auto" ? -1 : (v == "1");
         return 0;
     }
+    if (k == "host_graphs") {
+        if (v != "0" && v != "1") return -1;
+        o.host_graphs = v == "1";
+        return 0;
+    }
     if (k == "kslice_free_sms") {
         char* end = nullptr;
         long n = strtol(value, &end, 10);
@@ -428,6 +434,7 @@ BAFE_API int bafe_cuda_get_option(const char* key, char* buf, size_t buf_size) {
     else if (k == "tc_convert") v = o.tc_convert < 0 ? "auto" : (o.tc_convert ? "1" : "0");
     else if (k == "host_panels") v = o.host_panels < 0 ? "auto" : std::to_string(o.host_panels);
     else if (k == "kslice_free_sms") v = std::to_string(o.kslice_free_sms);
+    else if (k == "host_graphs") v = o.host_graphs ? "1" : "0";
     else return -1;
     if (buf && buf_size) snprintf(buf, buf_size, "%s", v.c_str());
     return 0;

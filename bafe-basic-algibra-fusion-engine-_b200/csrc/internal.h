@@ -80,6 +80,7 @@ struct Options {
     int host_panels = -1;                   // host calls: -1 auto, 0/1 off, n: n row panels
     int tc_convert = -1;                    // 3xTF32 residuals inside the kernel: 1 yes, 0 no, -1 auto (small GEMMs)
     int kslice_free_sms = 0;                // K-sliced runs: SMs every slice but the last leaves to other streams
+    bool host_graphs = true;                // small host calls replay as one CUDA graph
 };
 Options& options();
 

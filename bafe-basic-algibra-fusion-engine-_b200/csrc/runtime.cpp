@@ -298,6 +298,14 @@ struct DeviceState {
     // Pinned copy of the device error word, read on `stream` at the end of
     // a host call (a synchronous read would add a blocking copy per call).
     unsigned* err_host = nullptr;
+    // Packed small host calls replayed as one CUDA graph (the copy in, the
+    // plan's launches, the copies out, the timing events): every pointer in
+    // them is this state's own, so the second such call captures them and
+    // later calls launch the graph.
+    cudaGraphExec_t graph_exec = nullptr;
+    int64_t graph_kernels = 0;          // kernels per replay (the launch counter)
+    int packed_calls = 0;
+    bool graph_failed = false;          // capture failed once: stay eager
 };
 
 // Host calls moving at most this many bytes in total copy through one
@@ -1178,12 +1186,109 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
         set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
         return 7;
     };
+    // The device error word rides on the same stream into a pinned word --
+    // for plans with a tensor-core step, the only kernels whose bounded
+    // waits can set it (a word left by an earlier device-resident run is
+    // reported by bafe_cuda_synchronize or the next such call).
+    const int edev = ds->device;
+    bool has_tc = false;
+    for (const Step& st : p.steps) has_tc = has_tc || st.kind == StepKind::GemmTc;
+    if (has_tc && edev >= 0 && edev < 64 && g_err_word[edev] && !ds->err_host &&
+        cudaHostAlloc((void**)&ds->err_host, 4, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        ds->err_host = nullptr;
+    }
+    const bool err_copy = has_tc && ds->err_host && edev >= 0 && edev < 64 && g_err_word[edev];
+    if (int rc = ensure_timing_events(ds, 2)) return rc;
+    std::vector<void*> dptrs(ds->in_stage);
+    for (int k = 0; k < p.n_inputs; ++k)
+        if (resident && resident[k]) dptrs[k] = ptrs[k];
+    dptrs.push_back(ds->out_stage);
+    const int64_t out_off = stage_off[p.n_inputs];
+    // everything after the inputs are in place: the plan, the copy out, the
+    // error word (err_async: its copy is queued)
+    bool err_async = false;
+    bool capturing = false;
+    // inside a capture a plain record only marks a dependency; an external
+    // record node records the timing event on every replay
+    auto record = [&](cudaEvent_t ev) {
+        if (capturing) cudaEventRecordWithFlags(ev, ds->stream, cudaEventRecordExternal);
+        else cudaEventRecord(ev, ds->stream);
+    };
+    auto enqueue_rest = [&]() -> int {
+        record(ds->tev[0]);
+        if (int rc = run_plan_device(p, dptrs.data(), (int)dptrs.size(), ds->stream)) return rc;
+        record(ds->tev[1]);
+        if (p.out_bytes) {
+            void* to = out_off >= 0 ? (void*)(stage + out_off) : ptrs[p.n_inputs];
+            cudaError_t e = cudaMemcpyAsync(to, ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e));
+                return 7;
+            }
+        }
+        if (err_copy) {
+            err_async = cudaMemcpyAsync(ds->err_host, g_err_word[edev], 4, cudaMemcpyDeviceToHost, ds->stream) == cudaSuccess;
+            if (!err_async) cudaGetLastError();
+        }
+        return 0;
+    };
+    auto enqueue_failed = [&](int rc) {
+        // queued copies may still use the pinned buffer: let them finish
+        cudaStreamSynchronize(ds->stream);
+        cudaGetLastError();
+        return rc;
+    };
     if (pack_all) {
         for (int k = 0; k < p.n_inputs; ++k)
             if (p.in_bytes[k]) memcpy(stage + stage_off[k], ptrs[k], (size_t)p.in_bytes[k]);
-        cudaError_t e = cudaMemcpyAsync(ds->in_block, stage, (size_t)ds->in_block_bytes, cudaMemcpyHostToDevice,
-                                        ds->stream);
-        if (e != cudaSuccess) return h2d_failed(e);
+        if (err_copy) *ds->err_host = 0;
+        auto enqueue_all = [&]() -> int {
+            cudaError_t e = cudaMemcpyAsync(ds->in_block, stage, (size_t)ds->in_block_bytes, cudaMemcpyHostToDevice,
+                                            ds->stream);
+            if (e != cudaSuccess) {
+                cudaGetLastError();
+                set_error(7, std::string("host-to-device copy: ") + cudaGetErrorString(e));
+                return 7;
+            }
+            return enqueue_rest();
+        };
+        // the second packed call of this state captures the sequence as a
+        // graph (the first has made every allocation and load); later ones
+        // replay it.  A capture that fails leaves the state eager.
+        if (!ds->graph_exec && !ds->graph_failed && ds->packed_calls >= 1 && options().host_graphs) {
+            const int64_t lc0 = g_launch_count;
+            cudaGraph_t graph = nullptr;
+            bool ok = cudaStreamBeginCapture(ds->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+            capturing = ok;
+            const int rc = ok ? enqueue_all() : 0;
+            capturing = false;
+            if (ok) ok = cudaStreamEndCapture(ds->stream, &graph) == cudaSuccess && graph && rc == 0;
+            if (ok) ok = cudaGraphInstantiate(&ds->graph_exec, graph, 0) == cudaSuccess;
+            if (graph) cudaGraphDestroy(graph);
+            ds->graph_kernels = g_launch_count - lc0;
+            g_launch_count = lc0;
+            if (!ok) {
+                cudaGetLastError();
+                if (ds->graph_exec) cudaGraphExecDestroy(ds->graph_exec);
+                ds->graph_exec = nullptr;
+                ds->graph_failed = true;
+                clear_error();                           // the call runs eagerly below
+            }
+        }
+        if (ds->graph_exec) {
+            if (cudaGraphLaunch(ds->graph_exec, ds->stream) != cudaSuccess) {
+                cudaGetLastError();
+                set_error(7, "cudaGraphLaunch of the host call failed");
+                return enqueue_failed(7);
+            }
+            g_launch_count += ds->graph_kernels;
+            err_async = err_copy;
+        } else {
+            if (int rc = enqueue_all()) return enqueue_failed(rc);
+            ++ds->packed_calls;
+        }
     } else {
         for (int k = 0; k < p.n_inputs; ++k) {
             if (p.in_bytes[k] == 0 || (resident && resident[k])) continue;
@@ -1195,48 +1300,8 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
             cudaError_t e = cudaMemcpyAsync(ds->in_stage[k], src, (size_t)p.in_bytes[k], cudaMemcpyDefault, ds->stream);
             if (e != cudaSuccess) return h2d_failed(e);
         }
-    }
-    std::vector<void*> dptrs(ds->in_stage);
-    for (int k = 0; k < p.n_inputs; ++k)
-        if (resident && resident[k]) dptrs[k] = ptrs[k];
-    dptrs.push_back(ds->out_stage);
-    if (int rc = ensure_timing_events(ds, 2)) return rc;
-    cudaEventRecord(ds->tev[0], ds->stream);
-    if (int rc = run_plan_device(p, dptrs.data(), (int)dptrs.size(), ds->stream)) {
-        cudaStreamSynchronize(ds->stream);
-        return rc;
-    }
-    cudaEventRecord(ds->tev[1], ds->stream);
-    const int64_t out_off = stage_off[p.n_inputs];
-    if (p.out_bytes) {
-        void* to = out_off >= 0 ? (void*)(stage + out_off) : ptrs[p.n_inputs];
-        cudaError_t e = cudaMemcpyAsync(to, ds->out_stage, (size_t)p.out_bytes, cudaMemcpyDefault, ds->stream);
-        if (e != cudaSuccess) {
-            cudaGetLastError();
-            cudaStreamSynchronize(ds->stream);
-            cudaGetLastError();
-            set_error(7, std::string("device-to-host copy: ") + cudaGetErrorString(e));
-            return 7;
-        }
-    }
-    // The device error word rides on the same stream into a pinned word --
-    // for plans with a tensor-core step, the only kernels whose bounded
-    // waits can set it (a word left by an earlier device-resident run is
-    // reported by bafe_cuda_synchronize or the next such call).
-    const int edev = ds->device;
-    bool has_tc = false;
-    for (const Step& st : p.steps) has_tc = has_tc || st.kind == StepKind::GemmTc;
-    bool err_async = false;
-    if (has_tc && edev >= 0 && edev < 64 && g_err_word[edev]) {
-        if (!ds->err_host && cudaHostAlloc((void**)&ds->err_host, 4, cudaHostAllocDefault) != cudaSuccess) {
-            cudaGetLastError();
-            ds->err_host = nullptr;
-        }
-        if (ds->err_host) {
-            *ds->err_host = 0;
-            err_async = cudaMemcpyAsync(ds->err_host, g_err_word[edev], 4, cudaMemcpyDeviceToHost, ds->stream) == cudaSuccess;
-            if (!err_async) cudaGetLastError();
-        }
+        if (err_copy) *ds->err_host = 0;
+        if (int rc = enqueue_rest()) return enqueue_failed(rc);
     }
     cudaError_t e = cudaStreamSynchronize(ds->stream);
     if (e != cudaSuccess) {
@@ -1301,6 +1366,7 @@ void release_plan_device_state(Plan& p) {
         if (s->out_stage) cudaFree(s->out_stage);
         if (s->tc_ws) cudaFree(s->tc_ws);
         if (s->tc_ctr) cudaFree(s->tc_ctr);
+        if (s->graph_exec) cudaGraphExecDestroy(s->graph_exec);
         if (s->host_stage) cudaFreeHost(s->host_stage);
         if (s->err_host) cudaFreeHost(s->err_host);
         for (cudaStream_t st : {s->h2d, s->d2h}) if (st) { cudaStreamSynchronize(st); cudaStreamDestroy(st); }

@@ -309,6 +309,12 @@ void bafe_cuda_clear_error(void);
  *                     with the kernels; auto = one panel per 96 MiB of
  *                     row-split bytes, 8 to 32, once they exceed 64 MiB;
  *                     0 or 1 = one piece (read at each call)
+ *   "host_graphs":    "1" (default) | "0": a host-pointer call small
+ *                     enough to move its inputs in one copy through the
+ *                     plan's pinned buffer is captured, from its second
+ *                     call on, as one CUDA graph (copy in, kernels, copies
+ *                     out) and replayed; "0" issues them one by one (read at
+ *                     each call)
  *   "kslice_free_sms": "0" (default) | n: bafe_cuda_run_device_ksliced
  *                     launches every slice but the last on all SMs but n
  *                     (rounded up to CTA pairs), so that kernels queued on

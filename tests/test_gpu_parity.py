@@ -360,3 +360,57 @@ def test_small_host_calls_repeat_with_fresh_inputs(cuda):
         else:
             out = k(a, b, c)
         assert out.reshape(-1).tobytes() == want.tobytes(), it
+
+
+@pytest.mark.parametrize("precision,n", [("exact", 64), ("3xtf32", 256)])
+def test_small_host_calls_replayed_as_a_graph(cuda, precision, n):
+    """From the second small host call on, the copy in, the plan's kernels
+    and the copies out replay as one CUDA graph: each call still returns its
+    own inputs' result (fresh numpy arrays every call), launches the plan's
+    kernels once, and matches the eagerly issued call bit for bit."""
+    from bafe_b200.graph import GraphBuilder
+    from oracle import oracle
+    bafe.set_option("gemm_precision", precision)
+    try:
+        g = GraphBuilder()
+        ai, bi, ci = (g.add_input(nm, (n, n), 0, 0) for nm in "ABC")
+        g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [ai, bi]), ci])]))
+        k = bafe.compile_graph(g)
+    finally:
+        bafe.set_option("gemm_precision", "auto")
+    rng = np.random.default_rng(n)
+    per_call = []
+    for it in range(5):
+        a, b, c = (rng.standard_normal((n, n)).astype(np.float32) for _ in range(3))
+        before = bafe.launch_count()
+        out = k(a, b, c)
+        per_call.append(bafe.launch_count() - before)
+        bafe.set_option("host_graphs", "0")
+        try:
+            eager = k(a, b, c)
+        finally:
+            bafe.set_option("host_graphs", "1")
+        assert out.tobytes() == eager.tobytes(), it
+        if precision == "exact":
+            want = oracle.evaluate(g.to_list(), {ai: a, bi: b, ci: c}, g.output).reshape(n, n)
+            assert out.tobytes() == want.tobytes(), it
+        else:
+            ref = np.maximum(a.astype(np.float64) @ b.astype(np.float64) + c, 0)
+            assert np.abs(out - ref).max() <= 1e-4 * (n / 64) ** 0.5, it
+    assert len(set(per_call)) == 1 and per_call[0] >= 1, per_call
+
+
+def test_replayed_host_calls_still_time_the_device(cuda):
+    """The plan's device time (bafe_cuda_plan_last_device_ms, the autotune
+    loop's measurement) is recorded by the replayed graph too."""
+    from bafe_b200._binding import lib
+    from bafe_b200.graph import GraphBuilder
+    g = GraphBuilder()
+    ai, bi = (g.add_input(nm, (48, 48), 0, 0) for nm in "AB")
+    g.set_output(g.add("relu", [g.add("matmul", [ai, bi])]))
+    k = bafe.compile_graph(g)
+    a = np.ones((48, 48), np.float32)
+    for _ in range(4):
+        k(a, a)
+        ms = lib.bafe_cuda_plan_last_device_ms(k.plan)
+        assert 0.0 < ms < 100.0, ms
