@@ -113,6 +113,7 @@ struct Step {
     int a_col = 0, b_col = 0;
     int n_epi = 0;                 // epilogue operands are srcs[2..2+n_epi)
     bool direct = false;           // fused-form summation order (one chunk)
+    int exact_tm = 4;              // GemmExact: outputs per thread and axis (tile 16 * exact_tm)
     int tc_variant = 0;            // GemmTc: 1 = tf32, 3 = 3xtf32
     bool tc_pair = false;          // GemmTc: CTA-pair kernel (256x256 tiles)
     int tc_elem = 0;               // GemmTc operands: 0 = f32 (tf32 MMAs), 1 = bf16 (kind::f16)

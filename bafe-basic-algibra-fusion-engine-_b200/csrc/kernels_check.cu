@@ -36,6 +36,12 @@ struct CheckSpec {
 extern "C" __global__ void __launch_bounds__(256) check_gemm_exact(const bafe::GemmArgs g) {
     bafe::gemm_exact<CheckSpec, false>(g);
 }
+extern "C" __global__ void __launch_bounds__(256) check_gemm_exact_tile32(const bafe::GemmArgs g) {
+    bafe::gemm_exact<CheckSpec, false, 2>(g);
+}
+extern "C" __global__ void __launch_bounds__(256) check_gemm_exact_tile16(const bafe::GemmArgs g) {
+    bafe::gemm_exact<CheckSpec, false, 1>(g);
+}
 extern "C" __global__ void __launch_bounds__(bafe::TcCfg<3>::THREADS, 1) check_gemm_tc3(const __grid_constant__ bafe::TcArgs g) {
     bafe::gemm_tc<CheckSpec, 3>(g);
 }

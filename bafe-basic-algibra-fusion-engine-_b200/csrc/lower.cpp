@@ -732,9 +732,14 @@ struct Lowerer {
             s.aux.push_back(b_hi);
         }
         if (s.kind == StepKind::GemmExact) {
+            // the widest micro-tile that still gives >= 128 blocks (a
+            // 64x64 tile per block leaves most SMs idle on small problems)
+            s.exact_tm = 4;
+            auto blocks = [&](int64_t t) { return ((M + t - 1) / t) * ((Nn + t - 1) / t) * std::max<int64_t>(batch, 1); };
+            while (s.exact_tm > 1 && blocks(16 * s.exact_tm) < 128) s.exact_tm /= 2;
             src << "extern \"C\" __global__ void __launch_bounds__(256) " << s.kernel
                 << "(const bafe::GemmArgs g) { bafe::gemm_exact<" << S_ << ", " << (s.direct ? "true" : "false")
-                << ">(g); }\n";
+                << ", " << s.exact_tm << ">(g); }\n";
         } else {
             const char* cfg = s.tc_pair ? "TcPairCfg" : "TcCfg";
             const char* fn = s.tc_pair ? "gemm_tc_pair" : "gemm_tc";
@@ -756,6 +761,7 @@ struct Lowerer {
                                                                         : s.tc_variant == 1 ? "gemm.tc.tf32" : "gemm.tc.3xtf32") +
                                                                 (s.tc_pair ? ".pair" : "")
                                                           : (s.direct ? "gemm.exact.direct" : "gemm.exact.chunk32");
+        if (s.kind == StepKind::GemmExact) kindname += " tile=" + std::to_string(16 * s.exact_tm);
         s.describe = kindname + geo + " epi=" + epi_desc + " -> " + bufname(s.dst);
         P.steps.push_back(s);
         return 0;

@@ -592,9 +592,11 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 for (int k = 0; k < s.n_epi; ++k)
                     g.ep[k] = at_row(ptr_of(s.srcs[2 + k]), s.src_rb.empty() ? 0 : s.src_rb[2 + k]);
                 void* params[] = {&g};
-                // grid (N tiles, M tiles, batch); y and z stop at 65535, so
-                // larger problems launch in blocks of 65535 (z0 / y0 offsets)
-                const int64_t kMaxYZ = 65535, m_tiles = (m_run + 63) / 64, nx = (s.N + 63) / 64;
+                // grid (N tiles, M tiles, batch) of 16 * exact_tm wide tiles;
+                // y and z stop at 65535, so larger problems launch in blocks
+                // of 65535 (z0 / y0 offsets)
+                const int64_t tile = 16 * s.exact_tm;
+                const int64_t kMaxYZ = 65535, m_tiles = (m_run + tile - 1) / tile, nx = (s.N + tile - 1) / tile;
                 if (nx > 0x7fffffff) { set_error(8, "GEMM grid too large"); return 8; }
                 for (int64_t z0 = 0; z0 < s.batch; z0 += kMaxYZ)
                     for (int64_t y0 = 0; y0 < m_tiles; y0 += kMaxYZ) {
