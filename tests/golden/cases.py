@@ -313,8 +313,33 @@ CASES = [
 CASE_BY_NAME = {c["name"]: c for c in CASES}
 
 
-def make_input(name_shape_spec, full: bool = True) -> np.ndarray:
-    """Materialise one input of a case from its spec (seeded)."""
+_BIG_CACHE: dict = {}
+
+
+def make_input(name_shape_spec, full: bool = True, rows: int | None = None) -> np.ndarray:
+    """Materialise one input of a case from its spec (seeded).  rows: only
+    the first `rows` rows of a row-major 2-D normal / uniform input (the
+    seeded generator fills arrays in order, so they equal the full array's
+    first rows).  The last two arrays of 256 MiB or more are kept, read-only,
+    for the next request (the large configurations' shared operands)."""
+    name, shape, dtype, fortran, layout, spec = name_shape_spec
+    if (rows is not None and len(shape) == 2 and not fortran and dtype != "bfloat16"
+            and spec["kind"] in ("normal", "uniform") and rows < shape[0]):
+        from inputs import generate
+        return generate(spec, (rows, shape[1]), dtype, fortran)
+    if int(np.prod(shape)) * 4 < (256 << 20):
+        return _make_input(name_shape_spec)
+    key = (tuple(shape), dtype, fortran, json.dumps(spec, sort_keys=True))
+    if key not in _BIG_CACHE:
+        if len(_BIG_CACHE) >= 2:
+            _BIG_CACHE.pop(next(iter(_BIG_CACHE)))
+        a = _make_input(name_shape_spec)
+        a.setflags(write=False)
+        _BIG_CACHE[key] = a
+    return _BIG_CACHE[key]
+
+
+def _make_input(name_shape_spec) -> np.ndarray:
     from inputs import generate, special_values
     name, shape, dtype, fortran, layout, spec = name_shape_spec
     kind = spec["kind"]

@@ -25,7 +25,7 @@ def generate(spec: dict, shape, dtype: str = "float32", fortran: bool = False) -
         a = rng.integers(spec.get("lo", -100), spec.get("hi", 100), tuple(shape), dtype=np.int64)
     else:
         raise ValueError(kind)
-    a = a.astype(np.dtype(dtype))
+    a = a.astype(np.dtype(dtype), copy=False)
     return np.asfortranarray(a) if fortran else a
 
 

@@ -217,3 +217,91 @@ def test_fuse_compile_routes_to_b200(backend, cuda, name):
     finally:
         bafe.set_option("gemm_precision", "auto")
     assert out.tobytes() == np.ascontiguousarray(golden).tobytes()
+
+
+# ---- the reference's own Python front end -------------------------------
+# baseline/_ref holds the reference's Python package, installed unmodified
+# (pip install --target baseline/_ref from a copy of the reference).  Its
+# binding loads the library named by $BAFE_LIB -- here the drop-in library
+# -- and its JittedFunction / FusedFunction compile through
+# bafe_jit_get_or_compile (__init__.py:509-522, 844-885) and call the
+# result with numpy buffers and an np.zeros output (__init__.py:364-383).
+
+REF_PY = ROOT / "baseline" / "_ref"
+needs_ref_py = pytest.mark.skipif(not (REF_PY / "bafe" / "__init__.py").exists() or not DROPIN.exists(),
+                                  reason="the reference's Python package is not installed in baseline/_ref")
+
+
+@pytest.fixture
+def ref_bafe(monkeypatch, tmp_path):
+    """The reference's `bafe` module bound to the drop-in library; returns
+    (module, select), select(name) setting BAFE_BACKEND for the next compile."""
+    import importlib
+    import sys
+    monkeypatch.setenv("BAFE_LIB", str(DROPIN))
+    monkeypatch.setenv("BAFE_CACHE_DIR", str(tmp_path))
+    if str(REF_PY) not in sys.path:
+        sys.path.insert(0, str(REF_PY))
+    mod = importlib.import_module("bafe")
+    assert Path(mod.__file__).resolve().is_relative_to(REF_PY.resolve()), mod.__file__
+
+    def select(name):
+        if name is None:
+            monkeypatch.delenv("BAFE_BACKEND", raising=False)
+        else:
+            monkeypatch.setenv("BAFE_BACKEND", name)
+    return mod, select
+
+
+def _reference_front_end_cases(bafe):
+    """(golden name, jitted callable, its arguments) -- the reference's own
+    front end: @bafe.jit (test_e2e.py:61) and bafe.fuse (test_fuse.py:54)."""
+    @bafe.jit
+    def relu_mm_plus_c(A, B, C):
+        return bafe.relu(bafe.matmul(A, B) + C)
+
+    @bafe.jit
+    def mm(A, B):
+        return bafe.matmul(A, B)
+
+    @bafe.jit
+    def relu_add(X, bias):
+        return bafe.relu(X + bias)
+
+    out = []
+    meta, stored, golden = cases.load("e2e_relu_matmul_plus_c")
+    out.append(("e2e_relu_matmul_plus_c", relu_mm_plus_c, [stored[n] for n in "ABC"], golden))
+    meta, stored, golden = cases.load("fuse_matmul_then_add_bias")
+    out.append(("fuse_matmul_then_add_bias", bafe.fuse(mm, relu_add), [stored["A"], stored["B"], stored["bias"]], golden))
+    return out
+
+
+@needs_ref_py
+def test_reference_python_front_end_on_its_own_emitter(ref_bafe):
+    """BAFE_BACKEND unset: the reference's Python package over the drop-in
+    library still runs the C99 emitter and reproduces the goldens."""
+    bafe, select = ref_bafe
+    select(None)
+    for name, fn, args, golden in _reference_front_end_cases(bafe):
+        out = fn(*args)
+        assert np.asarray(out).tobytes() == np.ascontiguousarray(golden).tobytes(), name
+
+
+@needs_ref_py
+@pytest.mark.gpu
+def test_reference_python_front_end_on_b200(ref_bafe, cuda):
+    """BAFE_BACKEND=cuda: the reference's @bafe.jit and bafe.fuse compile
+    onto this backend and, in `exact` GEMM precision, reproduce the goldens
+    bit for bit."""
+    import bafe_b200
+    bafe, select = ref_bafe
+    select("cuda")
+    bafe_b200.set_option("gemm_precision", "exact")
+    try:
+        for name, fn, args, golden in _reference_front_end_cases(bafe):
+            before = bafe_b200.launch_count()
+            out = fn(*args)
+            assert bafe_b200.launch_count() > before, f"{name}: no kernel of the backend ran"
+            assert np.asarray(out).tobytes() == np.ascontiguousarray(golden).tobytes(), name
+    finally:
+        bafe_b200.set_option("gemm_precision", "auto")

@@ -23,9 +23,11 @@ def _inputs(meta, stored):
             arrays[spec["name"]] = stored[spec["name"]]
         else:
             t = (spec["name"], tuple(spec["shape"]), spec["dtype"], spec["fortran"], spec["layout"], spec["spec"])
-            a = cases.make_input(t)
             if meta["panel"] and spec["name"] in meta["panel_inputs"]:
-                a = np.ascontiguousarray(a[meta["panel"][0]:meta["panel"][1]])
+                r0, r1 = meta["panel"]
+                a = np.ascontiguousarray(cases.make_input(t, rows=r1)[r0:r1])
+            else:
+                a = cases.make_input(t)
             arrays[spec["name"]] = a
     return arrays
 
