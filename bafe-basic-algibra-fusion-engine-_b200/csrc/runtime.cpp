@@ -1279,7 +1279,7 @@ int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* r
                 clear_error();                           // the call runs eagerly below
             }
         }
-        if (ds->graph_exec) {
+        if (ds->graph_exec && options().host_graphs) {
             if (cudaGraphLaunch(ds->graph_exec, ds->stream) != cudaSuccess) {
                 cudaGetLastError();
                 set_error(7, "cudaGraphLaunch of the host call failed");

@@ -74,7 +74,9 @@ def config(request, cuda):
     case = cases.CASE_BY_NAME[panels[0]]
     dev = []
     for spec in case["inputs"]:
-        dev.append(torch.from_numpy(cases.make_input(spec)).cuda())
+        host = cases.make_input(spec)
+        dev.append(torch.empty(host.shape, dtype=torch.float32, device="cuda"))
+        dev[-1].copy_(torch.from_numpy(np.require(host, requirements="W")))
     sig = [float(s[5].get("std", 1.0)) for s in case["inputs"]]
     K = case["inputs"][0][1][1]
     plan_exact, exact = _run(torch, case, dev, "exact")
