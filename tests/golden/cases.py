@@ -177,6 +177,16 @@ CASES = [
          inputs=[("A", (256, 320), "float32", False, 0, N01(214)), ("B", (320, 256), "float32", False, 0, N01(215)),
                  ("C", (256, 256), "float32", False, 0, N01(216))],
          store_inputs=False),
+    # ---- tensor-core layouts at sizes where auto picks the tensor cores --
+    dict(name="col_a_relu_matmul_plus_c_320x384x512", cite="bafe/src/codegen.c:206-213 (A Fortran order), 240-290",
+         build=lambda g, A, B, C: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), C])]),
+         inputs=[("A", (320, 512), "float32", True, 1, N01(217)), ("B", (512, 384), "float32", False, 0, N01(218)),
+                 ("C", (320, 384), "float32", False, 0, N01(219))],
+         store_inputs=False),
+    dict(name="batched_matmul_4x256x320x256", cite="bafe/src/codegen.c:215-236 (batched rank-3 matmul)",
+         build=lambda g, A, B: g.add("matmul", [A, B]),
+         inputs=[("A", (4, 256, 320), "float32", False, 0, N01(220)), ("B", (4, 320, 256), "float32", False, 0, N01(221))],
+         store_inputs=False),
     # ---- scripts/test_smoke.c (deterministic pattern) ----------------------
     dict(name="smoke_c_pattern", cite="scripts/test_smoke.c:11-24,54-56",
          build=lambda g, A, B, b: g.add("relu", [g.add("add", [g.add("matmul", [A, B]), b])]),
