@@ -181,6 +181,25 @@ class Kernel:
         self.run_device([t.data_ptr() for t in inputs] + [out.data_ptr()], s.cuda_stream)
 
     @property
+    def num_steps(self) -> int:
+        """Launch steps of the plan (the lines of describe())."""
+        return int(lib.bafe_cuda_plan_num_steps(self.plan))
+
+    def run_torch_timed(self, inputs: Sequence, out, events: Sequence, stream=None) -> None:
+        """run_torch with events[2i] / events[2i+1] (torch.cuda.Event with
+        timing) recorded before / after step i's launches."""
+        import torch
+        s = stream if stream is not None else torch.cuda.current_stream()
+        ptrs = [t.data_ptr() for t in inputs] + [out.data_ptr()]
+        arr = (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+        for e in events:
+            if not e.cuda_event:          # torch creates the CUDA event at its first record
+                e.record(s)
+        evs = (ctypes.c_void_p * len(events))(*[ctypes.c_void_p(e.cuda_event) for e in events])
+        check(lib.bafe_cuda_run_device_timed(self.plan, arr, len(ptrs), ctypes.c_void_p(int(s.cuda_stream)), evs,
+                                             len(events)), "run_device_timed")
+
+    @property
     def k_slice_align(self) -> int:
         """Multiple of K that K-slice bounds must be; 0: the plan cannot run in K slices."""
         return int(lib.bafe_cuda_plan_k_slice_align(self.plan))

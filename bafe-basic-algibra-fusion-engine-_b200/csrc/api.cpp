@@ -334,6 +334,21 @@ BAFE_API int bafe_cuda_run_device(int plan, void* const* ptrs, int n_ptrs, void*
     return run_plan_device(*p, ptrs, n_ptrs, stream);
 }
 
+BAFE_API int bafe_cuda_plan_num_steps(int plan) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return -1; }
+    return (int)p->steps.size();
+}
+
+BAFE_API int bafe_cuda_run_device_timed(int plan, void* const* ptrs, int n_ptrs, void* stream, void* const* step_events,
+                                        int n_events) {
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    Plan* p = plan_ptr(plan);
+    if (!p) { set_error(10, "unknown plan " + std::to_string(plan)); return 10; }
+    return run_plan_device_timed(*p, ptrs, n_ptrs, stream, step_events, n_events);
+}
+
 BAFE_API int bafe_cuda_plan_k_slice_align(int plan) {
     std::lock_guard<std::recursive_mutex> lk(g_mu);
     Plan* p = plan_ptr(plan);

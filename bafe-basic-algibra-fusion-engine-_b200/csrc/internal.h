@@ -196,6 +196,10 @@ int run_plan_device(Plan& p, void* const* ptrs, int n_ptrs, void* stream);
 int run_plan_device_ksliced(Plan& p, void* const* ptrs, int n_ptrs, void* stream, int n_slices,
                             const int64_t* k_bounds, void* const* ready);
 int plan_k_slice_align(const Plan& p);
+// run_plan_device with step_events[2i] / [2i+1] (cudaEvent_t) recorded on the
+// stream before / after step i's launches.
+int run_plan_device_timed(Plan& p, void* const* ptrs, int n_ptrs, void* stream, void* const* step_events,
+                          int n_events);
 // resident: per input, nonzero = ptrs[k] is already a device buffer (or null: none);
 // ready: cudaEvent_t the kernels wait for before reading them (or null)
 int run_plan_host(Plan& p, void* const* ptrs, int n_ptrs, const unsigned char* resident = nullptr,

@@ -485,6 +485,7 @@ struct Pass {
     int64_t r0 = 0, rows = 0;
     int64_t k0 = 0, k1 = 0;
     bool first = true, last = true;
+    const cudaEvent_t* step_events = nullptr;   // All: recorded before / after each step (2 per step)
 };
 
 bool same_buf(const BufRef& a, const BufRef& b) { return a.kind == b.kind && a.idx == b.idx; }
@@ -543,6 +544,7 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
         }
         void* dst = at_row(ptr_of(s.dst), s.dst_rb);
         const int64_t n_run = cut ? pass.rows * s.row_elems : s.n;
+        if (pass.step_events) cudaEventRecord(pass.step_events[2 * si], stream);
         const int64_t m_run = cut ? pass.rows : s.M;
         switch (s.kind) {
             case StepKind::Zero: {
@@ -777,6 +779,7 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 break;
             }
         }
+        if (pass.step_events) cudaEventRecord(pass.step_events[2 * si + 1], stream);
     }
     return 0;
 }
@@ -838,6 +841,31 @@ int run_plan_device_ksliced(Plan& p, void* const* ptrs, int n_ptrs, void* stream
         if (int rc = run_steps(p, ds, dev, ptrs, st, sl)) return rc;
     }
     return 0;
+}
+
+int run_plan_device_timed(Plan& p, void* const* ptrs, int n_ptrs, void* stream_v, void* const* step_events,
+                          int n_events) {
+    if (n_ptrs != p.n_inputs + 1) {
+        set_error(8, "plan takes " + std::to_string(p.n_inputs + 1) + " pointers, got " + std::to_string(n_ptrs));
+        return 8;
+    }
+    if (!step_events || n_events != 2 * (int)p.steps.size()) {
+        set_error(8, "timed run: the plan has " + std::to_string(p.steps.size()) + " steps, so it takes " +
+                         std::to_string(2 * p.steps.size()) + " events");
+        return 8;
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        set_error(4, "no CUDA device available");
+        return 4;
+    }
+    DeviceState* ds = nullptr;
+    if (int rc = ensure_device_state(p, dev, ds)) return rc;
+    if (int rc = ensure_tmps(p, ds)) return rc;
+    Pass pass;
+    pass.step_events = reinterpret_cast<const cudaEvent_t*>(step_events);
+    return run_steps(p, ds, dev, ptrs, (cudaStream_t)stream_v, pass);
 }
 
 int plan_k_slice_align(const Plan& p) {

@@ -235,6 +235,18 @@ int bafe_cuda_plan_row_split(int plan, int64_t *rows, int64_t *in_row_bytes, int
  * nonzero code with the message available from bafe_cuda_last_error. */
 int bafe_cuda_run_device(int plan, void *const *ptrs, int n_ptrs, void *stream);
 
+/* Number of launch steps of a plan (the lines of bafe_cuda_plan_describe),
+ * -1 for an unknown plan. */
+int bafe_cuda_plan_num_steps(int plan);
+/* bafe_cuda_run_device that also records step_events[2i] and
+ * step_events[2i+1] (cudaEvent_t, created by the caller) on `stream` right
+ * before and after step i's launches, n_events = 2 * the plan's steps: the
+ * caller reads each kernel's device time with cudaEventElapsedTime.
+ * Extension (per-kernel timing for rooflines).  Returns 0 or a nonzero
+ * code. */
+int bafe_cuda_run_device_timed(int plan, void *const *ptrs, int n_ptrs, void *stream, void *const *step_events,
+                               int n_events);
+
 /* K-sliced device run, for a multi-GPU caller whose B arrives over NVLink
  * in slabs of rows while the GEMM runs.  The plan must be one CTA-pair
  * tensor-core GEMM (with its tf32 pre-passes) with an fp32 output,

@@ -414,3 +414,35 @@ def test_replayed_host_calls_still_time_the_device(cuda):
         k(a, a)
         ms = lib.bafe_cuda_plan_last_device_ms(k.plan)
         assert 0.0 < ms < 100.0, ms
+
+
+def test_device_run_timed_per_step(cuda):
+    """bafe_cuda_run_device_timed records the caller's events around every
+    launch step; the steps' times add up to at most the whole call's and the
+    result is the plain device run's."""
+    torch = cuda
+    from bafe_b200.graph import GraphBuilder
+    g = GraphBuilder()
+    a = g.add_input("A", (1024, 1024), 0, 0)
+    b = g.add_input("B", (1024, 1024), 0, 2)
+    c = g.add_input("C", (1024, 1024), 0, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
+    k = bafe.compile_graph(g)
+    n = k.num_steps
+    assert n == 3 and k.describe().strip().splitlines()[-1].startswith("gemm.tc.3xtf32")
+    ins = [torch.randn(1024, 1024, device="cuda") for _ in range(3)]
+    want = torch.empty(1024, 1024, device="cuda")
+    k.run_torch(ins, want)
+    out = torch.empty(1024, 1024, device="cuda")
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * n)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    k.run_torch_timed(ins, out, evs)
+    e1.record()
+    torch.cuda.synchronize()
+    bafe.synchronize()
+    steps = [evs[2 * j].elapsed_time(evs[2 * j + 1]) for j in range(n)]
+    assert all(t > 0 for t in steps) and sum(steps) <= e0.elapsed_time(e1) * 1.01 + 0.01, steps
+    assert torch.equal(out, want)
+    with pytest.raises(RuntimeError):
+        k.run_torch_timed(ins, out, evs[:-1])

@@ -236,3 +236,23 @@ def test_gemm_beyond_32_bit_tile_coordinates_takes_the_exact_kernel():
     if gpu_available():
         assert plan(1 << 20).startswith("gemm.tc")
     assert plan((1 << 31) - 100).startswith("gemm.exact")
+
+
+def test_plan_steps_match_the_description():
+    """bafe_cuda_plan_num_steps counts the launch steps describe() lists
+    (one line each): the per-step timing events follow it."""
+    g = GraphBuilder()
+    a = g.add_input("A", (512, 512), 0, 0)
+    b = g.add_input("B", (512, 512), 0, 2)
+    c = g.add_input("C", (512, 512), 0, 0)
+    g.set_output(g.add("relu", [g.add("add", [g.add("matmul", [a, b]), c])]))
+    bafe.set_option("gemm_precision", "3xtf32")
+    try:
+        k = bafe.compile_graph(g)
+    finally:
+        bafe.set_option("gemm_precision", "auto")
+    assert k.num_steps == len(k.describe().strip().splitlines()) == 3
+    e = GraphBuilder()
+    x = e.add_input("X", (1000,), 0, 0)
+    e.set_output(e.add("relu", [x]))
+    assert bafe.compile_graph(e).num_steps == 1
