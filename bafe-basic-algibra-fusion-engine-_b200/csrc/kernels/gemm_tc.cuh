@@ -29,18 +29,21 @@
 // error a random walk over chunks (~KC * K^0.5), inside the 3xTF32 bound.
 //
 // kind::tf32 reads the top 19 bits of each fp32 operand (the low 13
-// mantissa bits are ignored).  3xTF32 operands: A's raw values are its
-// "hi" part (truncated by the tensor core) and A_lo = rn_tf32(x -
-// trunc_tf32(x)); B is split to nearest, B_hi = rn_tf32(x), B_lo =
-// rn_tf32(x - B_hi), so the dropped A_lo.B_lo term has no systematic sign
-// (with both sides truncated it always had the product's sign and biased
-// sums toward zero: mean error -1.9e-9 at 16384^3, now ~0).  Each k-step
-//     acc += A.B_lo + A_lo.B_hi, then acc += A.B_hi   (three MMAs)
-// By default streaming pre-passes (tf32_residual for A, tf32_split for B)
+// mantissa bits are ignored).  3xTF32 operands: A is split to nearest,
+// A_hi = rn_tf32(x), A_lo = rn_tf32(x - A_hi); B's raw values are its "hi"
+// part (truncated by the tensor core) and B_lo = rn_tf32(x - trunc_tf32(x)).
+// With one side rounded to nearest the dropped A_lo.B_lo term has no
+// systematic sign (with both sides truncated it always had the product's
+// sign and biased sums toward zero: mean error -1.9e-9 at 16384^3, now ~0).
+// Rounding A rather than B: a sharded GEMM's rank holds a row panel of A
+// but all of B, so it writes one copy of B (B_lo) instead of two.  The
+// stage holds [A_hi][B][A_lo][B_lo]; each k-step
+//     acc += A_hi.B_lo + A_lo.B, then acc += A_hi.B   (three MMAs)
+// By default streaming pre-passes (tf32_split for A, tf32_residual for B)
 // write the parts to memory and TMA loads them.  With CONVERT the producer
 // loads only the raw operands and the accumulate threads write the parts
-// into the stage in shared memory (lo into the second half, B_hi over the
-// raw B; elementwise, so the swizzle needs no index
+// into the stage in shared memory (lo into the second half, A_hi over the
+// raw A; elementwise, so the swizzle needs no index
 // mapping), releasing each stage to the MMA issuer on LO(s): no pre-pass,
 // no scratch, half the operand bytes from L2 and HBM -- but 64 KB more
 // shared-memory traffic per k-block and CTA, which costs throughput on B200.
@@ -334,10 +337,10 @@ __device__ __forceinline__ void sts128(u32 addr, uint4 v) {
 // at (ct + i * NT) * 16 bytes) from `hi` to the same offsets at `lo`, four
 // chunks per round (four shared-memory loads in flight; the callers hold
 // 128 accumulators, so a wider round spills).
-// The first A_PER rounds cover the stage's A tile: the raw operand stays
-// the hi part and lo = tf32_lo(x).  The remaining rounds cover B: hi and lo
-// come from the round-to-nearest split (tf32_split) and hi is written back
-// over the raw operand -- the same operands the pre-pass gives the kernel.
+// The first A_PER rounds cover the stage's A tile: hi and lo come from the
+// round-to-nearest split (tf32_split) and hi is written back over the raw
+// operand.  The remaining rounds cover B: the raw operand stays the hi part
+// and lo = tf32_lo(x) -- the same operands the pre-passes give the kernel.
 template <int PER, int NT, int A_PER>
 __device__ __forceinline__ void convert_stage(u32 hi, u32 lo, int ct) {
     constexpr int R = 4;
@@ -347,7 +350,7 @@ __device__ __forceinline__ void convert_stage(u32 hi, u32 lo, int ct) {
         uint4 v[R];
 #pragma unroll
         for (int j = 0; j < R; ++j) v[j] = lds128(hi + 16u * (u32)(ct + (r + j) * NT));
-        if (r < A_PER) {
+        if (r >= A_PER) {
 #pragma unroll
             for (int j = 0; j < R; ++j) {
                 v[j].x = __float_as_uint(tf32_lo(__uint_as_float(v[j].x)));

@@ -723,13 +723,18 @@ struct Lowerer {
         }
         if (s.kind == StepKind::GemmTc && s.tc_variant == 3 && !s.tc_convert) {
             // 3xTF32 operand parts, written once per call by streaming
-            // pre-passes into plan scratch: A_lo = rn_tf32(x - trunc_tf32(x))
-            // (A's raw values are its hi part); B split to nearest, B_lo and
-            // B_hi (bafe::tf32_split).
-            s.aux.push_back(emit_residual(s.srcs[0], M * K * a_items, "A"));
-            BufRef b_hi;
-            s.aux.push_back(emit_residual(s.srcs[1], K * Nn * b_items, "B", &b_hi));
-            s.aux.push_back(b_hi);
+            // pre-passes into plan scratch: A split to nearest, A_lo and A_hi
+            // (bafe::tf32_split); B_lo = rn_tf32(x - trunc_tf32(x)) (B's raw
+            // values are its hi part, truncated by the tensor core).  One
+            // operand rounded to nearest keeps the dropped lo.lo term free
+            // of the product's sign; rounding A -- a row panel per rank when
+            // the GEMM is sharded -- rather than B, which every rank reads
+            // whole, leaves each rank one write of B instead of two.
+            // aux = {A_lo, B_lo, A_hi}.
+            BufRef a_hi;
+            s.aux.push_back(emit_residual(s.srcs[0], M * K * a_items, "A", &a_hi));
+            s.aux.push_back(emit_residual(s.srcs[1], K * Nn * b_items, "B"));
+            s.aux.push_back(a_hi);
         }
         if (s.kind == StepKind::GemmExact) {
             // the widest micro-tile that still gives >= 128 blocks (a

@@ -490,17 +490,17 @@ struct Pass {
 
 bool same_buf(const BufRef& a, const BufRef& b) { return a.kind == b.kind && a.idx == b.idx; }
 
-// Role of step si in a K-sliced plan: 0 the GEMM (last step), 1 A's
-// residual pre-pass (writes aux[0]), 2 B's split pre-pass (writes aux[1]
-// and aux[2]), -1 anything else (the plan cannot be sliced).
+// Role of step si in a K-sliced plan: 0 the GEMM (last step), 1 A's split
+// pre-pass (writes aux[0] = A_lo and aux[2] = A_hi), 2 B's residual pre-pass
+// (writes aux[1] = B_lo), -1 anything else (the plan cannot be sliced).
 int k_slice_role(const Plan& p, size_t si) {
     const Step& G = p.steps.back();
     const Step& s = p.steps[si];
     if (si + 1 == p.steps.size()) return 0;
     if (s.kind != StepKind::Ew || G.aux.size() < 3 || s.srcs.size() != 1) return -1;
-    if (!s.has_dst2 && same_buf(s.dst, G.aux[0]) && same_buf(s.srcs[0], G.srcs[0])) return 1;
-    if (s.has_dst2 && same_buf(s.dst, G.aux[1]) && same_buf(s.dst2, G.aux[2]) && same_buf(s.srcs[0], G.srcs[1]))
-        return 2;
+    if (s.has_dst2 && same_buf(s.dst, G.aux[0]) && same_buf(s.dst2, G.aux[2]) && same_buf(s.srcs[0], G.srcs[0]))
+        return 1;
+    if (!s.has_dst2 && same_buf(s.dst, G.aux[1]) && same_buf(s.srcs[0], G.srcs[1])) return 2;
     return -1;
 }
 
@@ -522,7 +522,7 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
         Step& s = p.steps[si];
         if (pass.kind == Pass::Once && s.panel) continue;
         if (pass.kind == Pass::Panel && !s.panel) continue;
-        // K slices: A's residual once (KPrep); B's split over the slice's
+        // K slices: A's split once (KPrep); B's residual over the slice's
         // rows of B and the GEMM over its K range (KSlice)
         const int role = ksl ? k_slice_role(p, si) : -1;
         if (ksl && (pass.kind == Pass::KPrep) != (role == 1)) continue;
@@ -532,10 +532,8 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
             if (cnt == 0) continue;
             char* bsrc = static_cast<char*>(ptr_of(s.srcs[0])) + off * s.src_esize[0];
             char* lo = static_cast<char*>(ptr_of(s.dst)) + off * 4;
-            char* hi = static_cast<char*>(ptr_of(s.dst2)) + off * 4;
-            const bool vec = ds->fn_vec[si] != nullptr && ((uintptr_t)bsrc | (uintptr_t)lo | (uintptr_t)hi) % 16 == 0;
-            uint64_t args[5] = {(uint64_t)(uintptr_t)bsrc, (uint64_t)(uintptr_t)lo, (uint64_t)cnt, (uint64_t)s.ncols,
-                                (uint64_t)(uintptr_t)hi};
+            const bool vec = ds->fn_vec[si] != nullptr && ((uintptr_t)bsrc | (uintptr_t)lo) % 16 == 0;
+            uint64_t args[4] = {(uint64_t)(uintptr_t)bsrc, (uint64_t)(uintptr_t)lo, (uint64_t)cnt, (uint64_t)s.ncols};
             void* params[] = {args};
             if (int rc = launch(vec ? ds->fn_vec[si] : ds->fn[si], grid_for(vec ? cnt / 4 : cnt, dev), 1, 1, 256, 1, 1, 0,
                                 stream, params))
@@ -620,9 +618,11 @@ int run_steps(Plan& p, DeviceState* ds, int dev, void* const* ptrs, cudaStream_t
                 std::string err;
                 const void* a_lo = s.aux.size() > 0 ? at_row(ptr_of(s.aux[0]), s.aux_rb.empty() ? 0 : s.aux_rb[0]) : nullptr;
                 const void* b_lo = s.aux.size() > 1 ? ptr_of(s.aux[1]) : nullptr;
-                const void* a = at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
-                // 3xTF32 reads B's round-to-nearest hi part, written by the split pre-pass
-                const void* b = s.aux.size() > 2 ? ptr_of(s.aux[2]) : ptr_of(s.srcs[1]);
+                // 3xTF32 reads A's round-to-nearest hi part (aux[2], written by
+                // the split pre-pass, row-split like A) and B's raw values
+                const void* a = s.aux.size() > 2 ? at_row(ptr_of(s.aux[2]), s.aux_rb.size() > 2 ? s.aux_rb[2] : 0)
+                                                 : at_row(ptr_of(s.srcs[0]), s.src_rb.empty() ? 0 : s.src_rb[0]);
+                const void* b = ptr_of(s.srcs[1]);
                 if (ds->tc_cache.size() != p.steps.size()) ds->tc_cache.assign(p.steps.size(), DeviceState::TcCached());
                 DeviceState::TcCached& cached = ds->tc_cache[si];
                 Step panel;                                  // the step over this call's rows

@@ -128,11 +128,12 @@ void analyse_row_streaming(Plan& P, const Shape& out_shape) {
                     s.src_rb[k] = s.src_row[k] ? 0 : s.N * s.src_esize[k];
                     need(s.srcs[k], s.src_rb[k]);
                 }
-                if (s.aux.size() == 3) {               // A_lo splits like A; B_lo, B_hi stay whole
+                if (s.aux.size() == 3) {               // A_lo, A_hi split like A; B_lo stays whole
                     s.aux_rb[0] = s.K * 4;
+                    s.aux_rb[2] = s.K * 4;
                     need(s.aux[0], s.aux_rb[0]);
                     need(s.aux[1], 0);
-                    need(s.aux[2], 0);
+                    need(s.aux[2], s.aux_rb[2]);
                 } else if (!s.aux.empty()) {
                     ok = false;
                 }

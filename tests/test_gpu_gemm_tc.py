@@ -103,7 +103,7 @@ def test_3xtf32_fused_epilogues(cuda, epi):
     steps = k.describe().strip().splitlines()
     # residual pre-passes for A and B, then one GEMM carrying the epilogue
     assert [l.split()[0].replace(".pair", "") for l in steps] == ["ew", "ew", "gemm.tc.3xtf32"], steps
-    assert "tf32_residual(A)" in steps[0] and "tf32_split(B)" in steps[1]
+    assert "tf32_split(A)" in steps[0] and "tf32_residual(B)" in steps[1]
     bound = 1e-4 * math.sqrt(512 / 64)
     print(f"3xtf32 epilogue {epi}: max err {err:.3e}")
     assert err <= bound
