@@ -595,13 +595,14 @@ struct Lowerer {
         const bool bf16_ops = T == BAFE_DTYPE_F32 && a.dtype == BAFE_DTYPE_BF16 && b.dtype == BAFE_DTYPE_BF16;
         if ((f32_ops || bf16_ops) && tc_shape_ok(s, f32_ops ? 4 : 2) && prec != "exact") {
             // auto: tensor cores from 256^3 multiply-adds on for bf16 (one
-            // product per k-step), above 256^3 for f32 (three): a 256^3 f32
-            // GEMM is one CTA-pair tile, latency-bound, and the bit-exact
-            // CUDA-core kernel is as fast there (measured on B200: 24.7 us,
-            // against 24.8 us for 3xTF32 with its pre-passes; 512^3: 47.2
-            // against 32.8 us)
+            // product per k-step), above 512^3 for f32 (three): up to there
+            // the 3xTF32 plan (pre-passes + a few pair tiles) is latency-
+            // bound and the bit-exact CUDA-core kernel, spread over enough
+            // blocks, is faster (measured on B200, relu(A.B + C): 256^3 12.7
+            // against 32.8 us, 512^3 35.6 against 38.9 us, 640^3 59.4
+            // against 43.0 us)
             const double macs = (double)M * (double)Nn * (double)K;
-            const bool big = bf16_ops ? macs >= 16777216.0 : macs > 16777216.0;   // 256^3
+            const bool big = bf16_ops ? macs >= 16777216.0 : macs > 134217728.0;   // 256^3 / 512^3
             if (prec == "tf32" || prec == "3xtf32" || big) {
                 s.kind = StepKind::GemmTc;
                 s.tc_variant = (bf16_ops || prec == "tf32") ? 1 : 3;

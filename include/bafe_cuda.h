@@ -303,7 +303,7 @@ void bafe_cuda_clear_error(void);
 
 /* Backend options (strings, process-wide):
  *   "gemm_precision": "auto" (default) | "3xtf32" | "tf32" | "exact";
- *                     auto: 3xTF32 tensor cores for f32 GEMMs above 256^3
+ *                     auto: 3xTF32 tensor cores for f32 GEMMs above 512^3
  *                     multiply-adds, bf16 tensor cores from 256^3, the
  *                     bit-exact CUDA-core kernel otherwise (read when a
  *                     plan is built)

@@ -164,14 +164,18 @@ def test_fused_call_is_bit_exact_to_reference_fuse(cuda, name):
 
 @pytest.mark.gpu
 def test_fused_tensor_core_plan_matches_reference_fuse(cuda):
-    """The 256 x 320 x 256 fused case in the default precision runs one
-    3xTF32 tensor-core kernel with the epilogue fused; it stays within
+    """The 256 x 320 x 256 fused case with 3xTF32 requested runs one
+    tensor-core kernel with the epilogue fused; it stays within
     1e-4 * sqrt(K/64) * rms(A) * rms(B) of the reference's fused output."""
-    h, args, golden = _fuse_case_args("fuse_gemm_then_relu_add_c_256")
-    k = h.kernel_for(*args)
-    steps = k.describe().strip().splitlines()
-    assert "gemm.tc.3xtf32" in steps[-1] and "epi=relu(add(acc,C))" in steps[-1], k.describe()
-    out = h(*args)
+    bafe.set_option("gemm_precision", "3xtf32")
+    try:
+        h, args, golden = _fuse_case_args("fuse_gemm_then_relu_add_c_256")
+        k = h.kernel_for(*args)
+        steps = k.describe().strip().splitlines()
+        assert "gemm.tc.3xtf32" in steps[-1] and "epi=relu(add(acc,C))" in steps[-1], k.describe()
+        out = h(*args)
+    finally:
+        bafe.set_option("gemm_precision", "auto")
     A, B = (a.astype(np.float64) for a in args[:2])
     bound = 1e-4 * np.sqrt(A.shape[1] / 64) * np.sqrt(np.mean(A * A)) * np.sqrt(np.mean(B * B))
     err = float(np.abs(out.astype(np.float64) - golden).max())

@@ -31,6 +31,16 @@ def _graph(M, N, K, epi=True):
     return g
 
 
+def _compile_3xtf32(g):
+    """The 3xTF32 plan (at 512^3 multiply-adds and below `auto` picks the
+    exact CUDA-core kernel, which has no K slices)."""
+    bafe.set_option("gemm_precision", "3xtf32")
+    try:
+        return bafe.compile_graph(g)
+    finally:
+        bafe.set_option("gemm_precision", "auto")
+
+
 def _operands(torch, M, N, K, seed, epi=True):
     gen = torch.Generator(device="cuda").manual_seed(seed)
     std = 1.0 / K ** 0.5
@@ -129,7 +139,7 @@ def test_k_slices_without_epilogue(cuda):
     """A plain matmul (no epilogue operands): the last slice stores the sums."""
     torch = cuda
     M, N, K = 256, 512, 1024
-    k = bafe.compile_graph(_graph(M, N, K, epi=False))
+    k = _compile_3xtf32(_graph(M, N, K, epi=False))
     ins = _operands(torch, M, N, K, 5, epi=False)
     want = _whole(torch, k, ins, M, N, split=False)
     out = torch.empty(M, N, device="cuda")
@@ -153,7 +163,7 @@ def test_k_slices_refused_where_they_do_not_apply(cuda):
     out = torch.empty(M, N, device="cuda")
     with pytest.raises(RuntimeError):
         kx.run_torch_ksliced(ins, out, [0, 512, 1024])
-    k = bafe.compile_graph(_graph(M, N, K))
+    k = _compile_3xtf32(_graph(M, N, K))
     a = k.k_slice_align
     for bad in ([0, a + 4, 1024], [0, 5 * a, 5 * a, 1024], [a, 1024], [0, 5 * a]):
         with pytest.raises(RuntimeError):

@@ -99,7 +99,7 @@ def _rms(a) -> float:
 @pytest.mark.parametrize("name", SMALL)
 def test_tensor_core_precisions_match_reference(name, precision, cuda):
     """Every small golden case in the default precision (`auto`: tensor
-    cores above 256^3 multiply-adds for f32, from 256^3 for bf16; the f32
+    cores above 512^3 multiply-adds for f32, from 256^3 for bf16; the f32
     256^3 configurations run the exact kernel, bit for bit) and with 3xTF32
     forced wherever the shape allows it.  A
     plan that stays on the CUDA cores must be bit-exact; a tensor-core plan
