@@ -140,6 +140,14 @@ def _load() -> ctypes.CDLL:
         "bafe_cuda_run_device_ksliced": ([c_int, POINTER(c_void_p), c_int, c_void_p, c_int, POINTER(ctypes.c_int64),
                                           POINTER(c_void_p)], c_int),
         "bafe_cuda_plan_k_slice_align": ([c_int], c_int),
+        "bafe_cuda_relay_alloc": ([c_int, c_int64, POINTER(ctypes.c_uint64), c_void_p], c_int),
+        "bafe_cuda_relay_free": ([ctypes.c_uint64], c_int),
+        "bafe_cuda_relay_open": ([c_int, c_void_p, POINTER(ctypes.c_uint64)], c_int),
+        "bafe_cuda_relay_close": ([ctypes.c_uint64], c_int),
+        "bafe_cuda_signal_wait": ([ctypes.c_uint64, ctypes.c_uint32, c_void_p], c_int),
+        "bafe_cuda_signal_write": ([ctypes.c_uint64, ctypes.c_uint32, c_void_p], c_int),
+        "bafe_cuda_relay_step": ([ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64, POINTER(c_int64),
+                                  c_int, ctypes.c_uint32, c_int, c_void_p], c_int),
         "bafe_cuda_plan_num_steps": ([c_int], c_int),
         "bafe_cuda_run_device_timed": ([c_int, POINTER(c_void_p), c_int, c_void_p, POINTER(c_void_p), c_int], c_int),
         "bafe_cuda_run_host": ([c_int, POINTER(c_void_p), c_int], c_int),
@@ -190,7 +198,9 @@ EXPORTED_SYMBOLS = (
     "bafe_cuda_jit_cache_dir", "bafe_cuda_jit_get_stats", "bafe_cuda_jit_clear",
     "bafe_cuda_jit_invalidate_memory_cache", "bafe_cuda_version", "bafe_cuda_plan_of",
     "bafe_cuda_plan_num_inputs", "bafe_cuda_plan_describe", "bafe_cuda_plan_output_bytes",
-    "bafe_cuda_plan_input_bytes", "bafe_cuda_plan_row_split", "bafe_cuda_run_device", "bafe_cuda_run_device_ksliced", "bafe_cuda_plan_k_slice_align", "bafe_cuda_plan_num_steps", "bafe_cuda_run_device_timed", "bafe_cuda_run_host", "bafe_cuda_run_host_resident", "bafe_cuda_synchronize", "bafe_cuda_last_error",
+    "bafe_cuda_plan_input_bytes", "bafe_cuda_plan_row_split", "bafe_cuda_run_device", "bafe_cuda_run_device_ksliced", "bafe_cuda_plan_k_slice_align",
+    "bafe_cuda_relay_alloc", "bafe_cuda_relay_free", "bafe_cuda_relay_open", "bafe_cuda_relay_close",
+    "bafe_cuda_signal_wait", "bafe_cuda_signal_write", "bafe_cuda_relay_step", "bafe_cuda_plan_num_steps", "bafe_cuda_run_device_timed", "bafe_cuda_run_host", "bafe_cuda_run_host_resident", "bafe_cuda_synchronize", "bafe_cuda_last_error",
     "bafe_cuda_clear_error", "bafe_cuda_set_option", "bafe_cuda_get_option", "bafe_cuda_launch_count",
     "bafe_cuda_abi_size", "bafe_cuda_gemm_3xtf32_static_scratch",
     "bafe_cuda_calibrate", "bafe_cuda_hardware_model", "bafe_cuda_plan_predict_ms", "bafe_cuda_plan_last_device_ms",

@@ -17,6 +17,11 @@
   overlaps the broadcast of the later ones.  The slices carry the fp32
   sums through the output in the same chunk order as one launch: the
   result is the same bit for bit.
+* The same B can instead travel by copy engines (`CopyEngineRelay`): each
+  rank pushes B's chunks to the next rank of a chain through CUDA IPC
+  mappings and raises that rank's per-chunk flags with stream writes; the
+  GEMM slices wait on the flags with stream waits.  No SM is used for the
+  transfer, so the persistent GEMM keeps every SM while slabs arrive.
 * Elementwise graphs shard by contiguous element ranges with no collective
   (range starts are multiples of 4 elements so every shard keeps 16-byte
   vector access).
@@ -146,6 +151,239 @@ def broadcast_slabs(B, bounds: Sequence[int], dist, src: int = 0, stream=None):
             else:
                 events.append(None)
     return events
+
+
+RELAY_FLAG_WORDS = 1024               # uint32 flags per rank: one per chunk, the last = the ack
+RELAY_ACK = RELAY_FLAG_WORDS - 1
+
+
+def relay_chunks(slab_bounds: Sequence[int], row_bytes: int, split: int = 4,
+                 min_bytes: int = 2 << 20, max_bytes: int = 16 << 20) -> Tuple[List[int], List[int]]:
+    """Chunks of a copy-engine relay over K slabs of a row-major operand.
+
+    Each slab [k_j, k_{j+1}) (rows) is cut into whole-row chunks of about
+    slab/`split` bytes, clamped to [min_bytes, max_bytes]: small enough that
+    a chunk crosses each hop of the chain quickly (the last rank's first
+    slab waits for its chunks to pass every hop), large enough that the copy
+    engines run at link speed.  Returns (byte bounds of the chunks, index of
+    each slab's last chunk)."""
+    bounds, last = [0], []
+    for j in range(len(slab_bounds) - 1):
+        rows = slab_bounds[j + 1] - slab_bounds[j]
+        if rows <= 0:
+            raise ValueError("slab bounds must increase")
+        want = min(max(rows * row_bytes // split, min_bytes), max_bytes)
+        per = max(1, want // row_bytes)
+        n = (rows + per - 1) // per
+        for i in range(1, n + 1):
+            bounds.append((slab_bounds[j] + (rows * i) // n) * row_bytes)
+        last.append(len(bounds) - 2)
+    if len(bounds) - 1 > RELAY_ACK:
+        raise ValueError(f"{len(bounds) - 1} relay chunks: at most {RELAY_ACK}")
+    return bounds, last
+
+
+class _DeviceArray:
+    """A raw device allocation seen by torch.as_tensor (CUDA array interface)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class CopyEngineRelay:
+    """B of a row-panel GEMM relayed down the chain of ranks 0 -> 1 -> ...
+    -> N-1 by copy engines, inside each step (bafe_cuda_relay_step).
+
+    Rank r's copy stream pushes chunk c of its B into rank r+1's B and
+    raises rank r+1's flag c to the step number; rank r+1 forwards a chunk
+    once its flag reaches the step, and its GEMM's K slice j waits (an event
+    on a watch stream, recorded after a stream wait on the flag of slab j's
+    last chunk) for slab j alone.  No SM is used for the transfer, so the
+    persistent GEMM keeps every SM while later slabs are in flight.  A rank
+    writes its predecessor's ack word once its GEMM and its forwarding of
+    the step are done; the predecessor waits for it before overwriting the
+    rank's B in the next step.  Steps are numbered from 1 and must be the
+    same sequence on every rank.
+
+    Construct with `over_ranks` (one process per GPU: buffers exchanged
+    through CUDA IPC handles over `dist`) or `chain` (ranks emulated in one
+    process, each with its own buffers, on any devices)."""
+
+    def __init__(self, buf: int = 0, flags: int = 0, next_buf: int = 0, next_flags: int = 0, prev_flags: int = 0,
+                 root: bool = False):
+        self.buf, self.flags = int(buf), int(flags)
+        self.next_buf, self.next_flags, self.prev_flags = int(next_buf), int(next_flags), int(prev_flags)
+        self.root = bool(root)
+        self._done = None
+        self._owned, self._opened = [], []
+
+    # ------------------------------------------------------------- setup --
+    @staticmethod
+    def _alloc(device: int, nbytes: int, handle=True):
+        import ctypes
+        from ._binding import check, lib
+        ptr = ctypes.c_uint64(0)
+        h = ctypes.create_string_buffer(64) if handle else None
+        check(lib.bafe_cuda_relay_alloc(int(device), int(nbytes), ctypes.byref(ptr), h), "relay_alloc")
+        return ptr.value, (h.raw if handle else None)
+
+    @staticmethod
+    def _open(device: int, handle: bytes) -> int:
+        import ctypes
+        from ._binding import check, lib
+        ptr = ctypes.c_uint64(0)
+        check(lib.bafe_cuda_relay_open(int(device), handle, ctypes.byref(ptr)), "relay_open")
+        return ptr.value
+
+    @classmethod
+    def over_ranks(cls, shape, dist, device: int, typestr: str = "<f4", itemsize: int = 4):
+        """Allocate this rank's B (shape, zeroed) and flag block, exchange
+        IPC handles over `dist` (one all_gather_object, on every rank alike)
+        and map the successor's B and flags and the predecessor's flags.
+        -> (relay, B as a torch tensor on `device` or None, error message or
+        None).  Errors do not raise: every rank gets a relay (holding what
+        it allocated and mapped), so that all of them can agree on the
+        outcome and then close() together."""
+        import math
+        import torch
+        world, rank = dist.get_world_size(), dist.get_rank()
+        r = cls(root=rank == 0)
+        err, mine = None, None
+        try:
+            buf, hbuf = cls._alloc(device, math.prod(shape) * itemsize)
+            r._owned.append(buf)
+            flags, hflags = cls._alloc(device, 4 * RELAY_FLAG_WORDS)
+            r._owned.append(flags)
+            r.buf, r.flags, mine = buf, flags, (hbuf, hflags)
+        except Exception as e:
+            err = f"{type(e).__name__}: {e}"
+        handles = [None] * world
+        dist.all_gather_object(handles, mine)
+        if err is None and any(h is None for h in handles):
+            err = "relay allocation failed on another rank"
+        if err is None:
+            try:
+                if rank + 1 < world:
+                    r.next_buf = cls._open(device, handles[rank + 1][0])
+                    r._opened.append(r.next_buf)
+                    r.next_flags = cls._open(device, handles[rank + 1][1])
+                    r._opened.append(r.next_flags)
+                if rank > 0:
+                    r.prev_flags = cls._open(device, handles[rank - 1][1])
+                    r._opened.append(r.prev_flags)
+            except Exception as e:
+                err = f"{type(e).__name__}: {e}"
+        t = None
+        if r.buf:
+            t = torch.as_tensor(_DeviceArray(r.buf, shape, typestr), device=torch.device("cuda", device))
+        return r, t, err
+
+    @classmethod
+    def chain(cls, shape, devices: Sequence[int], typestr: str = "<f4", itemsize: int = 4):
+        """Ranks emulated in one process: rank i's buffers on devices[i],
+        its successor's and predecessor's used through plain pointers (one
+        device, or devices with peer access).  -> (relays, B tensors)."""
+        import math
+        import torch
+        nbytes = math.prod(shape) * itemsize
+        bufs = [cls._alloc(d, nbytes, handle=False)[0] for d in devices]
+        flags = [cls._alloc(d, 4 * RELAY_FLAG_WORDS, handle=False)[0] for d in devices]
+        n = len(devices)
+        relays = []
+        for i in range(n):
+            r = cls(bufs[i], flags[i], bufs[i + 1] if i + 1 < n else 0, flags[i + 1] if i + 1 < n else 0,
+                    flags[i - 1] if i > 0 else 0, root=i == 0)
+            r._owned = [bufs[i], flags[i]]
+            relays.append(r)
+        tensors = [torch.as_tensor(_DeviceArray(b, shape, typestr), device=torch.device("cuda", d))
+                   for b, d in zip(bufs, devices)]
+        return relays, tensors
+
+    def close(self, dist=None) -> None:
+        """Unmap the peers' buffers, then free this rank's.  Every rank must
+        be done with the buffers (the caller synchronises its device; across
+        processes it passes `dist`, and the ranks meet in a barrier before
+        and after unmapping, so no buffer is freed while a peer maps it)."""
+        from ._binding import lib
+        multi = dist is not None and dist.is_initialized() and dist.get_world_size() > 1
+        if multi:
+            dist.barrier()
+        for p in self._opened:
+            lib.bafe_cuda_relay_close(p)
+        if multi:
+            dist.barrier()
+        for p in self._owned:
+            lib.bafe_cuda_relay_free(p)
+        self._opened, self._owned = [], []
+
+    def release(self, step: int) -> None:
+        """Raise every flag of this rank (chunks and ack) far past `step` on
+        a fresh stream, so that none of this rank's stream waits can stay
+        pending -- the way out when a step did not complete in time (a peer
+        failed).  The relayed contents are then garbage; close the relay."""
+        import ctypes
+        import torch
+        from ._binding import lib
+        if not self.flags:
+            return
+        s = torch.cuda.Stream()
+        sp = ctypes.c_void_p(int(s.cuda_stream))
+        v = (int(step) + (1 << 30)) & 0xFFFFFFFF
+        for i in range(RELAY_FLAG_WORDS):
+            lib.bafe_cuda_signal_write(self.flags + 4 * i, v, sp)
+
+    # -------------------------------------------------------------- step --
+    def send(self, step: int, chunk_bounds: Sequence[int], stream, start=None) -> None:
+        """Enqueue this rank's part of step `step` on `stream` (its copy
+        stream): the root after `start` (an event: the step's operand is
+        ready); a forwarding rank after its successor's ack of the previous
+        step, chunk by chunk as each arrives."""
+        import ctypes
+        import torch
+        from ._binding import check, lib
+        sp = ctypes.c_void_p(int(stream.cuda_stream))
+        if start is not None:
+            stream.wait_event(start)
+        self._done = None
+        if not self.next_buf:
+            return
+        check(lib.bafe_cuda_signal_wait(self.flags + 4 * RELAY_ACK, (step - 1) & 0xFFFFFFFF, sp), "signal_wait")
+        n = len(chunk_bounds) - 1
+        b = (ctypes.c_int64 * (n + 1))(*[int(x) for x in chunk_bounds])
+        check(lib.bafe_cuda_relay_step(self.buf, self.flags, self.next_buf, self.next_flags, b, n,
+                                       step & 0xFFFFFFFF, int(self.root), sp), "relay_step")
+        self._done = torch.cuda.Event()
+        self._done.record(stream)
+
+    def ready(self, step: int, last_chunks: Sequence[int], stream) -> list:
+        """Events for the GEMM's K slices: event j is recorded on `stream`
+        (a watch stream) once slab j's last chunk has arrived; the root's
+        slabs are resident (None)."""
+        import ctypes
+        import torch
+        from ._binding import check, lib
+        if self.root:
+            return [None] * len(last_chunks)
+        sp = ctypes.c_void_p(int(stream.cuda_stream))
+        evs = []
+        for c in last_chunks:
+            check(lib.bafe_cuda_signal_wait(self.flags + 4 * int(c), step & 0xFFFFFFFF, sp), "signal_wait")
+            e = torch.cuda.Event()
+            e.record(stream)
+            evs.append(e)
+        return evs
+
+    def finish(self, step: int, stream) -> None:
+        """After this rank's GEMM of the step (enqueued on `stream`): wait
+        for its forwarding, then acknowledge the step to the predecessor."""
+        import ctypes
+        from ._binding import check, lib
+        if self._done is not None:
+            stream.wait_event(self._done)
+        if self.prev_flags:
+            check(lib.bafe_cuda_signal_write(self.prev_flags + 4 * RELAY_ACK, step & 0xFFFFFFFF,
+                                             ctypes.c_void_p(int(stream.cuda_stream))), "signal_write")
 
 
 class _null:

@@ -273,6 +273,120 @@ def time_bcast_steps(c, kernel, ins, out, bounds, free_sms, steps, warmup):
     return c.max(ev[0].elapsed_time(ev[steps])), launches
 
 
+def time_relay_steps(c, kernel, ins, out, bounds, relay, steps, warmup, timeout_s=30.0):
+    """Steps whose B reaches every rank inside the step through the
+    copy-engine relay (parallel.CopyEngineRelay): rank 0's B is pushed down
+    the chain 0 -> 1 -> ... chunk by chunk by copy engines, and the plan
+    runs in K slices, slice j waiting (a stream wait on the flag of slab j's
+    last chunk) for slab j only; the GEMM keeps every SM.  Each step's relay
+    starts after the previous step on rank 0 and after the next rank
+    acknowledged it.  Runs on its own streams; completion is polled with a
+    deadline, after which the rank raises its own flags so that no stream
+    wait stays pending.  -> (max-over-ranks ms of the timed region or None,
+    GEMM launches counted, True when every rank completed)."""
+    import bafe_b200 as bafe
+    from bafe_b200.parallel import relay_chunks
+    torch = c.torch
+    comp, copy, watch = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    comp.wait_stream(torch.cuda.current_stream())
+    chunk_bounds, last = relay_chunks(bounds, ins[1].shape[1] * ins[1].element_size())
+    n = [0]
+
+    def step(start):
+        n[0] += 1
+        start.record(comp)
+        relay.send(n[0], chunk_bounds, copy, start if c.rank == 0 else None)
+        evs = relay.ready(n[0], last, watch)
+        kernel.run_torch_ksliced(ins, out, bounds, ready=evs, stream=comp)
+        relay.finish(n[0], comp)
+
+    def drained(ev):
+        t_end = time.perf_counter() + timeout_s
+        while not ev.query():
+            if time.perf_counter() > t_end:
+                return False
+            time.sleep(0.0005)
+        return True
+
+    def run(k_steps, events):
+        try:
+            for i in range(k_steps):
+                step(events[i])
+        except Exception:
+            return False
+        finally:
+            events[k_steps].record(comp)
+        return drained(events[k_steps])
+
+    ok = run(warmup, [torch.cuda.Event() for _ in range(warmup + 1)])
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    launches = 0
+    if c.sum(0.0 if ok else 1.0) == 0:
+        c.barrier()
+        launches0 = bafe.launch_count()
+        ok = run(steps, ev)
+        launches = bafe.launch_count() - launches0
+    else:
+        ok = False
+    if not ok:
+        relay.release(n[0])
+    comp.synchronize()
+    copy.synchronize()
+    watch.synchronize()
+    all_ok = c.sum(0.0 if ok else 1.0) == 0
+    c.barrier()
+    return (c.max(ev[0].elapsed_time(ev[steps])) if all_ok else None), launches, all_ok
+
+
+def bench_relay(c, k, ins, out, S, ms_bcast, flops_total, steps, warmup):
+    """The B-inside-the-step variant over the copy-engine relay: K slabs
+    sized from the K-sliced GEMM's time with B resident, the NCCL
+    broadcast's time (the relay moves B at a similar link rate) and a
+    measured slice-boundary cost, with every SM kept by the GEMM."""
+    from bafe_b200.parallel import CopyEngineRelay, k_slab_schedule
+    torch = c.torch
+    relay, Brel, err = CopyEngineRelay.over_ranks(tuple(ins[1].shape), c.dist, c.local)
+    if c.sum(0.0 if err is None else 1.0) > 0:
+        relay.close(c.dist)
+        return {"unavailable": (err or "relay setup failed on another rank")[:300]}
+    all_ok, t, bounds, boundary_ms = False, {}, [0, S], 0.0
+    try:
+        if c.rank == 0:
+            Brel.copy_(ins[1])
+        torch.cuda.synchronize()
+        rins = [ins[0], Brel] + list(ins[2:])
+        # the cost of one more slice: two equal slices against one, B resident
+        half = (S // 2) // k.k_slice_align * k.k_slice_align
+        for name, b in (("one", [0, S]), ("two", [0, half, S])):
+            for _ in range(2):
+                k.run_torch_ksliced(rins, out, b)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(3):
+                k.run_torch_ksliced(rins, out, b)
+            e1.record()
+            torch.cuda.synchronize()
+            t[name] = c.max(e0.elapsed_time(e1) / 3)
+        boundary_ms = max(t["two"] - t["one"], 0.01)
+        bounds = k_slab_schedule(S, k.k_slice_align, t["one"], max(ms_bcast, 0.1), boundary_ms, keep=1.0)
+        if os.environ.get("BENCH_RELAY_SLABS"):
+            bounds = [int(x) for x in os.environ["BENCH_RELAY_SLABS"].split(",")]
+        ms_total, n_launch, all_ok = time_relay_steps(c, k, rins, out, bounds, relay, steps, warmup)
+    finally:
+        torch.cuda.synchronize()
+        relay.close(c.dist)
+    if not all_ok:
+        return {"unavailable": "a relay step did not complete within its deadline on some rank"}
+    ms = ms_total / steps
+    return {"value": round(flops_total / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "k_slabs": bounds, "slice_boundary_ms": round(boundary_ms, 4),
+            "gemm_k_sliced_ms": round(t["one"], 4), "gpu_launches": int(c.sum(n_launch)),
+            "how": ("rank 0's B pushed down the chain of ranks by copy engines inside each timed step "
+                    "(CUDA IPC buffers, stream-ordered flag waits, no SM used by the transfer); "
+                    f"{len(bounds) - 1} K slabs, GEMM K slice j waits for slab j; max over ranks")}
+
+
 class _NpPtr:
     """A numpy array seen through time_e2e's data_ptr() (pageable host memory)."""
 
@@ -582,6 +696,9 @@ def bench_gemm(c: Ctx) -> dict:
                                 + ("one piece, then the GEMM" if len(bounds) == 2 else
                                    f"{len(bounds) - 1} K slabs on a side stream; GEMM K slice j waits for slab j")
                                 + "); max over ranks"}
+        if k.k_slice_align and os.environ.get("BENCH_RELAY", "1") != "0":
+            res["b_relay_copy_engine"] = bench_relay(c, k, ins, out, S, max(ms_plain - ms_step, 0.0),
+                                                     flops_total, args.steps, args.warmup)
     if args.e2e_steps > 0 and epi == "c":
         hA, hB, hC = A.cpu().pin_memory(), B.cpu().pin_memory(), C.cpu().pin_memory()
         hO = torch.empty(rows, S).pin_memory()

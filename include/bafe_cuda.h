@@ -269,6 +269,36 @@ int bafe_cuda_run_device_ksliced(int plan, void *const *ptrs, int n_ptrs, void *
  * plan. */
 int bafe_cuda_plan_k_slice_align(int plan);
 
+/* ------------------------------------------------------------------------
+ * Copy-engine relay (extension; the reference is single-threaded).  Moves
+ * an operand (B of a row-panel GEMM) down a chain of ranks inside a call
+ * without occupying SMs, so the K-sliced GEMM keeps every SM while the
+ * operand's later slabs are in flight.  Rank r's copy engine pushes chunk c
+ * of its buffer into rank r+1's buffer and then raises rank r+1's flag c to
+ * the step number; waits are stream-ordered (cuStreamWaitValue32, executed
+ * by the GPU's front end).  A flag block is an array of uint32 (zeroed at
+ * allocation); flags count steps and are never reset.
+ * ---------------------------------------------------------------------- */
+/* cudaMalloc `bytes` on `device`, zero them, and write the 64-byte CUDA IPC
+ * handle of the allocation to ipc_handle (NULL: no handle). */
+int bafe_cuda_relay_alloc(int device, int64_t bytes, uint64_t *dptr, void *ipc_handle);
+int bafe_cuda_relay_free(uint64_t dptr);
+/* Map another process's relay buffer on `device` (peer access enabled). */
+int bafe_cuda_relay_open(int device, const void *ipc_handle, uint64_t *dptr);
+int bafe_cuda_relay_close(uint64_t dptr);
+/* Enqueue on `stream` (a cudaStream_t) a wait until *(uint32_t *)addr >=
+ * value (wrap-around compare), or a fenced write of value to addr after
+ * the stream's earlier work.  addr may be a peer's mapped flag. */
+int bafe_cuda_signal_wait(uint64_t addr, uint32_t value, void *stream);
+int bafe_cuda_signal_write(uint64_t addr, uint32_t value, void *stream);
+/* Enqueue one step of the relay on `stream`.  Chunk c is bytes
+ * [bounds[c], bounds[c+1]) of the buffer.  For each chunk in order: unless
+ * `have` (this rank holds the operand already), wait until flags[c] >=
+ * step; then, if next_buf is nonzero, copy the chunk to the same offsets of
+ * next_buf and write next_flags[c] = step.  Returns 0 or a nonzero code. */
+int bafe_cuda_relay_step(uint64_t buf, uint64_t flags, uint64_t next_buf, uint64_t next_flags,
+                         const int64_t *bounds, int n_chunks, uint32_t step, int have, void *stream);
+
 /* Same as calling the plan's function: host pointers, synchronous.
  * Returns 0 or a nonzero code. */
 int bafe_cuda_run_host(int plan, void *const *ptrs, int n_ptrs);

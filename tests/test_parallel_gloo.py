@@ -11,7 +11,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
-from bafe_b200.parallel import element_ranges, row_panels
+from bafe_b200.parallel import element_ranges, relay_chunks, row_panels
 
 ROOT = Path(__file__).resolve().parent.parent
 PATHS = [str(ROOT / "bafe-basic-algibra-fusion-engine-_b200"), str(ROOT), str(ROOT / "tests" / "golden")]
@@ -309,3 +309,18 @@ def test_k_slab_schedule_follows_the_measured_times():
     # a broadcast cheaper than a slice boundary is not worth slicing
     assert k_slab_schedule(K, align, 18.4, 0.05, 0.16, keep=0.9) == [0, K]
     assert k_slab_schedule(100, 64, 1.0, 1.0, 0.01) == [0, 100]
+
+
+def test_relay_chunks_cover_the_slabs_in_whole_rows():
+    slabs, row = [0, 96, 480, 1152], 512 * 4
+    bounds, last = relay_chunks(slabs, row, min_bytes=64 << 10)
+    assert bounds[0] == 0 and bounds[-1] == 1152 * row
+    assert all(b > a for a, b in zip(bounds, bounds[1:]))
+    assert all(b % row == 0 for b in bounds)
+    assert [bounds[i + 1] // row for i in last] == slabs[1:]      # each slab ends on a chunk bound
+    # the 16384^3 operand: a small first slab in a few chunks, later chunks at most 16 MiB
+    big, last = relay_chunks([0, 96, 1056, 16384], 16384 * 4)
+    assert len(big) - 1 <= 1023 and max(b - a for a, b in zip(big, big[1:])) <= 16 << 20
+    assert last[0] >= 2
+    with pytest.raises(ValueError):
+        relay_chunks([0, 96, 96], row)
