@@ -1324,6 +1324,24 @@ __device__ __forceinline__ void gemm_tc_pair(const TcArgs& g) {
                     tile_coords(g, t, mb, nb, bi);
                     Spec::prefetch(g, bi, (i64)mb * 2 * BM + (i64)cta * BM + q * 32 + lane, (i64)nb * BN + half * 128);
                 }
+                // ... and in a K slice that continues earlier sums, the sums
+                // this pair's next tile starts from (read when it begins)
+                if (g.acc_in && c == (c1 - 2 > c0 ? c1 - 2 : c0) && u + num_pairs < g.num_units) {
+                    int tn, c0n, c1n, partn;
+                    unit_chunks(u + num_pairs, tn, c0n, c1n, partn);
+                    if (partn <= 0) {
+                        int mb, nb, bi;
+                        tile_coords(g, tn, mb, nb, bi);
+                        const i64 i = (i64)mb * 2 * BM + (i64)cta * BM + q * 32 + lane;
+                        const i64 j0 = (i64)nb * BN + half * 128;
+                        if (i < g.M) {
+                            const char* row = reinterpret_cast<const char*>(g.out) + (bi * g.o_bstride + i * g.N) * 4;
+#pragma unroll
+                            for (int l = 0; l < 4; ++l)
+                                if (j0 + 32 * l < g.N) prefetch_l2(row + (j0 + 32 * l) * 4);
+                        }
+                    }
+                }
                 const bool ready = conv_ok && wait(TFULL(buf), use, sh, g, 4u);
                 if (!__all_sync(0xFFFFFFFFu, ready)) { ok = false; break; }
                 tc_fence_after();
